@@ -1,0 +1,457 @@
+#!/usr/bin/env python
+"""Benchmark of the selective-scan hot path on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1, NCCL)
+
+Metric: selective-scan forward+backward throughput in TB/s of algorithmic
+HBM bytes, on config 2 -- the Mamba-130M layer (batch 8, d_inner 1536, seqlen 2048,
+d_state 16, bf16 streams, z gate, softplus).  A step is one forward and one backward over
+one batch.  Multi-GPU runs are weak-scaled: every rank processes its own batch of 8 (the
+batch dimension is sharded across GPUs with no data-path collective); `value` counts the
+bytes of all ranks over the slowest rank's time.  Decode tokens/s (config 3) is reported as
+a secondary field.
+
+Algorithmic bytes count every input read once and every output written once
+(bf16 = 2 bytes, B/C of shape (batch, 16, seqlen)):
+    forward  = 4*E*2 + 2*B*N*L*2      (u, delta, z read; out written; B, C read)
+    backward = 7*E*2 + 4*B*N*L*2      (u, delta, z, dout read; du, ddelta, dz written;
+                                       B, C read; dB, dC written)
+State checkpoints and the saved pre-gate output are implementation traffic and are not
+counted.  The reference arm (--impl reference) times the reference's math on the host
+CPU cores (the reference has no CPU path of its own; this is the C restatement in
+oracle/, run on a bounded sample of the same workload) and, for context, the reference's
+own CUDA kernels on the GPU in float32 (their only dtype).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG2 = dict(batch=8, dim=1536, seqlen=2048, dstate=16)
+CFG3 = dict(batch=64, dim=5120, dstate=16, steps=1024, layers=8)
+
+
+def scan_bytes(batch, dim, seqlen, dstate, es=2):
+    E = batch * dim * seqlen
+    bnl = batch * dstate * seqlen
+    return 4 * E * es + 2 * bnl * es, 7 * E * es + 4 * bnl * es
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d.get("hbm_gbs", 6650.0)), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_from_profiles(name):
+    """Per-launch DRAM bytes of a kernel, from a committed ncu summary (profiles/*.txt
+    lines `traffic_bytes_per_launch <kernel> <bytes>`), or None."""
+    d = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(d):
+        return None
+    for fn in sorted(os.listdir(d)):
+        if not fn.endswith(".txt"):
+            continue
+        with open(os.path.join(d, fn)) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch" and parts[1] == name:
+                    return float(parts[2])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.proc = None
+        self.t0 = self.t1 = None
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            ident = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        except Exception:
+            ident = str(device_index)
+        self.ident = ident
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "--query-gpu=" + self.QUERY, "--format=csv,noheader,nounits", "-lms", "50",
+                 "-i", self.ident], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def mark(self, which):
+        setattr(self, which, time.time())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.strip()]
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            if len(r) < 9:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.strip() == "Active":
+                    reasons.add(n)
+        loaded = sorted(sm)[len(sm) // 4:] if sm else []
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
+                "samples": len(rows)}
+
+
+def dist_setup(want_nccl=True):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    pg = None
+    if world > 1 and torch.cuda.is_available():
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl" if want_nccl else "gloo", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local, pg
+
+
+def max_over_ranks(x, pg):
+    import torch
+    if pg is None:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(pg):
+    import torch
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------------------
+def cpu_baseline_sample(target_s=10.0, batch=1, dim=96):
+    """The oracle's float build (C + OpenMP, all host cores) on a bounded sample of the
+    config-2 workload: (batch, dim) rows of the same seqlen / d_state."""
+    import numpy as np
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    from ssm_mamba_b200.workloads import scan_inputs
+    L, N = CFG2["seqlen"], CFG2["dstate"]
+    inp = scan_inputs(batch, dim, L, N, torch.bfloat16, seed=1, device="cpu", with_z=True)
+    f = lambda t: t.float().numpy()  # noqa: E731
+    args = [f(inp.u), f(inp.delta), f(inp.A), f(inp.B), f(inp.C)]
+    kw = dict(D=f(inp.D), z=f(inp.z), delta_bias=f(inp.delta_bias), dtype=np.float32)
+    reps, t_total = 0, 0.0
+    while t_total < target_s and reps < 50:
+        t0 = time.perf_counter()
+        fw = oracle.scan_fwd(*args, **kw)
+        oracle.scan_bwd(*args, f(inp.dout), fwd=fw, **kw)
+        t_total += time.perf_counter() - t0
+        reps += 1
+    fb, bb = scan_bytes(batch, dim, L, N)
+    return {"value": (fb + bb) * reps / t_total / 1e12, "unit": "TB/s", "cores": oracle.num_threads(),
+            "kind": "port",
+            "sample": f"oracle float32 fwd+bwd of {batch}x{dim} channel rows of config 2 (seqlen {L}, "
+                      f"d_state {N}; 1/{CFG2['batch'] * CFG2['dim'] // (batch * dim)} of the batch), "
+                      f"{reps} reps in {t_total:.1f} s", "seconds_per_step_full": t_total / reps *
+            (CFG2["batch"] * CFG2["dim"]) / (batch * dim)}
+
+
+def run_ours(args, world, rank, local, pg):
+    import torch
+    from ssm_mamba_b200._ext import _C
+    from ssm_mamba_b200 import selective_scan_fn, selective_state_update
+    from ssm_mamba_b200.workloads import scan_inputs
+    dev = torch.device("cuda", local)
+    B, D, L, N = CFG2["batch"], CFG2["dim"], CFG2["seqlen"], CFG2["dstate"]
+    inp = scan_inputs(B, D, L, N, torch.bfloat16, seed=1 + rank, device=dev, with_z=True)
+    fwd_bytes, bwd_bytes = scan_bytes(B, D, L, N)
+
+    def step():
+        out, y, ck, _ = _C.scan_fwd(inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, inp.z, inp.delta_bias, None,
+                                    None, True, True, True, 1, False)
+        ev_mid = torch.cuda.Event(enable_timing=True)
+        ev_mid.record()
+        g = _C.scan_bwd(inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, inp.z, inp.delta_bias, None, None, True,
+                        True, y, ck, inp.dout, None)
+        return ev_mid, out, g
+
+    for _ in range(args.warmup):
+        step()
+    barrier(pg)
+    clocks = ClockSampler(local)
+    clocks.start()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    mids = []
+    barrier(pg)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for i in range(args.steps):
+        starts[i].record()
+        ev_mid, _, _ = step()
+        mids.append(ev_mid)
+        ends[i].record()
+    t_end.record()
+    torch.cuda.synchronize()
+    barrier(pg)
+    clk = clocks.stop()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    fwd_ms = statistics.mean(starts[i].elapsed_time(mids[i]) for i in range(args.steps))
+    bwd_ms = statistics.mean(mids[i].elapsed_time(ends[i]) for i in range(args.steps))
+    elapsed_ms = max_over_ranks(elapsed_ms, pg)
+    total_bytes = (fwd_bytes + bwd_bytes) * args.steps * world
+    value = total_bytes / (elapsed_ms / 1e3) / 1e12
+    peak, peak_kind = measured_peaks()
+
+    # ---- end to end through the public API: pinned host inputs in, gradients out -------
+    e2e_steps = min(args.steps, 10)
+    f = lambda t: t.detach().to("cpu").pin_memory()  # noqa: E731
+    host_in = {k: f(getattr(inp, k)) for k in ("u", "delta", "z", "B", "C", "dout")}
+    A = inp.A.clone().requires_grad_()
+    Dp = inp.D.clone().requires_grad_()
+    bias = inp.delta_bias.clone().requires_grad_()
+    host_out = {k: torch.empty(host_in[k].shape, dtype=host_in[k].dtype).pin_memory()
+                for k in ("u", "delta", "z", "B", "C")}
+
+    def e2e_step():
+        d = {k: v.to(dev, non_blocking=True) for k, v in host_in.items()}
+        leaves = {k: d[k].requires_grad_() for k in ("u", "delta", "z", "B", "C")}
+        o = selective_scan_fn(leaves["u"], leaves["delta"], A, leaves["B"].unsqueeze(1),
+                              leaves["C"].unsqueeze(1), Dp, leaves["z"], bias, delta_softplus=True)
+        o.backward(d["dout"])
+        for k in host_out:
+            host_out[k].copy_(leaves[k].grad, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier(pg)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(pg)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), pg)
+    h2d = sum(v.numel() * v.element_size() for v in host_in.values())
+    d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+    e2e = {"value": (fwd_bytes + bwd_bytes) * e2e_steps * world / (e2e_ms / 1e3) / 1e12, "unit": "TB/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / e2e_steps,
+           "api": "ssm_mamba_b200.selective_scan_fn forward + autograd backward"}
+
+    # ---- decode (config 3), state rotated over 8 layer buffers (168 MB > L2) -------------
+    decode = None
+    if not args.no_decode:
+        from ssm_mamba_b200.workloads import decode_inputs
+        Bd, Dd, Nd, S, Ly = CFG3["batch"], CFG3["dim"], CFG3["dstate"], CFG3["steps"], CFG3["layers"]
+        dec = decode_inputs(Bd, Dd, Nd, S, torch.bfloat16, seed=2 + rank, device=dev)
+        states = [dec.state.clone() for _ in range(Ly)]
+
+        def loop():
+            for s in range(S):
+                selective_state_update(states[s % Ly], dec.x[s], dec.dt[s], dec.A, dec.B[s], dec.C[s], dec.D,
+                                       dec.z[s], dec.dt_bias, dt_softplus=True)
+
+        loop()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            loop()
+        for _ in range(2):
+            graph.replay()
+        barrier(pg)
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 3
+        d0.record()
+        for _ in range(reps):
+            graph.replay()
+        d1.record()
+        torch.cuda.synchronize()
+        barrier(pg)
+        dec_ms = max_over_ranks(d0.elapsed_time(d1), pg) / (reps * S)
+        step_bytes = 2 * Bd * Dd * Nd * 4 + 4 * Bd * Dd * 2 + Dd * Nd * 4 + 2 * Bd * Nd * 2 + 2 * Dd * 4
+        decode = {"metric": "decode tokens/s (one Mamba-2.8B-width layer)", "value": Bd * world / (dec_ms / 1e3),
+                  "unit": "tokens/s", "us_per_step": dec_ms * 1e3, "gpu_launches_per_step": 1,
+                  "roofline": {"bound": "hbm", "achieved": step_bytes / (dec_ms / 1e3) / 1e9, "peak": peak,
+                               "unit": "GB/s", "frac": step_bytes / (dec_ms / 1e3) / 1e9 / peak,
+                               "bytes_per_step": step_bytes},
+                  "config": "batch 64, d_inner 5120, d_state 16 fp32 state, bf16 x/dt/z/B/C, 1024 steps in "
+                            "one CUDA graph, state rotated over 8 layer buffers"}
+        del graph
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline_sample(target_s=args.cpu_seconds)
+
+    bwd_gbs = bwd_bytes / (bwd_ms / 1e3) / 1e9
+    fwd_gbs = fwd_bytes / (fwd_ms / 1e3) / 1e9
+    line = {
+        "metric": "scan fwd+bwd achieved HBM TB/s (% of peak) at 1/2/4/8 B200; decode tokens/s",
+        "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded normal draws, S4D-real A, dt-bias init)",
+        "config": {"workload": "config 2: Mamba-130M-shape layer selective_scan fwd+bwd, batch 8 per GPU, "
+                               "d_inner 1536, seqlen 2048, d_state 16, bf16 u/delta/z/B/C, z gate, softplus",
+                   "global_batch": B * world, "seq_len": L, "parallelism": f"batch-sharded x{world}, no collective",
+                   "l2": "inputs larger than L2 (~330 MB read per step)",
+                   "frac_of_hbm_peak": value / world * 1e3 / peak},
+        "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+        "roofline": {"bound": "hbm", "kernel": "ssm_scan_bwd (scan_bwd_kernel + scan_reduce_kernel)",
+                     "achieved": bwd_gbs, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": bwd_gbs / peak, "traffic": traffic_from_profiles("scan_bwd_kernel"),
+                     "algorithmic_bytes_per_launch": bwd_bytes},
+        "roofline_fwd": {"bound": "hbm", "kernel": "scan_fwd_kernel", "achieved": fwd_gbs, "peak": peak,
+                         "unit": "GB/s", "frac": fwd_gbs / peak, "traffic": traffic_from_profiles("scan_fwd_kernel"),
+                         "algorithmic_bytes_per_launch": fwd_bytes},
+        "e2e": e2e, "gpu_launches": 3 * args.steps, "clocks": clk, "decode": decode, "cpu_baseline": cpu,
+    }
+    return line
+
+
+def run_reference(args, world, rank, local, pg):
+    """Reference arm: the reference's math on the host CPU cores (oracle port, bounded
+    sample per step), plus the reference's own CUDA kernels on the GPU for context."""
+    import torch
+    if rank != 0:
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle
+    from ssm_mamba_b200.workloads import scan_inputs
+    L, N = CFG2["seqlen"], CFG2["dstate"]
+    sb, sd = 1, 48
+    inp = scan_inputs(sb, sd, L, N, torch.bfloat16, seed=1, device="cpu", with_z=True)
+    f = lambda t: t.float().numpy()  # noqa: E731
+    a = [f(inp.u), f(inp.delta), f(inp.A), f(inp.B), f(inp.C)]
+    kw = dict(D=f(inp.D), z=f(inp.z), delta_bias=f(inp.delta_bias), dtype=np.float32)
+
+    def step():
+        fw = oracle.scan_fwd(*a, **kw)
+        oracle.scan_bwd(*a, f(inp.dout), fwd=fw, **kw)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    fb, bb = scan_bytes(sb, sd, L, N)
+    value = (fb + bb) * args.steps / dt / 1e12
+    line = {
+        "impl": "reference", "metric": "scan fwd+bwd achieved HBM TB/s (% of peak) at 1/2/4/8 B200; decode tokens/s",
+        "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config 2 (Mamba-130M layer scan fwd+bwd), bounded sample of "
+                               f"{sb}x{sd} channel rows per step, seqlen {L}, d_state {N}",
+                   "global_batch": 8, "seq_len": L, "parallelism": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": oracle.num_threads(), "kind": "port",
+                         "sample": f"{sb}x{sd} of 8x1536 channel rows per step (reference has no CPU path; "
+                                   "C restatement of its kernels, float32, OpenMP)"},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    # the reference's own CUDA kernels (float32 only), same config-2 shape, for context
+    try:
+        import build_ref
+        if torch.cuda.is_available() and build_ref.available() and not args.no_ref_cuda:
+            ref = build_ref.load("ref_selective_scan")
+            dev = torch.device("cuda", local)
+            g = scan_inputs(CFG2["batch"], CFG2["dim"], L, N, torch.float32, seed=1, device=dev, with_z=False)
+            dh = torch.zeros(CFG2["batch"], CFG2["dim"], N, device=dev)
+
+            def rstep():
+                out, h = ref.forward(g.u, g.A, g.B, g.C, g.D, g.delta, g.delta_bias, None, None, "right")
+                ref.backward(g.u, g.A, g.B, g.C, g.D, g.delta, g.delta_bias, h, None, g.dout, dh, None, "right")
+
+            for _ in range(2):
+                rstep()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n = 3
+            e0.record()
+            for _ in range(n):
+                rstep()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / n
+            fb2, bb2 = scan_bytes(CFG2["batch"], CFG2["dim"], L, N, es=2)
+            line["ref_cuda_b200"] = {
+                "what": "reference CUDA kernels (oracle/_ref, built from its sources), float32, full config-2 "
+                        "shape, no z gate (the reference has none)", "ms_per_step": ms,
+                "value_bf16_byte_accounting": (fb2 + bb2) / (ms / 1e3) / 1e12, "unit": "TB/s"}
+    except Exception as e:  # context only; never fail the reference arm on it
+        line["ref_cuda_b200"] = {"error": str(e)[:200]}
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-ref-cuda", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        # rank 0 alone runs the reference arm; the other ranks exit without work
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        if rank != 0:
+            return
+        line = run_reference(args, world, rank, local, None)
+        print(json.dumps(line), flush=True)
+        return
+    world, rank, local, pg = dist_setup()
+    line = run_ours(args, world, rank, local, pg)
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

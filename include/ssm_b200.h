@@ -1,0 +1,189 @@
+/*
+ * ssm_b200 -- C ABI of the B200 (sm_100a) selective-scan library.
+ *
+ * Plain C: pointers, sizes and int64 strides, no torch or CUDA types.  Every pointer
+ * argument named as a tensor is a DEVICE pointer on the current CUDA device; `stream`
+ * is a cudaStream_t passed as void* (NULL = legacy default stream).  All entry points
+ * are asynchronous with respect to the host unless stated, and return SSM_OK (0) or an
+ * error code; ssm_last_error() gives the message of the last failure on this thread.
+ *
+ * The entry points replace the native half of the reference (nmquan1503/ssm-mamba):
+ *   ssm_scan_fwd      <- selective_scan.forward   (csrc/selective_scan/selective_scan.cpp:212-292,
+ *                                                  forward_kernel.cu:246-264)
+ *   ssm_scan_bwd      <- selective_scan.backward  (csrc/selective_scan/selective_scan.cpp:294-380,
+ *                                                  backward_kernel.cu:456-478)
+ *   ssm_state_update  <- selective_update.apply   (csrc/selective_update/selective_update.cpp:78-130,
+ *                                                  kernel.cu:74-91)
+ * The reference binds those through pybind (csrc/selective_scan/bindings.cpp:5-8,
+ * csrc/selective_update/bindings.cpp:5-7); here they are plain C so that any FFI
+ * (ctypes, cffi, a torch extension) can bind them.
+ *
+ * Shapes (element strides; the innermost dimension always has stride 1):
+ *   u, delta, z, out, y, dout, du, ddelta, dz : (batch, dim, seqlen)
+ *   A, dA                                     : (dim, dstate)        float32
+ *   B, C, dB, dC                              : (batch, dstate, seqlen)
+ *   D, delta_bias, dD, ddelta_bias            : (dim)                float32
+ *   h_init, h_last, dh_last, dh_init          : (batch, dim, dstate) float32, contiguous
+ *   length                                    : (batch)              int64
+ */
+#ifndef SSM_B200_H
+#define SSM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SSM_API __attribute__((visibility("default")))
+#else
+#define SSM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types of the streaming tensors (u, delta, z, B, C, out, y and their grads) */
+#define SSM_F32 0
+#define SSM_BF16 1
+
+/* status codes */
+#define SSM_OK 0
+#define SSM_ERR_INVALID 1     /* bad shape, stride, alignment, dtype or missing pointer */
+#define SSM_ERR_CUDA 2        /* CUDA runtime error (launch, attribute, driver entry point) */
+#define SSM_ERR_WORKSPACE 3   /* workspace too small */
+#define SSM_ERR_DEVICE 4      /* a kernel reported a bounded wait that ran out */
+
+/* checkpoint layouts written by ssm_scan_fwd and read by ssm_scan_bwd */
+#define SSM_CKPT_COMPACT 0    /* (batch, nchunks, dim, dstate) states only */
+#define SSM_CKPT_REFERENCE 1  /* (batch, dim, nchunks, 2*dstate) interleaved (prod, state):
+                                 the reference's `h` (selective_scan.cpp:271-274) */
+
+typedef struct ssm_scan_fwd_args {
+    int64_t batch, dim, seqlen, dstate;
+    int32_t dtype;                 /* SSM_F32 or SSM_BF16, for u, delta, z, B, C, out, y */
+    int32_t delta_softplus;        /* 1: delta = softplus(delta + bias), threshold 20 */
+    int32_t padding_right;         /* length handling: 1 right padding, 0 left padding */
+    int32_t _pad0;
+    const void* u;      int64_t u_batch_stride, u_dim_stride;
+    const void* delta;  int64_t delta_batch_stride, delta_dim_stride;
+    const float* A;     int64_t A_dim_stride;
+    const void* B;      int64_t B_batch_stride, B_state_stride;
+    const void* C;      int64_t C_batch_stride, C_state_stride;
+    const float* D;                /* may be NULL (no skip term) */
+    const void* z;      int64_t z_batch_stride, z_dim_stride;     /* may be NULL (no gate) */
+    const float* delta_bias;       /* may be NULL */
+    const float* h_init;           /* may be NULL (zero initial state) */
+    const int64_t* length;         /* may be NULL (every row has seqlen tokens) */
+    void* out;          int64_t out_batch_stride, out_dim_stride;
+    void* y;            int64_t y_batch_stride, y_dim_stride;     /* may be NULL: pre-gate output */
+    float* ckpt;                   /* may be NULL: state checkpoints for the backward */
+    int32_t ckpt_format;           /* SSM_CKPT_COMPACT or SSM_CKPT_REFERENCE */
+    int32_t _pad1;
+    int64_t ckpt_len;              /* tokens per checkpoint, a multiple of 4 */
+    float* h_last;                 /* may be NULL: final state (batch, dim, dstate) */
+} ssm_scan_fwd_args;
+
+typedef struct ssm_scan_bwd_args {
+    int64_t batch, dim, seqlen, dstate;
+    int32_t dtype;
+    int32_t delta_softplus;
+    int32_t padding_right;
+    int32_t reference_length_semantics; /* must be 1 when length != NULL: the backward then
+                                           reproduces the reference's handling of `length`
+                                           (backward_kernel.cu:225-400) */
+    const void* u;      int64_t u_batch_stride, u_dim_stride;
+    const void* delta;  int64_t delta_batch_stride, delta_dim_stride;
+    const float* A;     int64_t A_dim_stride;
+    const void* B;      int64_t B_batch_stride, B_state_stride;
+    const void* C;      int64_t C_batch_stride, C_state_stride;
+    const float* D;
+    const void* z;      int64_t z_batch_stride, z_dim_stride;
+    const float* delta_bias;
+    const float* h_init;
+    const int64_t* length;
+    const void* y;      int64_t y_batch_stride, y_dim_stride;     /* pre-gate output; needed iff z */
+    const float* ckpt;
+    int32_t ckpt_format;
+    int32_t _pad1;
+    int64_t ckpt_len;
+    const void* dout;   int64_t dout_batch_stride, dout_dim_stride;
+    const float* dh_last;          /* may be NULL (zero) */
+    void* du;           int64_t du_batch_stride, du_dim_stride;
+    void* ddelta;       int64_t ddelta_batch_stride, ddelta_dim_stride;
+    void* dz;           int64_t dz_batch_stride, dz_dim_stride;   /* needed iff z */
+    float* dA;                     /* (dim, dstate) contiguous */
+    void* dB;                      /* (batch, dstate, seqlen) contiguous, dtype */
+    void* dC;                      /* (batch, dstate, seqlen) contiguous, dtype */
+    float* dD;                     /* may be NULL */
+    float* ddelta_bias;            /* may be NULL */
+    float* dh_init;                /* may be NULL; written iff h_init != NULL */
+} ssm_scan_bwd_args;
+
+typedef struct ssm_state_update_args {
+    int64_t batch, dim, dstate;
+    int32_t dtype;                 /* for x, dt, z, B, C, out */
+    int32_t dt_softplus;
+    const float* state;  int64_t state_batch_stride, state_dim_stride;  /* read */
+    float* state_out;    int64_t state_out_batch_stride, state_out_dim_stride; /* written;
+                                      may equal `state` (in place) */
+    const void* x;       int64_t x_batch_stride;
+    const void* dt;      int64_t dt_batch_stride;
+    const float* A;      int64_t A_dim_stride;
+    const void* B;       int64_t B_batch_stride;
+    const void* C;       int64_t C_batch_stride;
+    const float* D;                /* may be NULL */
+    const void* z;       int64_t z_batch_stride;   /* may be NULL */
+    const float* dt_bias;          /* may be NULL */
+    void* out;           int64_t out_batch_stride;
+} ssm_state_update_args;
+
+/* Message of the last failed call on the calling thread ("" if none). */
+SSM_API const char* ssm_last_error(void);
+
+/* Library version string. */
+SSM_API const char* ssm_version(void);
+
+/* Number of state checkpoints a forward with these sizes writes: ceil(seqlen / ckpt_len). */
+SSM_API int64_t ssm_scan_num_ckpt(int64_t seqlen, int64_t ckpt_len);
+
+/* Checkpoint interval (tokens) ssm_scan_bwd needs: the forward feeding a backward must
+ * write SSM_CKPT_COMPACT checkpoints every ssm_scan_ckpt_len(dstate) tokens (8 for
+ * dstate <= 128, 4 above). */
+SSM_API int64_t ssm_scan_ckpt_len(int64_t dstate);
+
+/* Forward selective scan (replaces selective_scan.forward).  Writes out, optionally y
+ * (pre-gate output, needed by the backward when z is given), the state checkpoints and
+ * the final state. */
+SSM_API int ssm_scan_fwd(const ssm_scan_fwd_args* args, void* stream);
+
+/* Rebuilds the compact checkpoints ssm_scan_bwd needs from the reference's chunk states
+ * `ref_ckpt` (SSM_CKPT_REFERENCE layout, 128-token chunks, as selective_scan.forward
+ * returns them in `h`), recomputing every chunk from its start state with the reference
+ * backward's load rules (backward_kernel.cu:242-246, 345-353).  args->ckpt must be a
+ * SSM_CKPT_COMPACT buffer with ckpt_len = ssm_scan_ckpt_len(dstate); args->out and args->y
+ * must be NULL.  No reference counterpart: the reference backward recomputes inside
+ * its own kernel. */
+SSM_API int ssm_scan_ckpt_from_reference(const ssm_scan_fwd_args* args, const float* ref_ckpt,
+                                 void* stream);
+
+/* Bytes of device workspace ssm_scan_bwd needs for these arguments. */
+SSM_API size_t ssm_scan_bwd_workspace_size(const ssm_scan_bwd_args* args);
+
+/* Backward selective scan (replaces selective_scan.backward).  Overwrites every gradient
+ * output (no pre-zeroing needed).  Deterministic: no floating-point atomics.  The
+ * workspace must hold ssm_scan_bwd_workspace_size(args) bytes and be 256-byte aligned. */
+SSM_API int ssm_scan_bwd(const ssm_scan_bwd_args* args, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/* One decode step (replaces selective_update.apply).  state_out may alias state. */
+SSM_API int ssm_state_update(const ssm_state_update_args* args, void* stream);
+
+/* Reads and clears the device-side error word of the current device (synchronizes
+ * `stream`).  Returns SSM_OK, or SSM_ERR_DEVICE with *code set to the kernel's code. */
+SSM_API int ssm_check_device_error(int* code, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SSM_B200_H */

@@ -1,0 +1,498 @@
+// C ABI of the library (include/ssm_b200.h): argument validation, TMA tensor maps, CTA
+// sizing and launches.  Mirrors the checks of the reference host glue
+// (nmquan1503/ssm-mamba, csrc/selective_scan/selective_scan.cpp:15-32, 229-268, 314-351;
+// csrc/selective_update/selective_update.cpp:11-21, 184-206): shapes, the 256-state limit
+// and dtypes -- here reported as status codes plus ssm_last_error() instead of exceptions.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/ssm_b200.h"
+#include "params.h"
+#include "scan_layout.h"
+
+namespace ssm {
+cudaError_t launch_scan_fwd(const FwdParams& p, int is_bf16, int lpc, const CUtensorMap* maps,
+                            cudaStream_t stream);
+cudaError_t launch_scan_bwd(const BwdParams& p, int is_bf16, int lpc, const CUtensorMap* maps,
+                            cudaStream_t stream);
+cudaError_t launch_scan_reduce(const ReduceParams& p, cudaStream_t stream);
+cudaError_t launch_state_update(const UpdParams& p, int is_bf16, int lpc, cudaStream_t stream);
+size_t bwd_smem_bytes(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
+int fwd_occupancy(int is_bf16, int lpc, int dt, int has_z, int has_y);
+int bwd_occupancy(int is_bf16, int lpc, int dt, int dstate, int has_z);
+}  // namespace ssm
+
+using namespace ssm;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(SSM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// ---- lanes per channel / states per thread / backward sub-tile for a state count ----------
+struct StateSplit { int lpc, spt, k; };
+
+StateSplit split_states(int64_t n) {
+    if (n > 128) return {32, 8, 4};
+    int ns = 4;
+    while (ns < n) ns *= 2;
+    return {ns / 4, 4, 8};
+}
+
+// ---- device attributes and the per-device error word ----------------------------------------
+struct DevInfo {
+    int sms = 0;
+    int* err = nullptr;
+};
+std::mutex g_mu;
+DevInfo g_dev[64];
+
+int device_info(DevInfo** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(SSM_ERR_CUDA, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevInfo& di = g_dev[dev];
+    if (di.sms == 0) {
+        e = cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+        e = cudaMalloc(&di.err, sizeof(int));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(error word)");
+        e = cudaMemset(di.err, 0, sizeof(int));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(error word)");
+    }
+    *out = &di;
+    return SSM_OK;
+}
+
+// ---- TMA tensor maps ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int get_encoder() {
+    if (g_encode) return SSM_OK;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_encode) return SSM_OK;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return fail(SSM_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    return SSM_OK;
+}
+
+// Can a (dim2, dim1, inner) tensor with these element strides be a TMA source/target?
+bool tma_ok(const void* ptr, int64_t s1, int64_t s2, int64_t es) {
+    if (!ptr) return true;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0) return false;
+    if (((s1 * es) & 15) != 0 || ((s2 * es) & 15) != 0) return false;
+    if (s1 * es >= (int64_t(1) << 40) || s2 * es >= (int64_t(1) << 40)) return false;
+    return true;
+}
+
+// 3-D map of a (d2, d1, d0=inner) tensor with element strides (s2, s1, 1); box (b0, b1, 1).
+int encode3d(CUtensorMap* map, const void* ptr, int is_bf16, int64_t d0, int64_t d1, int64_t d2,
+             int64_t s1, int64_t s2, int b0, int b1, CUtensorMapSwizzle swz) {
+    if (!ptr) {
+        memset(map, 0, sizeof(*map));
+        return SSM_OK;
+    }
+    const int64_t es = is_bf16 ? 2 : 4;
+    // a size-1 outer dimension may have any stride; give TMA a valid one
+    if (d1 == 1) s1 = d0;
+    if (d2 == 1) s2 = s1 * d1;
+    cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+    cuuint64_t strides[2] = {(cuuint64_t)(s1 * es), (cuuint64_t)(s2 * es)};
+    cuuint32_t box[3] = {(cuuint32_t)b0, (cuuint32_t)b1, 1u};
+    cuuint32_t estr[3] = {1u, 1u, 1u};
+    CUresult r = g_encode(map, is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                          const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SSM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return SSM_OK;
+}
+
+// ---- CTA sizing: channels per CTA ---------------------------------------------------------------
+// Picks dt (a multiple of the channels a warp holds, at most 128 threads per CTA) that
+// minimises the estimated time on the busiest SM: CTAs are spread evenly over the SMs and
+// run `res` at a time (res from the occupancy calculator), and an SM is assumed to reach
+// full throughput at 8 resident warps.  Results are cached per shape.
+template <typename OccFn>
+int choose_dt(int64_t batch, int64_t dim, int lpc, int sms, OccFn occupancy) {
+    const int cpw = 32 / lpc;
+    const int dtmax = 128 / lpc;
+    int best = -1;
+    double best_t = 1e300;
+    for (int dt = cpw; dt <= dtmax; dt += cpw) {
+        const int res = occupancy(dt);
+        if (res < 1) continue;
+        const int warps = dt * lpc / 32;
+        const int64_t ctas = batch * ((dim + dt - 1) / dt);
+        const int64_t per_sm = (ctas + sms - 1) / sms;
+        double t = 0;
+        for (int64_t left = per_sm; left > 0; left -= res) {
+            const int64_t m = left < res ? left : res;
+            const double thr = (m * warps) >= 8 ? 1.0 : (double)(m * warps) / 8.0;
+            t += (double)m * dt / thr;
+        }
+        t *= (double)(((dim + dt - 1) / dt) * dt) / (double)dim;  // ragged last channel tile
+        if (t < best_t * 0.999) {
+            best_t = t;
+            best = dt;
+        }
+    }
+    return best;
+}
+
+struct DtKey {
+    int dev, kind, is_bf16, lpc, dstate, has_z, has_y;
+    int64_t batch, dim;
+    bool operator==(const DtKey& o) const { return memcmp(this, &o, sizeof(*this)) == 0; }
+};
+std::mutex g_dt_mu;
+DtKey g_dt_keys[64];
+int g_dt_vals[64];
+int g_dt_n = 0;
+
+template <typename OccFn>
+int cached_dt(DtKey key, int sms, OccFn occ) {
+    {
+        std::lock_guard<std::mutex> lk(g_dt_mu);
+        for (int i = 0; i < g_dt_n; i++)
+            if (g_dt_keys[i] == key) return g_dt_vals[i];
+    }
+    const int dt = choose_dt(key.batch, key.dim, key.lpc, sms, occ);
+    std::lock_guard<std::mutex> lk(g_dt_mu);
+    const int slot = g_dt_n < 64 ? g_dt_n++ : (int)(key.dim % 64);
+    g_dt_keys[slot] = key;
+    g_dt_vals[slot] = dt;
+    return dt;
+}
+
+bool valid_dtype(int32_t t) { return t == SSM_F32 || t == SSM_BF16; }
+
+}  // namespace
+
+extern "C" {
+
+const char* ssm_last_error(void) { return g_err.c_str(); }
+
+const char* ssm_version(void) { return "ssm_b200 0.1.0 (sm_100a)"; }
+
+int64_t ssm_scan_num_ckpt(int64_t seqlen, int64_t ckpt_len) {
+    if (seqlen <= 0 || ckpt_len <= 0) return 0;
+    return (seqlen + ckpt_len - 1) / ckpt_len;
+}
+
+// Checkpoint interval (tokens) the backward needs from the forward's compact checkpoints.
+int64_t ssm_scan_ckpt_len(int64_t dstate) { return split_states(dstate).k; }
+
+static int fwd_impl(const ssm_scan_fwd_args* a, const float* restart, void* stream_) {
+    if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_fwd: args is NULL");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    if (a->batch < 1 || a->dim < 1 || a->seqlen < 1 || a->dstate < 1)
+        return fail(SSM_ERR_INVALID, "ssm_scan_fwd: sizes must be positive (batch=%lld dim=%lld seqlen=%lld dstate=%lld)",
+                    (long long)a->batch, (long long)a->dim, (long long)a->seqlen, (long long)a->dstate);
+    if (a->dstate > 256) return fail(SSM_ERR_INVALID, "selective_scan only supports state_dim <= 256");
+    if (a->seqlen > (1 << 30) || a->dim > (1 << 30) || a->batch > (1 << 30))
+        return fail(SSM_ERR_INVALID, "ssm_scan_fwd: sizes too large");
+    if (!valid_dtype(a->dtype)) return fail(SSM_ERR_INVALID, "ssm_scan_fwd: dtype must be SSM_F32 or SSM_BF16");
+    if (!a->u || !a->delta || !a->A || !a->B || !a->C || (!a->out && !restart))
+        return fail(SSM_ERR_INVALID, "ssm_scan_fwd: u, delta, A, B, C and out are required");
+    if (restart && (!a->ckpt || a->ckpt_format != SSM_CKPT_COMPACT || a->out || a->y))
+        return fail(SSM_ERR_INVALID, "ssm_scan_ckpt_from_reference: needs a compact ckpt and no out / y");
+    if (a->ckpt) {
+        if (a->ckpt_format != SSM_CKPT_COMPACT && a->ckpt_format != SSM_CKPT_REFERENCE)
+            return fail(SSM_ERR_INVALID, "ssm_scan_fwd: unknown checkpoint format");
+        if (a->ckpt_len < 4 || (a->ckpt_len % 4) != 0)
+            return fail(SSM_ERR_INVALID, "ssm_scan_fwd: ckpt_len must be a positive multiple of 4");
+    }
+    const int is_bf16 = a->dtype == SSM_BF16;
+    const int64_t es = is_bf16 ? 2 : 4;
+    DevInfo* di = nullptr;
+    int rc = device_info(&di);
+    if (rc) return rc;
+    const StateSplit sp = split_states(a->dstate);
+    const int T = (int)(128 / es);
+
+    FwdParams p;
+    memset(&p, 0, sizeof(p));
+    p.batch = (int)a->batch; p.dim = (int)a->dim; p.seqlen = (int)a->seqlen; p.dstate = (int)a->dstate;
+    p.delta_softplus = a->delta_softplus; p.padding_right = a->padding_right;
+    p.ckpt_format = a->ckpt_format; p.ckpt_len = (int)a->ckpt_len;
+    p.nck = a->ckpt ? (int)ssm_scan_num_ckpt(a->seqlen, a->ckpt_len) : 0;
+    p.u = a->u; p.u_sb = a->u_batch_stride; p.u_sd = a->u_dim_stride;
+    p.delta = a->delta; p.delta_sb = a->delta_batch_stride; p.delta_sd = a->delta_dim_stride;
+    p.A = a->A; p.A_sd = a->A_dim_stride;
+    p.B = a->B; p.B_sb = a->B_batch_stride; p.B_sn = a->B_state_stride;
+    p.C = a->C; p.C_sb = a->C_batch_stride; p.C_sn = a->C_state_stride;
+    p.D = a->D; p.z = a->z; p.z_sb = a->z_batch_stride; p.z_sd = a->z_dim_stride;
+    p.delta_bias = a->delta_bias; p.h_init = a->h_init; p.length = a->length;
+    p.out = a->out; p.out_sb = a->out_batch_stride; p.out_sd = a->out_dim_stride;
+    p.y = a->y; p.y_sb = a->y_batch_stride; p.y_sd = a->y_dim_stride;
+    p.ckpt = a->ckpt; p.h_last = a->h_last; p.err = di->err;
+    p.restart = restart;
+    p.restart_len = 128;
+    p.restart_nck = (int)ssm_scan_num_ckpt(a->seqlen, 128);
+
+    const int has_z = a->z != nullptr, has_y = a->y != nullptr;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    DtKey key;
+    memset(&key, 0, sizeof(key));
+    key.dev = dev; key.kind = 0; key.is_bf16 = is_bf16; key.lpc = sp.lpc; key.dstate = 0;
+    key.has_z = has_z; key.has_y = has_y; key.batch = a->batch; key.dim = a->dim;
+    p.dt = cached_dt(key, di->sms, [&](int dt) { return fwd_occupancy(is_bf16, sp.lpc, dt, has_z, has_y); });
+    if (p.dt < 1) return fail(SSM_ERR_INVALID, "ssm_scan_fwd: no CTA shape fits shared memory");
+    p.ntile_d = (int)((a->dim + p.dt - 1) / p.dt);
+
+    p.use_tma = tma_ok(a->u, a->u_dim_stride, a->u_batch_stride, es) &&
+                tma_ok(a->delta, a->delta_dim_stride, a->delta_batch_stride, es) &&
+                tma_ok(a->z, a->z_dim_stride, a->z_batch_stride, es) &&
+                tma_ok(a->B, a->B_state_stride, a->B_batch_stride, es) &&
+                tma_ok(a->C, a->C_state_stride, a->C_batch_stride, es) &&
+                tma_ok(a->out, a->out_dim_stride, a->out_batch_stride, es) &&
+                tma_ok(a->y, a->y_dim_stride, a->y_batch_stride, es);
+    CUtensorMap maps[7];
+    memset(maps, 0, sizeof(maps));
+    if (p.use_tma) {
+        if ((rc = get_encoder())) return rc;
+        const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+        if ((rc = encode3d(&maps[0], a->u, is_bf16, a->seqlen, a->dim, a->batch, a->u_dim_stride, a->u_batch_stride, T, p.dt, sw)) ||
+            (rc = encode3d(&maps[1], a->delta, is_bf16, a->seqlen, a->dim, a->batch, a->delta_dim_stride, a->delta_batch_stride, T, p.dt, sw)) ||
+            (rc = encode3d(&maps[2], a->z, is_bf16, a->seqlen, a->dim, a->batch, a->z_dim_stride, a->z_batch_stride, T, p.dt, sw)) ||
+            (rc = encode3d(&maps[3], a->B, is_bf16, a->seqlen, a->dstate, a->batch, a->B_state_stride, a->B_batch_stride, T, (int)a->dstate, sw)) ||
+            (rc = encode3d(&maps[4], a->C, is_bf16, a->seqlen, a->dstate, a->batch, a->C_state_stride, a->C_batch_stride, T, (int)a->dstate, sw)) ||
+            (rc = encode3d(&maps[5], a->out, is_bf16, a->seqlen, a->dim, a->batch, a->out_dim_stride, a->out_batch_stride, T, p.dt, sw)) ||
+            (rc = encode3d(&maps[6], a->y, is_bf16, a->seqlen, a->dim, a->batch, a->y_dim_stride, a->y_batch_stride, T, p.dt, sw)))
+            return rc;
+    }
+    cudaError_t e = launch_scan_fwd(p, is_bf16, sp.lpc, maps, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "scan_fwd launch");
+    return SSM_OK;
+}
+
+int ssm_scan_fwd(const ssm_scan_fwd_args* a, void* stream) { return fwd_impl(a, nullptr, stream); }
+
+int ssm_scan_ckpt_from_reference(const ssm_scan_fwd_args* a, const float* ref_ckpt, void* stream) {
+    if (!ref_ckpt) return fail(SSM_ERR_INVALID, "ssm_scan_ckpt_from_reference: ref_ckpt is NULL");
+    return fwd_impl(a, ref_ckpt, stream);
+}
+
+static int bwd_common(const ssm_scan_bwd_args* a, DevInfo** di, StateSplit* sp, int* dt) {
+    if (a->batch < 1 || a->dim < 1 || a->seqlen < 1 || a->dstate < 1)
+        return fail(SSM_ERR_INVALID, "ssm_scan_bwd: sizes must be positive");
+    if (a->dstate > 256) return fail(SSM_ERR_INVALID, "selective_scan only supports state_dim <= 256");
+    if (a->seqlen > (1 << 30) || a->dim > (1 << 30) || a->batch > (1 << 30))
+        return fail(SSM_ERR_INVALID, "ssm_scan_bwd: sizes too large");
+    if (!valid_dtype(a->dtype)) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: dtype must be SSM_F32 or SSM_BF16");
+    int rc = device_info(di);
+    if (rc) return rc;
+    *sp = split_states(a->dstate);
+    const int is_bf16 = a->dtype == SSM_BF16;
+    const int has_z = a->z != nullptr;
+    const StateSplit s = *sp;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    DtKey key;
+    memset(&key, 0, sizeof(key));
+    key.dev = dev; key.kind = 1; key.is_bf16 = is_bf16; key.lpc = s.lpc; key.dstate = (int)a->dstate;
+    key.has_z = has_z; key.has_y = 0; key.batch = a->batch; key.dim = a->dim;
+    *dt = cached_dt(key, (*di)->sms, [&](int d) { return bwd_occupancy(is_bf16, s.lpc, d, (int)a->dstate, has_z); });
+    if (*dt < 1) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: no CTA shape fits shared memory");
+    return SSM_OK;
+}
+
+struct WsLayout { size_t bc, a, dd, total; };
+
+static WsLayout ws_layout(const ssm_scan_bwd_args* a, int dt) {
+    WsLayout w;
+    const int64_t ntile = (a->dim + dt - 1) / dt;
+    auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+    w.bc = 0;
+    size_t o = al((size_t)ntile * a->batch * 2 * a->dstate * a->seqlen * sizeof(float));
+    w.a = o;
+    o += al((size_t)a->batch * a->dim * a->dstate * sizeof(float));
+    w.dd = o;
+    o += al((size_t)a->batch * a->dim * 2 * sizeof(float));
+    w.total = o;
+    return w;
+}
+
+size_t ssm_scan_bwd_workspace_size(const ssm_scan_bwd_args* a) {
+    if (!a) return 0;
+    DevInfo* di;
+    StateSplit sp;
+    int dt;
+    if (bwd_common(a, &di, &sp, &dt)) return 0;
+    return ws_layout(a, dt).total;
+}
+
+int ssm_scan_bwd(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, void* stream_) {
+    if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: args is NULL");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    DevInfo* di;
+    StateSplit sp;
+    int dt;
+    int rc = bwd_common(a, &di, &sp, &dt);
+    if (rc) return rc;
+    if (!a->u || !a->delta || !a->A || !a->B || !a->C || !a->dout || !a->ckpt || !a->du ||
+        !a->ddelta || !a->dA || !a->dB || !a->dC)
+        return fail(SSM_ERR_INVALID, "ssm_scan_bwd: u, delta, A, B, C, dout, ckpt, du, ddelta, dA, dB, dC are required");
+    if (a->z && (!a->y || !a->dz))
+        return fail(SSM_ERR_INVALID, "ssm_scan_bwd: with z, the pre-gate output y and dz are required");
+    if (a->ckpt_format != SSM_CKPT_COMPACT || a->ckpt_len != sp.k)
+        return fail(SSM_ERR_INVALID, "ssm_scan_bwd: needs compact checkpoints every %d tokens (got format %d, len %lld)",
+                    sp.k, (int)a->ckpt_format, (long long)a->ckpt_len);
+    if (a->length && !a->reference_length_semantics)
+        return fail(SSM_ERR_INVALID, "ssm_scan_bwd: `length` is only supported with the reference's semantics");
+    const WsLayout w = ws_layout(a, dt);
+    if (!workspace || ws_bytes < w.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+        return fail(SSM_ERR_WORKSPACE, "ssm_scan_bwd: workspace needs %zu bytes, 256-byte aligned", w.total);
+    const int is_bf16 = a->dtype == SSM_BF16;
+    const int64_t es = is_bf16 ? 2 : 4;
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+
+    BwdParams p;
+    memset(&p, 0, sizeof(p));
+    p.batch = (int)a->batch; p.dim = (int)a->dim; p.seqlen = (int)a->seqlen; p.dstate = (int)a->dstate;
+    p.dt = dt; p.ntile_d = (int)((a->dim + dt - 1) / dt);
+    p.delta_softplus = a->delta_softplus; p.padding_right = a->padding_right;
+    p.ref_len = a->length != nullptr;
+    p.ckpt_format = a->ckpt_format; p.ckpt_len = (int)a->ckpt_len;
+    p.nck = (int)ssm_scan_num_ckpt(a->seqlen, a->ckpt_len);
+    p.u = a->u; p.u_sb = a->u_batch_stride; p.u_sd = a->u_dim_stride;
+    p.delta = a->delta; p.delta_sb = a->delta_batch_stride; p.delta_sd = a->delta_dim_stride;
+    p.A = a->A; p.A_sd = a->A_dim_stride;
+    p.B = a->B; p.B_sb = a->B_batch_stride; p.B_sn = a->B_state_stride;
+    p.C = a->C; p.C_sb = a->C_batch_stride; p.C_sn = a->C_state_stride;
+    p.D = a->D; p.z = a->z; p.z_sb = a->z_batch_stride; p.z_sd = a->z_dim_stride;
+    p.delta_bias = a->delta_bias; p.h_init = a->h_init; p.length = a->length;
+    p.y = a->y; p.y_sb = a->y_batch_stride; p.y_sd = a->y_dim_stride;
+    p.ckpt = a->ckpt;
+    p.dout = a->dout; p.dout_sb = a->dout_batch_stride; p.dout_sd = a->dout_dim_stride;
+    p.dh_last = a->dh_last;
+    p.du = a->du; p.du_sb = a->du_batch_stride; p.du_sd = a->du_dim_stride;
+    p.ddelta = a->ddelta; p.ddelta_sb = a->ddelta_batch_stride; p.ddelta_sd = a->ddelta_dim_stride;
+    p.dz = a->dz; p.dz_sb = a->dz_batch_stride; p.dz_sd = a->dz_dim_stride;
+    p.dh_init = a->h_init ? a->dh_init : nullptr;
+    p.ws_bc = reinterpret_cast<float*>(ws + w.bc);
+    p.ws_a = reinterpret_cast<float*>(ws + w.a);
+    p.ws_dd = reinterpret_cast<float*>(ws + w.dd);
+    p.err = di->err;
+
+    p.use_tma = tma_ok(a->u, a->u_dim_stride, a->u_batch_stride, es) &&
+                tma_ok(a->delta, a->delta_dim_stride, a->delta_batch_stride, es) &&
+                tma_ok(a->dout, a->dout_dim_stride, a->dout_batch_stride, es) &&
+                tma_ok(a->z, a->z_dim_stride, a->z_batch_stride, es) &&
+                tma_ok(a->y, a->y_dim_stride, a->y_batch_stride, es) &&
+                tma_ok(a->B, a->B_state_stride, a->B_batch_stride, es) &&
+                tma_ok(a->C, a->C_state_stride, a->C_batch_stride, es) &&
+                tma_ok(a->du, a->du_dim_stride, a->du_batch_stride, es) &&
+                tma_ok(a->ddelta, a->ddelta_dim_stride, a->ddelta_batch_stride, es) &&
+                tma_ok(a->dz, a->dz_dim_stride, a->dz_batch_stride, es);
+    CUtensorMap maps[10];
+    memset(maps, 0, sizeof(maps));
+    if (p.use_tma) {
+        if ((rc = get_encoder())) return rc;
+        const int TB = kBwdTile;
+        const CUtensorMapSwizzle none = CU_TENSOR_MAP_SWIZZLE_NONE;
+        const CUtensorMapSwizzle osw = is_bf16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+        const int64_t L = a->seqlen, Dm = a->dim, Bs = a->batch, N = a->dstate;
+        if ((rc = encode3d(&maps[0], a->u, is_bf16, L, Dm, Bs, a->u_dim_stride, a->u_batch_stride, TB, dt, none)) ||
+            (rc = encode3d(&maps[1], a->delta, is_bf16, L, Dm, Bs, a->delta_dim_stride, a->delta_batch_stride, TB, dt, none)) ||
+            (rc = encode3d(&maps[2], a->dout, is_bf16, L, Dm, Bs, a->dout_dim_stride, a->dout_batch_stride, TB, dt, none)) ||
+            (rc = encode3d(&maps[3], a->z, is_bf16, L, Dm, Bs, a->z_dim_stride, a->z_batch_stride, TB, dt, none)) ||
+            (rc = encode3d(&maps[4], a->y, is_bf16, L, Dm, Bs, a->y_dim_stride, a->y_batch_stride, TB, dt, none)) ||
+            (rc = encode3d(&maps[5], a->B, is_bf16, L, N, Bs, a->B_state_stride, a->B_batch_stride, TB, (int)N, none)) ||
+            (rc = encode3d(&maps[6], a->C, is_bf16, L, N, Bs, a->C_state_stride, a->C_batch_stride, TB, (int)N, none)) ||
+            (rc = encode3d(&maps[7], a->du, is_bf16, L, Dm, Bs, a->du_dim_stride, a->du_batch_stride, TB, dt, osw)) ||
+            (rc = encode3d(&maps[8], a->ddelta, is_bf16, L, Dm, Bs, a->ddelta_dim_stride, a->ddelta_batch_stride, TB, dt, osw)) ||
+            (rc = encode3d(&maps[9], a->dz, is_bf16, L, Dm, Bs, a->dz_dim_stride, a->dz_batch_stride, TB, dt, osw)))
+            return rc;
+    }
+    cudaError_t e = launch_scan_bwd(p, is_bf16, sp.lpc, maps, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "scan_bwd launch");
+
+    ReduceParams r;
+    memset(&r, 0, sizeof(r));
+    r.batch = p.batch; r.dim = p.dim; r.seqlen = p.seqlen; r.dstate = p.dstate; r.ntile_d = p.ntile_d;
+    r.bc_dtype = is_bf16;
+    r.ws_bc = p.ws_bc; r.ws_a = p.ws_a; r.ws_dd = p.ws_dd;
+    r.dB = a->dB; r.dC = a->dC; r.dA = a->dA; r.dD = a->dD; r.ddelta_bias = a->ddelta_bias;
+    e = launch_scan_reduce(r, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "scan_reduce launch");
+    return SSM_OK;
+}
+
+int ssm_state_update(const ssm_state_update_args* a, void* stream_) {
+    if (!a) return fail(SSM_ERR_INVALID, "ssm_state_update: args is NULL");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    if (a->batch < 1 || a->dim < 1 || a->dstate < 1)
+        return fail(SSM_ERR_INVALID, "ssm_state_update: sizes must be positive");
+    if (a->dstate > 256) return fail(SSM_ERR_INVALID, "selective_update only supports state_dim <= 256");
+    if (!valid_dtype(a->dtype)) return fail(SSM_ERR_INVALID, "ssm_state_update: dtype must be SSM_F32 or SSM_BF16");
+    if (!a->state || !a->state_out || !a->x || !a->dt || !a->A || !a->B || !a->C || !a->out)
+        return fail(SSM_ERR_INVALID, "ssm_state_update: state, state_out, x, dt, A, B, C and out are required");
+    const StateSplit sp = split_states(a->dstate);
+    const int64_t threads = a->batch * a->dim * sp.lpc;
+    if ((threads + 255) / 256 > 0x7fffffff) return fail(SSM_ERR_INVALID, "ssm_state_update: too many rows");
+    UpdParams p;
+    memset(&p, 0, sizeof(p));
+    p.batch = (int)a->batch; p.dim = (int)a->dim; p.dstate = (int)a->dstate;
+    p.dt_softplus = a->dt_softplus;
+    p.state = a->state; p.st_sb = a->state_batch_stride; p.st_sd = a->state_dim_stride;
+    p.state_out = a->state_out; p.so_sb = a->state_out_batch_stride; p.so_sd = a->state_out_dim_stride;
+    p.x = a->x; p.x_sb = a->x_batch_stride;
+    p.dtv = a->dt; p.dt_sb = a->dt_batch_stride;
+    p.A = a->A; p.A_sd = a->A_dim_stride;
+    p.B = a->B; p.B_sb = a->B_batch_stride;
+    p.C = a->C; p.C_sb = a->C_batch_stride;
+    p.D = a->D; p.z = a->z; p.z_sb = a->z_batch_stride;
+    p.dt_bias = a->dt_bias;
+    p.out = a->out; p.out_sb = a->out_batch_stride;
+    cudaError_t e = launch_state_update(p, a->dtype == SSM_BF16, sp.lpc, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "state_update launch");
+    return SSM_OK;
+}
+
+int ssm_check_device_error(int* code, void* stream_) {
+    DevInfo* di;
+    int rc = device_info(&di);
+    if (rc) return rc;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    int v = 0;
+    cudaError_t e = cudaMemcpyAsync(&v, di->err, sizeof(int), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_fail(e, "ssm_check_device_error");
+    if (code) *code = v;
+    if (v != 0) {
+        cudaMemsetAsync(di->err, 0, sizeof(int), stream);
+        cudaStreamSynchronize(stream);
+        return fail(SSM_ERR_DEVICE, "a kernel reported device error %d", v);
+    }
+    return SSM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,164 @@
+// Device helpers shared by the sm_100a selective-scan kernels: element conversion,
+// MUFU exp2, the 128-byte TMA swizzle, TMA tensor copies and mbarriers with bounded
+// waits.  Everything here is written for sm_100a only.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ssm {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Error codes a kernel can leave in the device error word.
+enum DeviceError : int {
+    kDevErrNone = 0,
+    kDevErrTmaTimeout = 1,   // an mbarrier wait for a TMA load ran out of time
+    kDevErrSmemAlign = 2,    // dynamic shared memory base not 1024-byte aligned
+};
+
+// ---------------------------------------------------------------------------------------
+// element conversion
+// ---------------------------------------------------------------------------------------
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+    static __device__ __forceinline__ float to_f(float v) { return v; }
+    static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+template <> struct Elem<__nv_bfloat16> {
+    static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+template <typename T> __device__ __forceinline__ float to_f(T v) { return Elem<T>::to_f(v); }
+template <typename T> __device__ __forceinline__ T from_f(float v) { return Elem<T>::from_f(v); }
+
+// 2^x on the MUFU pipe (PTX ex2.approx.ftz.f32; max relative error 2^-22 per the PTX ISA).
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// softplus with threshold 20, as the reference computes it
+// (csrc/selective_scan/forward_kernel.cu:155-159, built with --use_fast_math).
+__device__ __forceinline__ float softplus20(float x) {
+    return x <= 20.f ? log1pf(__expf(x)) : x;
+}
+
+__device__ __forceinline__ float sigmoidf_fast(float x) {
+    return __fdividef(1.f, 1.f + __expf(-x));
+}
+
+// ---------------------------------------------------------------------------------------
+// 128-byte swizzle (CU_TENSOR_MAP_SWIZZLE_128B): inside each 1024-byte block of eight
+// 128-byte rows, 16-byte chunk j of row r sits at chunk position j ^ (r & 7).  Tiles whose
+// rows are exactly 128 bytes use it so that column-wise accesses by consecutive rows hit
+// distinct banks.  Returns a byte offset.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t byte_in_row) {
+    return row * 128u + ((((byte_in_row >> 4) ^ row) & 7u) << 4) + (byte_in_row & 15u);
+}
+
+// 64-byte swizzle (CU_TENSOR_MAP_SWIZZLE_64B) for 64-byte rows: 16-byte chunk j of row r
+// sits at chunk position j ^ ((r >> 1) & 3) (address bits [4:5] ^= bits [7:8]).
+__device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t byte_in_row) {
+    return row * 64u + ((((byte_in_row >> 4) ^ (row >> 1)) & 3u) << 4) + (byte_in_row & 15u);
+}
+
+// ---------------------------------------------------------------------------------------
+// shared-memory address helpers, mbarrier, TMA
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait: gives up after roughly `limit_cycles` SM clocks (about 1 s by default)
+// and returns false, so that a lost copy turns into an error code instead of a hang.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  long long limit_cycles = 2000000000LL) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long start = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - start > limit_cycles) return false;
+    }
+    return true;
+}
+
+// Make generic-proxy writes to shared memory visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 3-D tiled TMA load, global -> shared, completion counted on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 3-D tiled TMA store, shared -> global (out-of-range parts of the box are not written).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0,
+                                             int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until every committed TMA store has finished reading shared memory.
+__device__ __forceinline__ void tma_store_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Wait until every committed TMA store is complete (writes visible in global memory).
+__device__ __forceinline__ void tma_store_wait_all() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ float4 lds128(const void* p) {
+    return *reinterpret_cast<const float4*>(p);
+}
+
+}  // namespace ssm

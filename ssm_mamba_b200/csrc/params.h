@@ -1,0 +1,95 @@
+// Kernel parameter blocks (host and device).  Built by capi.cu from the C-ABI argument
+// structs after validation; strides are in elements.
+#pragma once
+
+#include <stdint.h>
+
+namespace ssm {
+
+struct FwdParams {
+    int batch, dim, seqlen, dstate;
+    int dt;              // channels per CTA
+    int ntile_d;         // ceil(dim / dt)
+    int use_tma;         // 1: TMA tensor-map path, 0: plain-load fallback
+    int delta_softplus, padding_right;
+    int ckpt_format;     // 0 compact, 1 reference
+    int ckpt_len, nck;
+    const void* u; int64_t u_sb, u_sd;
+    const void* delta; int64_t delta_sb, delta_sd;
+    const float* A; int64_t A_sd;
+    const void* B; int64_t B_sb, B_sn;
+    const void* C; int64_t C_sb, C_sn;
+    const float* D;
+    const void* z; int64_t z_sb, z_sd;
+    const float* delta_bias;
+    const float* h_init;
+    const int64_t* length;
+    void* out; int64_t out_sb, out_sd;
+    void* y; int64_t y_sb, y_sd;
+    float* ckpt;
+    float* h_last;
+    // rechunk mode (reference-format chunk states -> compact checkpoints, with the
+    // reference backward's load rules): restart the state from `restart` every
+    // `restart_len` tokens and zero-fill loads from token len on when seqlen % 128 != 0
+    const float* restart;
+    int restart_len, restart_nck;
+    int* err;            // device error word
+};
+
+struct BwdParams {
+    int batch, dim, seqlen, dstate;
+    int dt, ntile_d;
+    int use_tma;
+    int delta_softplus, padding_right;
+    int ref_len;         // reproduce the reference backward's length semantics
+    int ckpt_format, ckpt_len, nck;
+    const void* u; int64_t u_sb, u_sd;
+    const void* delta; int64_t delta_sb, delta_sd;
+    const float* A; int64_t A_sd;
+    const void* B; int64_t B_sb, B_sn;
+    const void* C; int64_t C_sb, C_sn;
+    const float* D;
+    const void* z; int64_t z_sb, z_sd;
+    const float* delta_bias;
+    const float* h_init;
+    const int64_t* length;
+    const void* y; int64_t y_sb, y_sd;
+    const float* ckpt;
+    const void* dout; int64_t dout_sb, dout_sd;
+    const float* dh_last;
+    void* du; int64_t du_sb, du_sd;
+    void* ddelta; int64_t ddelta_sb, ddelta_sd;
+    void* dz; int64_t dz_sb, dz_sd;
+    float* dh_init;
+    // workspace partials
+    float* ws_bc;        // (ntile_d, batch, 2, dstate, seqlen): per channel-tile dB, dC sums
+    float* ws_a;         // (batch, dim, dstate): per-batch dA
+    float* ws_dd;        // (batch, dim, 2): per-batch dD, ddelta_bias
+    int* err;
+};
+
+struct ReduceParams {
+    int batch, dim, seqlen, dstate, ntile_d;
+    int bc_dtype;        // 0 f32, 1 bf16
+    const float* ws_bc; const float* ws_a; const float* ws_dd;
+    void* dB; void* dC;
+    float* dA; float* dD; float* ddelta_bias;
+};
+
+struct UpdParams {
+    int batch, dim, dstate;
+    int dt_softplus;
+    const float* state; int64_t st_sb, st_sd;
+    float* state_out; int64_t so_sb, so_sd;
+    const void* x; int64_t x_sb;
+    const void* dtv; int64_t dt_sb;
+    const float* A; int64_t A_sd;
+    const void* B; int64_t B_sb;
+    const void* C; int64_t C_sb;
+    const float* D;
+    const void* z; int64_t z_sb;
+    const float* dt_bias;
+    void* out; int64_t out_sb;
+};
+
+}  // namespace ssm

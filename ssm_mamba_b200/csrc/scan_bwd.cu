@@ -1,0 +1,634 @@
+// Backward selective scan for sm_100a, plus the deterministic reduction of its partials.
+//
+// Replaces the reference backward kernel (nmquan1503/ssm-mamba,
+// csrc/selective_scan/backward_kernel.cu:89-478).  Same gradients -- recompute the states,
+// run dh_t = exp(delta_{t+1} A) dh_{t+1} + C_t dout_t backwards, and form du, ddelta, dA,
+// dB, dC, dD, ddelta_bias, dh_init -- with a different organisation:
+//
+//  * Same CTA / thread layout as the forward: a CTA owns (batch row, `dt` channels), a
+//    thread owns one channel and SPT states, and walks the sequence backwards in tiles of
+//    32 tokens, each split into sub-tiles of K tokens.
+//  * Every sub-tile restarts from a state checkpoint the forward saved K tokens earlier,
+//    recomputes its K states into registers (one exp2 per token and state), then runs the
+//    reverse recurrence over them.  There is no block scan and no second exp pass.
+//  * dB and dC (sums over channels) are reduced in registers: the lanes of the channels in a
+//    warp hold their states in an XOR-rotated order (lane r keeps state 4g + (s ^ r) in
+//    register s), so the 4-lane transpose-reduce is three shuffles and three adds with no
+//    selects.  Warps combine through shared memory, CTAs through a per-channel-tile
+//    workspace that ssm_scan_reduce_kernel sums in a fixed order.  No floating-point atomics
+//    (the reference issues one atomicAdd per (token, state, channel), backward_kernel.cu:395-400).
+//  * du / ddelta need sums over states: a reduce-scatter across the state lanes leaves each
+//    lane with whole tokens to finish (skip term, softplus derivative, dD, ddelta_bias).
+//  * Inputs arrive by one TMA stage that is refilled for the next tile as soon as the tile
+//    prologue has consumed it; du, ddelta, dz leave by TMA stores.
+//  * With `length` the reference's rules are reproduced exactly (backward_kernel.cu:225-400):
+//    chunks of 128 tokens starting at or after len are skipped, loads are zero-filled from
+//    len on when seqlen % 128 != 0, padded tokens are identity steps without C*dout, and only
+//    tokens t < len feed ddelta, dA, dB and dC.
+#include "common.cuh"
+#include "params.h"
+#include "scan_layout.h"
+#include "warp_reduce.cuh"
+
+namespace ssm {
+
+template <typename IT, int LPC, int SPT, int K>
+__global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
+    const __grid_constant__ BwdParams p, const __grid_constant__ CUtensorMap tm_u,
+    const __grid_constant__ CUtensorMap tm_delta, const __grid_constant__ CUtensorMap tm_dout,
+    const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_y,
+    const __grid_constant__ CUtensorMap tm_B, const __grid_constant__ CUtensorMap tm_C,
+    const __grid_constant__ CUtensorMap tm_du, const __grid_constant__ CUtensorMap tm_ddelta,
+    const __grid_constant__ CUtensorMap tm_dz) {
+    constexpr int ES = sizeof(IT);
+    constexpr int TB = kBwdTile;
+    constexpr int NS = LPC * SPT;
+    constexpr int CPW = 32 / LPC;                 // channel lanes per warp
+    constexpr bool ROT = (CPW >= 4) && (SPT == 4);
+    constexpr int NROT = ROT ? 4 : 1;
+    constexpr int Q = NS / 4;
+    constexpr int QM = (Q < 8 ? Q : 8) - 1;
+    constexpr int NSUB = TB / K;
+    constexpr int RS = TB + 4;
+    constexpr int V = 2 * K;                      // S1 and S2 per sub-tile token
+    constexpr int RR = LPC < V ? LPC : V;
+    static_assert(TB % K == 0 && K % 4 == 0, "sub-tiles must be whole float4 groups");
+
+    extern __shared__ __align__(1024) unsigned char smem[];
+    if ((smem_u32(smem) & 1023u) != 0u) {
+        if (threadIdx.x == 0) atomicExch(p.err, kDevErrSmemAlign);
+        return;
+    }
+    const int DT = p.dt;
+    const int tid = threadIdx.x, nthr = DT * LPC;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int c = tid / LPC, g = tid % LPC;
+    const int cw = lane / LPC;
+    const int rot = ROT ? (cw & 3) : 0;
+    const int b = blockIdx.x / p.ntile_d, tile_d = blockIdx.x % p.ntile_d;
+    const int d0 = tile_d * DT, d = d0 + c;
+    const bool dvalid = d < p.dim;
+    const int N = p.dstate, Lq = p.seqlen;
+    const bool has_z = p.z != nullptr;
+    const BwdSmem S = bwd_smem_layout(DT, NS, N, ES, NROT, nthr / 32, has_z ? 1 : 0);
+    float* sD = reinterpret_cast<float*>(smem + S.sD);
+    float* sDU = reinterpret_cast<float*>(smem + S.sDU);
+    float* sG = reinterpret_cast<float*>(smem + S.sG);
+    float* sSP = reinterpret_cast<float*>(smem + S.sSP);
+    float* sU = reinterpret_cast<float*>(smem + S.sU);
+    float* sB = reinterpret_cast<float*>(smem + S.sB);
+    float* sC = reinterpret_cast<float*>(smem + S.sC);
+    float* slots = reinterpret_cast<float*>(smem + S.slots);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S.bar);
+
+    // ---- per-batch length rules (reference semantics when length is given) ----------------
+    const bool ref = p.length != nullptr;
+    int len = Lq;
+    if (ref) {
+        long long v = p.length[b];
+        len = v < 0 ? 0 : (v > Lq ? Lq : (int)v);
+    }
+    const int Lload = (ref && (Lq % 128) != 0) ? len : Lq;           // zero-fill from here
+    const int Rskip = ref ? min(Lq, ((len + 127) / 128) * 128) : Lq;  // skipped chunks
+    const int mlo = (ref && !p.padding_right) ? Lq - len : 0;         // masked: t < mlo
+    const int mhi = (ref && p.padding_right) ? len : Lq;              //      or t >= mhi
+
+    // ---- per-thread constants ----------------------------------------------------------------
+    float A2[SPT], An[SPT], G[SPT], an[SPT], dAacc[SPT];
+    int nidx[SPT];
+#pragma unroll
+    for (int s = 0; s < SPT; s++) {
+        const int n = g * SPT + (s ^ rot);
+        nidx[s] = n;
+        const bool ok = dvalid && n < N;
+        const float a = ok ? p.A[(int64_t)d * p.A_sd + n] : 0.f;
+        An[s] = a;
+        A2[s] = a * kLog2e;
+        G[s] = (ok && p.dh_last) ? p.dh_last[((int64_t)b * p.dim + d) * N + n] : 0.f;
+        an[s] = 1.f;
+        dAacc[s] = 0.f;
+    }
+    const float Dd = (dvalid && p.D) ? p.D[d] : 0.f;
+    float dD_acc = 0.f, db_acc = 0.f;
+
+    auto load_ckpt = [&](int ts, float (&hv)[SPT]) {
+#pragma unroll
+        for (int s = 0; s < SPT; s++) {
+            const int n = nidx[s];
+            float v = 0.f;
+            if (dvalid && n < N) {
+                if (ts == 0) {
+                    if (p.h_init) v = p.h_init[((int64_t)b * p.dim + d) * N + n];
+                } else {
+                    v = p.ckpt[(((int64_t)b * p.nck + (ts / K - 1)) * p.dim + d) * N + n];
+                }
+            }
+            hv[s] = v;
+        }
+    };
+
+    const int ntiles = (Lq + TB - 1) / TB;
+    const uint32_t tile_bytes = (uint32_t)DT * TB * ES;
+    const uint32_t bc_bytes = (uint32_t)N * TB * ES;
+    const uint32_t stage_bytes = (has_z ? 5u : 3u) * tile_bytes + 2u * bc_bytes;
+
+    auto issue = [&](int tile) {
+        const int t0 = tile * TB;
+        mbar_arrive_expect_tx(bar, stage_bytes);
+        tma_load_3d(smem + S.u, &tm_u, bar, t0, d0, b);
+        tma_load_3d(smem + S.delta, &tm_delta, bar, t0, d0, b);
+        tma_load_3d(smem + S.dout, &tm_dout, bar, t0, d0, b);
+        if (has_z) {
+            tma_load_3d(smem + S.z, &tm_z, bar, t0, d0, b);
+            tma_load_3d(smem + S.y, &tm_y, bar, t0, d0, b);
+        }
+        tma_load_3d(smem + S.B, &tm_B, bar, t0, 0, b);
+        tma_load_3d(smem + S.C, &tm_C, bar, t0, 0, b);
+    };
+
+    auto load_plain = [&](int tile) {
+        const int t0 = tile * TB;
+        const IT zero = from_f<IT>(0.f);
+        for (int i = tid; i < DT * TB; i += nthr) {
+            const int cc = i / TB, tt = i % TB, dd = d0 + cc, tg = t0 + tt;
+            const bool in = dd < p.dim && tg < Lq;
+            const uint32_t off = (uint32_t)(cc * TB + tt) * ES;
+            *reinterpret_cast<IT*>(smem + S.u + off) =
+                in ? static_cast<const IT*>(p.u)[b * p.u_sb + dd * p.u_sd + tg] : zero;
+            *reinterpret_cast<IT*>(smem + S.delta + off) =
+                in ? static_cast<const IT*>(p.delta)[b * p.delta_sb + dd * p.delta_sd + tg] : zero;
+            *reinterpret_cast<IT*>(smem + S.dout + off) =
+                in ? static_cast<const IT*>(p.dout)[b * p.dout_sb + dd * p.dout_sd + tg] : zero;
+            if (has_z) {
+                *reinterpret_cast<IT*>(smem + S.z + off) =
+                    in ? static_cast<const IT*>(p.z)[b * p.z_sb + dd * p.z_sd + tg] : zero;
+                *reinterpret_cast<IT*>(smem + S.y + off) =
+                    in ? static_cast<const IT*>(p.y)[b * p.y_sb + dd * p.y_sd + tg] : zero;
+            }
+        }
+        for (int i = tid; i < N * TB; i += nthr) {
+            const int n = i / TB, tt = i % TB, tg = t0 + tt;
+            const bool in = tg < Lq;
+            const uint32_t off = (uint32_t)(n * TB + tt) * ES;
+            *reinterpret_cast<IT*>(smem + S.B + off) =
+                in ? static_cast<const IT*>(p.B)[b * p.B_sb + n * p.B_sn + tg] : zero;
+            *reinterpret_cast<IT*>(smem + S.C + off) =
+                in ? static_cast<const IT*>(p.C)[b * p.C_sb + n * p.C_sn + tg] : zero;
+        }
+    };
+
+    // byte offset of (channel row, token) in a swizzled output tile
+    auto out_off = [&](int row, int t) -> uint32_t {
+        return ES == 2 ? swz64(row, t * ES) : swz128(row, t * ES);
+    };
+
+    if (p.use_tma && tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (p.use_tma && tid == 0) issue(ntiles - 1);
+
+    // checkpoint of the first sub-tile processed, then prefetched one sub-tile ahead
+    float h0[SPT], h0n[SPT];
+    {
+        const int last_ts = ((Lq - 1) / K) * K;
+        load_ckpt(last_ts, h0);
+    }
+
+    for (int it = ntiles - 1; it >= 0; it--) {
+        const int t0 = it * TB;
+        int ok = 1;
+        if (p.use_tma) {
+            if (tid == 0) tma_store_wait_read_all();  // previous tile's output tiles are free
+            ok = mbar_wait_bounded(bar, (uint32_t)((ntiles - 1 - it) & 1)) ? 1 : 0;
+        } else {
+            load_plain(it);
+        }
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) atomicExch(p.err, kDevErrTmaTimeout);
+            return;
+        }
+
+        // ---- prologue ------------------------------------------------------------------------
+        for (int i = tid; i < DT * TB; i += nthr) {
+            const int cc = i / TB, tt = i % TB, tg = t0 + tt;
+            const uint32_t off = (uint32_t)(cc * TB + tt) * ES;
+            const bool ld = tg < Lload;
+            const float uv = ld ? to_f(*reinterpret_cast<const IT*>(smem + S.u + off)) : 0.f;
+            const float dr = ld ? to_f(*reinterpret_cast<const IT*>(smem + S.delta + off)) : 0.f;
+            float dv = ld ? to_f(*reinterpret_cast<const IT*>(smem + S.dout + off)) : 0.f;
+            const float x = dr + ((d0 + cc < p.dim && p.delta_bias) ? p.delta_bias[d0 + cc] : 0.f);
+            float dl = x, spg = 1.f;
+            if (p.delta_softplus && x <= 20.f) {
+                const float e = __expf(x);
+                dl = log1pf(e);
+                spg = __fdividef(e, 1.f + e);
+            }
+            if (has_z) {
+                const float zv = to_f(*reinterpret_cast<const IT*>(smem + S.z + off));
+                const float yv = to_f(*reinterpret_cast<const IT*>(smem + S.y + off));
+                const float sg = sigmoidf_fast(zv);
+                const float dzv = dv * yv * sg * (1.f + zv * (1.f - sg));
+                dv = dv * zv * sg;
+                *reinterpret_cast<IT*>(smem + S.dz + out_off(cc, tt)) =
+                    from_f<IT>(tg < Rskip ? dzv : 0.f);
+            }
+            sD[cc * RS + tt] = dl;
+            sDU[cc * RS + tt] = dl * uv;
+            sG[cc * RS + tt] = dv;
+            sSP[cc * RS + tt] = spg;
+            sU[cc * RS + tt] = uv;
+        }
+        for (int i = tid; i < Q * TB; i += nthr) {
+            const int q = i / TB, tt = i % TB, tg = t0 + tt;
+            const bool ld = tg < Lload;
+            float vb[4], vc[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int n = q * 4 + k;
+                const uint32_t off = (uint32_t)(n * TB + tt) * ES;
+                vb[k] = (ld && n < N) ? to_f(*reinterpret_cast<const IT*>(smem + S.B + off)) : 0.f;
+                vc[k] = (ld && n < N) ? to_f(*reinterpret_cast<const IT*>(smem + S.C + off)) : 0.f;
+            }
+#pragma unroll
+            for (int r = 0; r < NROT; r++) {
+                const int pos = r * (int)S.rot_stride + tt * NS + ((q ^ (tt & QM)) << 2);
+                *reinterpret_cast<float4*>(sB + pos) =
+                    make_float4(vb[0 ^ r], vb[1 ^ r], vb[2 ^ r], vb[3 ^ r]);
+                *reinterpret_cast<float4*>(sC + pos) =
+                    make_float4(vc[0 ^ r], vc[1 ^ r], vc[2 ^ r], vc[3 ^ r]);
+            }
+        }
+        __syncthreads();
+        if (p.use_tma && tid == 0 && it > 0) issue(it - 1);  // raw tiles consumed
+
+        // ---- sub-tiles, last to first -------------------------------------------------------
+        unsigned char* odu = smem + S.du;
+        unsigned char* odd = smem + S.ddelta;
+        float* wslot = slots + warp * S.slot_stride;
+#pragma unroll 1
+        for (int sub = NSUB - 1; sub >= 0; sub--) {
+            const int tl0 = sub * K;
+            const int ts = t0 + tl0;
+            if (ts >= Lq) continue;  // past the end of the sequence: nothing to do
+            // prefetch the checkpoint of the next sub-tile (one step earlier in time)
+            if (ts > 0) load_ckpt(ts - K, h0n);
+
+            float v[V];
+            if (ts >= Rskip) {
+                // reference: a 128-token chunk that starts at or after len is skipped
+#pragma unroll
+                for (int j = 0; j < V; j++) v[j] = 0.f;
+#pragma unroll
+                for (int k = 0; k < K; k++) {
+                    if (ROT) {
+                        if (cw < 4) {
+                            const int n = g * 4 + cw;
+                            if (n < N) {
+                                wslot[n * (TB + 1) + tl0 + k] = 0.f;
+                                wslot[(NS + n) * (TB + 1) + tl0 + k] = 0.f;
+                            }
+                        }
+                    } else if (cw == 0) {
+#pragma unroll
+                        for (int s = 0; s < SPT; s++) {
+                            const int n = nidx[s];
+                            if (n < N) {
+                                wslot[n * (TB + 1) + tl0 + k] = 0.f;
+                                wslot[(NS + n) * (TB + 1) + tl0 + k] = 0.f;
+                            }
+                        }
+                    }
+                }
+            } else {
+                const bool general = (ts + K > Lq) || (ref && !(ts + K <= len && ts >= mlo && ts + K <= mhi));
+                float av[K][SPT], hv[K][SPT];
+                // recompute the K states from the checkpoint
+#pragma unroll
+                for (int k4 = 0; k4 < K; k4 += 4) {
+                    const float4 dl4 = lds128(sD + c * RS + tl0 + k4);
+                    const float4 du4 = lds128(sDU + c * RS + tl0 + k4);
+                    const float dls[4] = {dl4.x, dl4.y, dl4.z, dl4.w};
+                    const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int k = k4 + j, t = tl0 + k;
+                        float Bv[SPT];
+#pragma unroll
+                        for (int s4 = 0; s4 < SPT / 4; s4++) {
+                            const int qq = g * (SPT / 4) + s4;
+                            const float4 b4 = lds128(sB + rot * (int)S.rot_stride + t * NS + ((qq ^ (t & QM)) << 2));
+                            Bv[s4 * 4 + 0] = b4.x; Bv[s4 * 4 + 1] = b4.y;
+                            Bv[s4 * 4 + 2] = b4.z; Bv[s4 * 4 + 3] = b4.w;
+                        }
+                        bool msk = false;
+                        if (general) {
+                            const int tg = ts + k;
+                            msk = tg >= Lq || tg < mlo || tg >= mhi;
+                        }
+#pragma unroll
+                        for (int s = 0; s < SPT; s++) {
+                            const float prev = k == 0 ? h0[s] : hv[k - 1][s];
+                            float a = ex2(dls[j] * A2[s]);
+                            float bb = dus[j] * Bv[s];
+                            if (msk) { a = 1.f; bb = 0.f; }
+                            av[k][s] = a;
+                            hv[k][s] = fmaf(a, prev, bb);
+                        }
+                    }
+                }
+                // reverse recurrence and gradient terms
+#pragma unroll
+                for (int k4 = K - 4; k4 >= 0; k4 -= 4) {
+                    const float4 dl4 = lds128(sD + c * RS + tl0 + k4);
+                    const float4 du4 = lds128(sDU + c * RS + tl0 + k4);
+                    const float4 dg4 = lds128(sG + c * RS + tl0 + k4);
+                    const float dls[4] = {dl4.x, dl4.y, dl4.z, dl4.w};
+                    const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
+                    const float dgs[4] = {dg4.x, dg4.y, dg4.z, dg4.w};
+#pragma unroll
+                    for (int j = 3; j >= 0; j--) {
+                        const int k = k4 + j, t = tl0 + k;
+                        float Bv[SPT], Cv[SPT];
+#pragma unroll
+                        for (int s4 = 0; s4 < SPT / 4; s4++) {
+                            const int qq = g * (SPT / 4) + s4;
+                            const int pos = rot * (int)S.rot_stride + t * NS + ((qq ^ (t & QM)) << 2);
+                            const float4 b4 = lds128(sB + pos);
+                            const float4 c4 = lds128(sC + pos);
+                            Bv[s4 * 4 + 0] = b4.x; Bv[s4 * 4 + 1] = b4.y;
+                            Bv[s4 * 4 + 2] = b4.z; Bv[s4 * 4 + 3] = b4.w;
+                            Cv[s4 * 4 + 0] = c4.x; Cv[s4 * 4 + 1] = c4.y;
+                            Cv[s4 * 4 + 2] = c4.z; Cv[s4 * 4 + 3] = c4.w;
+                        }
+                        bool msk = false, vld = true;
+                        if (general) {
+                            const int tg = ts + k;
+                            msk = tg >= Lq || tg < mlo || tg >= mhi;
+                            vld = tg < len;
+                        }
+                        const float dl = dls[j], du = dus[j], dg = dgs[j];
+                        const float dlv = vld ? dl : 0.f;
+                        float s1 = 0.f, s2 = 0.f;
+                        float dBv[SPT], dCv[SPT];
+#pragma unroll
+                        for (int s = 0; s < SPT; s++) {
+                            const float inj = msk ? 0.f : dg * Cv[s];
+                            const float Gs = fmaf(an[s], G[s], inj);
+                            G[s] = Gs;
+                            an[s] = av[k][s];
+                            const float qv = fmaf(-du, Bv[s], hv[k][s]);
+                            s1 = fmaf(Gs, Bv[s], s1);
+                            const float w = Gs * qv;
+                            s2 = fmaf(An[s], w, s2);
+                            dAacc[s] = fmaf(dlv, w, dAacc[s]);
+                            dBv[s] = vld ? Gs * du : 0.f;
+                            dCv[s] = vld ? dg * hv[k][s] : 0.f;
+                        }
+                        v[k] = s1;
+                        v[K + k] = vld ? s2 : 0.f;
+                        // dB, dC: sum over the channels of this warp
+                        if (ROT) {
+                            float rb = dBv[0], rc = dCv[0];
+#pragma unroll
+                            for (int i = 1; i < 4; i++) {
+                                rb += __shfl_xor_sync(0xffffffffu, dBv[i], LPC * i);
+                                rc += __shfl_xor_sync(0xffffffffu, dCv[i], LPC * i);
+                            }
+#pragma unroll
+                            for (int m = 4; m < CPW; m *= 2) {
+                                rb += __shfl_xor_sync(0xffffffffu, rb, LPC * m);
+                                rc += __shfl_xor_sync(0xffffffffu, rc, LPC * m);
+                            }
+                            if (cw < 4) {
+                                const int n = g * 4 + cw;
+                                if (n < N) {
+                                    wslot[n * (TB + 1) + t] = rb;
+                                    wslot[(NS + n) * (TB + 1) + t] = rc;
+                                }
+                            }
+                        } else {
+#pragma unroll
+                            for (int m = 1; m < CPW; m *= 2) {
+#pragma unroll
+                                for (int s = 0; s < SPT; s++) {
+                                    dBv[s] += __shfl_xor_sync(0xffffffffu, dBv[s], LPC * m);
+                                    dCv[s] += __shfl_xor_sync(0xffffffffu, dCv[s], LPC * m);
+                                }
+                            }
+                            if (cw == 0) {
+#pragma unroll
+                                for (int s = 0; s < SPT; s++) {
+                                    const int n = nidx[s];
+                                    if (n < N) {
+                                        wslot[n * (TB + 1) + t] = dBv[s];
+                                        wslot[(NS + n) * (TB + 1) + t] = dCv[s];
+                                    }
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+            // gradient of the initial state: decay of token 0 times dh_0 (dh_last when the
+            // whole row was skipped)
+            if (ts == 0 && p.dh_init != nullptr && dvalid) {
+#pragma unroll
+                for (int s = 0; s < SPT; s++) {
+                    const int n = nidx[s];
+                    if (n < N) p.dh_init[((int64_t)b * p.dim + d) * N + n] = an[s] * G[s];
+                }
+            }
+
+            // ---- per-token sums over states, then finish the tokens this lane owns ---------
+            reduce_scatter<LPC, V>(v, g);
+            const bool skipped = ts >= Rskip;
+            auto finish = [&](int k, float s1, float s2) {
+                const int t = tl0 + k, tg = ts + k;
+                float du = 0.f, ddl = 0.f;
+                if (!skipped) {
+                    const float dl = sD[c * RS + t], dg = sG[c * RS + t], uv = sU[c * RS + t];
+                    du = fmaf(Dd, dg, dl * s1);
+                    ddl = tg < len ? fmaf(uv, s1, s2) * sSP[c * RS + t] : 0.f;
+                    dD_acc = fmaf(dg, uv, dD_acc);
+                    db_acc += ddl;
+                }
+                *reinterpret_cast<IT*>(odu + out_off(c, t)) = from_f<IT>(du);
+                *reinterpret_cast<IT*>(odd + out_off(c, t)) = from_f<IT>(ddl);
+            };
+            if (LPC <= K) {
+#pragma unroll
+                for (int r = 0; r < K / LPC; r++) finish(g + LPC * r, v[LPC * r], v[K + LPC * r]);
+            } else {
+                const float other = __shfl_xor_sync(0xffffffffu, v[0], K);
+                if (g < K) finish(g, v[0], other);
+            }
+            if (ts > 0) {
+#pragma unroll
+                for (int s = 0; s < SPT; s++) h0[s] = h0n[s];
+            }
+        }
+        __syncthreads();
+
+        // ---- CTA sum of the warp dB/dC slots -> workspace; store du, ddelta, dz -------------
+        const int nw = nthr / 32;
+        for (int i = tid; i < 2 * N * TB; i += nthr) {
+            const int q = i / (N * TB), rem = i % (N * TB), n = rem / TB, t = rem % TB;
+            const int tg = t0 + t;
+            float acc = 0.f;
+            for (int w = 0; w < nw; w++) acc += slots[w * S.slot_stride + (q * NS + n) * (TB + 1) + t];
+            if (tg < Lq)
+                p.ws_bc[((((int64_t)tile_d * p.batch + b) * 2 + q) * N + n) * Lq + tg] = acc;
+        }
+        if (p.use_tma) {
+            if (tid == 0) {
+                fence_proxy_async_smem();
+                tma_store_3d(&tm_du, odu, t0, d0, b);
+                tma_store_3d(&tm_ddelta, odd, t0, d0, b);
+                if (has_z) tma_store_3d(&tm_dz, smem + S.dz, t0, d0, b);
+                tma_store_commit();
+            }
+        } else {
+            for (int i = tid; i < DT * TB; i += nthr) {
+                const int cc = i / TB, tt = i % TB, dd = d0 + cc, tg = t0 + tt;
+                if (dd >= p.dim || tg >= Lq) continue;
+                const uint32_t off = out_off(cc, tt);
+                static_cast<IT*>(p.du)[b * p.du_sb + dd * p.du_sd + tg] =
+                    *reinterpret_cast<const IT*>(odu + off);
+                static_cast<IT*>(p.ddelta)[b * p.ddelta_sb + dd * p.ddelta_sd + tg] =
+                    *reinterpret_cast<const IT*>(odd + off);
+                if (has_z)
+                    static_cast<IT*>(p.dz)[b * p.dz_sb + dd * p.dz_sd + tg] =
+                        *reinterpret_cast<const IT*>(smem + S.dz + off);
+            }
+            __syncthreads();
+        }
+    }
+
+    // ---- per-(batch, channel) partials of dA, dD, ddelta_bias ----------------------------------
+#pragma unroll
+    for (int s = 0; s < SPT; s++) {
+        const int n = nidx[s];
+        if (dvalid && n < N) p.ws_a[((int64_t)b * p.dim + d) * N + n] = dAacc[s];
+    }
+    dD_acc = allreduce<LPC>(dD_acc);
+    db_acc = allreduce<LPC>(db_acc);
+    if (g == 0 && dvalid) {
+        p.ws_dd[((int64_t)b * p.dim + d) * 2 + 0] = dD_acc;
+        p.ws_dd[((int64_t)b * p.dim + d) * 2 + 1] = db_acc;
+    }
+    if (p.use_tma && tid == 0) tma_store_wait_all();
+}
+
+// Deterministic final sums: dB/dC over channel tiles, dA/dD/ddelta_bias over the batch.
+__global__ void scan_reduce_kernel(const __grid_constant__ ReduceParams p) {
+    const int64_t nbc = (int64_t)p.batch * p.dstate * p.seqlen;   // per quantity
+    const int64_t na = (int64_t)p.dim * p.dstate;
+    const int64_t total = 2 * nbc + na + p.dim;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        if (i < 2 * nbc) {
+            const int q = (int)(i / nbc);
+            const int64_t r = i % nbc;                 // (b, n, t) flat
+            const int64_t b = r / ((int64_t)p.dstate * p.seqlen);
+            const int64_t nt = r % ((int64_t)p.dstate * p.seqlen);
+            float acc = 0.f;
+            for (int tile = 0; tile < p.ntile_d; tile++)
+                acc += p.ws_bc[(((int64_t)tile * p.batch + b) * 2 + q) * p.dstate * p.seqlen + nt];
+            void* dst = q == 0 ? p.dB : p.dC;
+            if (p.bc_dtype == 1)
+                static_cast<__nv_bfloat16*>(dst)[r] = __float2bfloat16_rn(acc);
+            else
+                static_cast<float*>(dst)[r] = acc;
+        } else if (i < 2 * nbc + na) {
+            const int64_t r = i - 2 * nbc;             // (d, n)
+            float acc = 0.f;
+            for (int b = 0; b < p.batch; b++) acc += p.ws_a[(int64_t)b * na + r];
+            p.dA[r] = acc;
+        } else {
+            const int64_t dd = i - 2 * nbc - na;
+            float a0 = 0.f, a1 = 0.f;
+            for (int b = 0; b < p.batch; b++) {
+                a0 += p.ws_dd[((int64_t)b * p.dim + dd) * 2 + 0];
+                a1 += p.ws_dd[((int64_t)b * p.dim + dd) * 2 + 1];
+            }
+            if (p.dD) p.dD[dd] = a0;
+            if (p.ddelta_bias) p.ddelta_bias[dd] = a1;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// launch
+// ---------------------------------------------------------------------------------------
+template <typename IT, int LPC, int SPT, int K>
+static cudaError_t launch_bwd_t(const BwdParams& p, const CUtensorMap* maps, cudaStream_t stream) {
+    auto kern = scan_bwd_kernel<IT, LPC, SPT, K>;
+    constexpr int CPW = 32 / LPC;
+    constexpr int NROT = ((CPW >= 4) && (SPT == 4)) ? 4 : 1;
+    const BwdSmem L = bwd_smem_layout(p.dt, LPC * SPT, p.dstate, sizeof(IT), NROT,
+                                      p.dt * LPC / 32, p.z != nullptr);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+    if (e != cudaSuccess) return e;
+    kern<<<p.batch * p.ntile_d, p.dt * LPC, L.total, stream>>>(p, maps[0], maps[1], maps[2], maps[3],
+                                                              maps[4], maps[5], maps[6], maps[7],
+                                                              maps[8], maps[9]);
+    return cudaGetLastError();
+}
+
+int bwd_occupancy(int is_bf16, int lpc, int dt, int dstate, int has_z) {
+    const void* k = nullptr;
+    int spt = 4;
+#define SSM_BWD_K(LPC_, SPT_, K_)                                                             \
+    if (lpc == LPC_) {                                                                       \
+        k = is_bf16 ? (const void*)scan_bwd_kernel<__nv_bfloat16, LPC_, SPT_, K_>            \
+                    : (const void*)scan_bwd_kernel<float, LPC_, SPT_, K_>;                   \
+        spt = SPT_;                                                                          \
+    }
+    SSM_BWD_K(1, 4, 8) SSM_BWD_K(2, 4, 8) SSM_BWD_K(4, 4, 8) SSM_BWD_K(8, 4, 8) SSM_BWD_K(16, 4, 8)
+    SSM_BWD_K(32, 8, 4)
+#undef SSM_BWD_K
+    if (!k) return 0;
+    const int cpw = 32 / lpc;
+    const int nrot = (cpw >= 4 && spt == 4) ? 4 : 1;
+    const size_t smem = bwd_smem_layout(dt, lpc * spt, dstate, is_bf16 ? 2 : 4, nrot, dt * lpc / 32, has_z).total;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, dt * lpc, smem) != cudaSuccess) return 0;
+    return n;
+}
+
+size_t bwd_smem_bytes(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z) {
+    const int cpw = 32 / lpc;
+    const int nrot = (cpw >= 4 && spt == 4) ? 4 : 1;
+    return bwd_smem_layout(dt, lpc * spt, dstate, is_bf16 ? 2 : 4, nrot, dt * lpc / 32, has_z).total;
+}
+
+cudaError_t launch_scan_bwd(const BwdParams& p, int is_bf16, int lpc, const CUtensorMap* maps,
+                            cudaStream_t stream) {
+#define SSM_BWD_CASE(LPC_, SPT_, K_)                                                     \
+    if (lpc == LPC_) {                                                                   \
+        return is_bf16 ? launch_bwd_t<__nv_bfloat16, LPC_, SPT_, K_>(p, maps, stream)    \
+                       : launch_bwd_t<float, LPC_, SPT_, K_>(p, maps, stream);           \
+    }
+    SSM_BWD_CASE(1, 4, 8)
+    SSM_BWD_CASE(2, 4, 8)
+    SSM_BWD_CASE(4, 4, 8)
+    SSM_BWD_CASE(8, 4, 8)
+    SSM_BWD_CASE(16, 4, 8)
+    SSM_BWD_CASE(32, 8, 4)
+#undef SSM_BWD_CASE
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_scan_reduce(const ReduceParams& p, cudaStream_t stream) {
+    const int64_t total = 2 * (int64_t)p.batch * p.dstate * p.seqlen + (int64_t)p.dim * p.dstate + p.dim;
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    if (blocks < 1) blocks = 1;
+    scan_reduce_kernel<<<(int)blocks, 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace ssm

@@ -1,0 +1,394 @@
+// Forward selective scan for sm_100a.
+//
+// Replaces the reference forward kernel (nmquan1503/ssm-mamba,
+// csrc/selective_scan/forward_kernel.cu:69-264).  Same math -- delta = softplus(delta + bias),
+// h_t = exp(delta*A) h_{t-1} + delta*u*B, y = D*u + sum_n C*h -- with a different shape:
+//
+//  * One CTA owns one batch row b and a tile of `dt` channels and walks the whole sequence
+//    in tiles of T tokens (T*sizeof(elem) = 128 bytes).  The time recurrence stays in
+//    registers, so there is no block scan and no per-chunk carry through shared memory.
+//  * A thread owns one channel and SPT consecutive states; the LPC = NS/SPT lanes of a
+//    channel are adjacent.  y_t = sum_n C h needs one reduce-scatter across those lanes
+//    every G = max(4, LPC) tokens.
+//  * Each tile's u, delta, z and the (B, C) tile are brought in by 3-D TMA loads
+//    (128-byte swizzle, 2 stages, mbarrier completion) and the outputs leave by TMA stores.
+//    B and C are loaded once per CTA and shared by all of its channels (the reference
+//    re-reads them for every channel).  Shapes whose strides TMA cannot describe use a
+//    plain-load fallback into the same shared-memory layout.
+//  * softplus, delta*u and the padding mask are computed once per (channel, token) in a
+//    tile prologue; the inner loop is exp2 + 2 FMA + 1 MUL per (token, state).
+//  * The gate out = y * silu(z) (modules/mamba.py:182 in the reference) is fused into the
+//    epilogue, and the pre-gate y is optionally written for the backward.
+//  * State checkpoints every ckpt_len tokens: compact (batch, nck, dim, dstate) for this
+//    library's backward, or the reference's interleaved (prod, state) chunk carries
+//    (selective_scan.cpp:271-274, forward_kernel.cu:224-228).
+#include "common.cuh"
+#include "params.h"
+#include "scan_layout.h"
+#include "warp_reduce.cuh"
+
+namespace ssm {
+
+template <typename IT, int LPC, int SPT>
+__global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
+    const __grid_constant__ FwdParams p, const __grid_constant__ CUtensorMap tm_u,
+    const __grid_constant__ CUtensorMap tm_delta, const __grid_constant__ CUtensorMap tm_z,
+    const __grid_constant__ CUtensorMap tm_B, const __grid_constant__ CUtensorMap tm_C,
+    const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_y) {
+    constexpr int ES = sizeof(IT);
+    constexpr int T = 128 / ES;              // tokens per tile
+    constexpr int NS = LPC * SPT;            // padded state count
+    constexpr int G = LPC > 4 ? LPC : 4;     // tokens per reduce group
+    constexpr int Q = NS / 4;                // float4 groups per B/C row
+    constexpr int QM = (Q < 8 ? Q : 8) - 1;  // swizzle mask for the f32 B/C rows
+    static_assert(T % G == 0, "tile must hold whole reduce groups");
+
+    extern __shared__ __align__(1024) unsigned char smem[];
+    if ((smem_u32(smem) & 1023u) != 0u) {  // the swizzled TMA tiles need a 1024-byte base
+        if (threadIdx.x == 0) atomicExch(p.err, kDevErrSmemAlign);
+        return;
+    }
+    const int DT = p.dt;
+    const FwdSmem L = fwd_smem_layout(DT, NS, ES, p.z != nullptr, p.y != nullptr);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
+    float* sD = reinterpret_cast<float*>(smem + L.sD);
+    float* sDU = reinterpret_cast<float*>(smem + L.sDU);
+    float* sB = reinterpret_cast<float*>(smem + L.sB);
+    float* sC = reinterpret_cast<float*>(smem + L.sC);
+    constexpr int RS = T + 4;                // padded row of sD / sDU (floats)
+
+    const int tid = threadIdx.x;
+    const int nthr = DT * LPC;
+    const int c = tid / LPC, g = tid % LPC;
+    const int b = blockIdx.x / p.ntile_d;
+    const int d0 = (blockIdx.x % p.ntile_d) * DT;
+    const int d = d0 + c;
+    const bool dvalid = d < p.dim;
+    const int N = p.dstate, Lq = p.seqlen;
+    const int ntiles = (Lq + T - 1) / T;
+    const bool has_z = p.z != nullptr;
+    const bool want_y = p.y != nullptr;
+    const bool want_prod = p.ckpt != nullptr && p.ckpt_format == 1;
+
+    int len = Lq;
+    if (p.length) {
+        long long v = p.length[b];
+        len = v < 0 ? 0 : (v > Lq ? Lq : (int)v);
+    }
+    const bool has_len = p.length != nullptr;
+    const bool rechunk = p.restart != nullptr;
+    const bool want_out = p.out != nullptr;
+    // rechunk mode loads as the reference backward does: zero-filled from len on when
+    // seqlen % 128 != 0 (backward_kernel.cu:242-246)
+    const int Lload = (rechunk && has_len && (Lq % 128) != 0) ? len : Lq;
+
+    // per-thread constants and state
+    float A2[SPT], h[SPT];
+#pragma unroll
+    for (int s = 0; s < SPT; s++) {
+        const int n = g * SPT + s;
+        const bool ok = dvalid && n < N;
+        A2[s] = ok ? p.A[(int64_t)d * p.A_sd + n] * kLog2e : 0.f;
+        h[s] = (ok && p.h_init) ? p.h_init[((int64_t)b * p.dim + d) * N + n] : 0.f;
+    }
+    const float Dd = (dvalid && p.D) ? p.D[d] : 0.f;
+    float Ssum = 0.f;  // running sum of effective delta (for the reference checkpoint product)
+
+    const uint32_t tile_bytes = (uint32_t)DT * 128u;
+    const uint32_t bc_bytes = (uint32_t)N * 128u;
+    const uint32_t stage_bytes = (has_z ? 3u : 2u) * tile_bytes + 2u * bc_bytes;
+
+    auto issue = [&](int tile, int st) {
+        const int t0 = tile * T;
+        mbar_arrive_expect_tx(&bar[st], stage_bytes);
+        tma_load_3d(smem + L.u[st], &tm_u, &bar[st], t0, d0, b);
+        tma_load_3d(smem + L.delta[st], &tm_delta, &bar[st], t0, d0, b);
+        if (has_z) tma_load_3d(smem + L.z[st], &tm_z, &bar[st], t0, d0, b);
+        tma_load_3d(smem + L.B[st], &tm_B, &bar[st], t0, 0, b);
+        tma_load_3d(smem + L.C[st], &tm_C, &bar[st], t0, 0, b);
+    };
+
+    // plain-load fallback into the same swizzled layout (zero fill out of range)
+    auto load_plain = [&](int tile, int st) {
+        const int t0 = tile * T;
+        for (int i = tid; i < DT * T; i += nthr) {
+            const int cc = i / T, tt = i % T, dd = d0 + cc, tg = t0 + tt;
+            const bool in = dd < p.dim && tg < Lq;
+            const uint32_t off = swz128(cc, tt * ES);
+            const IT zero = from_f<IT>(0.f);
+            *reinterpret_cast<IT*>(smem + L.u[st] + off) =
+                in ? static_cast<const IT*>(p.u)[b * p.u_sb + dd * p.u_sd + tg] : zero;
+            *reinterpret_cast<IT*>(smem + L.delta[st] + off) =
+                in ? static_cast<const IT*>(p.delta)[b * p.delta_sb + dd * p.delta_sd + tg] : zero;
+            if (has_z)
+                *reinterpret_cast<IT*>(smem + L.z[st] + off) =
+                    in ? static_cast<const IT*>(p.z)[b * p.z_sb + dd * p.z_sd + tg] : zero;
+        }
+        for (int i = tid; i < N * T; i += nthr) {
+            const int n = i / T, tt = i % T, tg = t0 + tt;
+            const bool in = tg < Lq;
+            const uint32_t off = swz128(n, tt * ES);
+            const IT zero = from_f<IT>(0.f);
+            *reinterpret_cast<IT*>(smem + L.B[st] + off) =
+                in ? static_cast<const IT*>(p.B)[b * p.B_sb + n * p.B_sn + tg] : zero;
+            *reinterpret_cast<IT*>(smem + L.C[st] + off) =
+                in ? static_cast<const IT*>(p.C)[b * p.C_sb + n * p.C_sn + tg] : zero;
+        }
+    };
+
+    auto write_ckpt = [&](int k) {
+        if (!dvalid) return;
+        if (p.ckpt_format == 0) {
+            float* dst = p.ckpt + (((int64_t)b * p.nck + k) * p.dim + d) * N;
+#pragma unroll
+            for (int s = 0; s < SPT; s++) {
+                const int n = g * SPT + s;
+                if (n < N) dst[n] = h[s];
+            }
+        } else {
+            float* dst = p.ckpt + (((int64_t)b * p.dim + d) * p.nck + k) * 2 * N;
+#pragma unroll
+            for (int s = 0; s < SPT; s++) {
+                const int n = g * SPT + s;
+                if (n < N) {
+                    dst[2 * n] = ex2(A2[s] * Ssum);
+                    dst[2 * n + 1] = h[s];
+                }
+            }
+        }
+    };
+
+    if (p.use_tma && tid == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_mbar_init();
+        prefetch_tensormap(&tm_u);
+        prefetch_tensormap(&tm_delta);
+        prefetch_tensormap(&tm_B);
+        prefetch_tensormap(&tm_C);
+    }
+    __syncthreads();
+    if (p.use_tma && tid == 0) {
+        issue(0, 0);
+        if (ntiles > 1) issue(1, 1);
+    }
+
+    for (int it = 0; it < ntiles; it++) {
+        const int st = it & 1;
+        const int t0 = it * T;
+        int ok = 1;
+        if (p.use_tma) {
+            ok = mbar_wait_bounded(&bar[st], (it >> 1) & 1) ? 1 : 0;
+        } else {
+            load_plain(it, st);
+        }
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) atomicExch(p.err, kDevErrTmaTimeout);
+            return;
+        }
+
+        // ---- prologue: per (channel, token) values, B/C to f32 rows --------------------
+        const unsigned char* su = smem + L.u[st];
+        const unsigned char* sdl = smem + L.delta[st];
+        for (int i = tid; i < DT * T; i += nthr) {
+            const int cc = i / T, tt = i % T, tg = t0 + tt;
+            const uint32_t off = swz128(cc, tt * ES);
+            const bool ld = tg < Lload;
+            const float x = (ld ? to_f(*reinterpret_cast<const IT*>(sdl + off)) : 0.f) +
+                            ((d0 + cc < p.dim && p.delta_bias) ? p.delta_bias[d0 + cc] : 0.f);
+            const float dl = p.delta_softplus ? softplus20(x) : x;
+            const float uv = ld ? to_f(*reinterpret_cast<const IT*>(su + off)) : 0.f;
+            bool masked = tg >= Lq;
+            if (has_len) masked |= p.padding_right ? (tg >= len) : (tg < Lq - len);
+            sD[cc * RS + tt] = masked ? 0.f : dl;
+            sDU[cc * RS + tt] = masked ? 0.f : dl * uv;
+        }
+        const unsigned char* sBr = smem + L.B[st];
+        const unsigned char* sCr = smem + L.C[st];
+        for (int i = tid; i < Q * T; i += nthr) {
+            const int q = i / T, tt = i % T;
+            const bool ld = t0 + tt < Lload;
+            float vb[4], vc[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int n = q * 4 + k;
+                const uint32_t off = swz128(n, tt * ES);
+                vb[k] = (ld && n < N) ? to_f(*reinterpret_cast<const IT*>(sBr + off)) : 0.f;
+                vc[k] = (ld && n < N) ? to_f(*reinterpret_cast<const IT*>(sCr + off)) : 0.f;
+            }
+            const int pos = tt * NS + ((q ^ (tt & QM)) << 2);
+            *reinterpret_cast<float4*>(sB + pos) = make_float4(vb[0], vb[1], vb[2], vb[3]);
+            *reinterpret_cast<float4*>(sC + pos) = make_float4(vc[0], vc[1], vc[2], vc[3]);
+        }
+        // the previous tile's TMA stores must be done reading the output tiles
+        if (p.use_tma && tid == 0) tma_store_wait_read_all();
+        __syncthreads();
+
+        // ---- scan ------------------------------------------------------------------------
+        const unsigned char* sz = smem + L.z[st];
+        unsigned char* so = smem + L.out;
+        unsigned char* sy = smem + L.y;
+#pragma unroll 1
+        for (int q0 = 0; q0 < T; q0 += G) {
+            float yv[G];
+#pragma unroll
+            for (int sb = 0; sb < G; sb += 4) {
+                const int tl = q0 + sb;
+                const float4 dl4 = lds128(sD + c * RS + tl);
+                const float4 du4 = lds128(sDU + c * RS + tl);
+                const float dls[4] = {dl4.x, dl4.y, dl4.z, dl4.w};
+                const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int t = tl + j;
+                    float Bv[SPT], Cv[SPT];
+#pragma unroll
+                    for (int s4 = 0; s4 < SPT / 4; s4++) {
+                        const int qq = g * (SPT / 4) + s4;
+                        const int pos = t * NS + ((qq ^ (t & QM)) << 2);
+                        const float4 b4 = lds128(sB + pos);
+                        const float4 c4 = lds128(sC + pos);
+                        Bv[s4 * 4 + 0] = b4.x; Bv[s4 * 4 + 1] = b4.y;
+                        Bv[s4 * 4 + 2] = b4.z; Bv[s4 * 4 + 3] = b4.w;
+                        Cv[s4 * 4 + 0] = c4.x; Cv[s4 * 4 + 1] = c4.y;
+                        Cv[s4 * 4 + 2] = c4.z; Cv[s4 * 4 + 3] = c4.w;
+                    }
+                    float yacc = 0.f;
+#pragma unroll
+                    for (int s = 0; s < SPT; s++) {
+                        const float a = ex2(dls[j] * A2[s]);
+                        h[s] = fmaf(a, h[s], dus[j] * Bv[s]);
+                        yacc = fmaf(Cv[s], h[s], yacc);
+                    }
+                    yv[sb + j] = yacc;
+                }
+                if (want_prod) Ssum += (dls[0] + dls[1]) + (dls[2] + dls[3]);
+                const int tg_end = t0 + tl + 4;
+                if (rechunk && tg_end < Lq && (tg_end % p.restart_len) == 0 && dvalid) {
+                    // the reference backward restarts every chunk from the forward's state
+                    const float* src = p.restart +
+                        (((int64_t)b * p.dim + d) * p.restart_nck + (tg_end / p.restart_len - 1)) * 2 * N;
+#pragma unroll
+                    for (int s = 0; s < SPT; s++) {
+                        const int n = g * SPT + s;
+                        if (n < N) h[s] = src[2 * n + 1];
+                    }
+                }
+                if (p.ckpt && tg_end <= Lq && (tg_end % p.ckpt_len) == 0)
+                    write_ckpt(tg_end / p.ckpt_len - 1);
+            }
+            // reduce-scatter y over the LPC lanes of this channel: afterwards slot LPC*r
+            // holds the full sum for token q0 + LPC*r + g.
+            reduce_scatter<LPC, G>(yv, g);
+            // epilogue: skip term, gate, pre-gate copy
+#pragma unroll
+            for (int r = 0; r < G / LPC; r++) {
+                const int tl = q0 + LPC * r + g;
+                const uint32_t off = swz128(c, tl * ES);
+                const float uv = to_f(*reinterpret_cast<const IT*>(su + off));
+                if (!want_out) continue;
+                const float yt = fmaf(Dd, uv, yv[LPC * r]);
+                float o = yt;
+                if (has_z) {
+                    const float zv = to_f(*reinterpret_cast<const IT*>(sz + off));
+                    o = yt * zv * sigmoidf_fast(zv);
+                }
+                *reinterpret_cast<IT*>(so + off) = from_f<IT>(o);
+                if (want_y) *reinterpret_cast<IT*>(sy + off) = from_f<IT>(yt);
+            }
+        }
+        __syncthreads();
+
+        // ---- store the output tiles, refill this stage ------------------------------------
+        if (p.use_tma) {
+            if (tid == 0) {
+                if (want_out) {
+                    fence_proxy_async_smem();
+                    tma_store_3d(&tm_out, so, t0, d0, b);
+                    if (want_y) tma_store_3d(&tm_y, sy, t0, d0, b);
+                    tma_store_commit();
+                }
+                if (it + 2 < ntiles) issue(it + 2, st);
+            }
+        } else {
+            for (int i = tid; i < DT * T && want_out; i += nthr) {
+                const int cc = i / T, tt = i % T, dd = d0 + cc, tg = t0 + tt;
+                if (dd >= p.dim || tg >= Lq) continue;
+                const uint32_t off = swz128(cc, tt * ES);
+                static_cast<IT*>(p.out)[b * p.out_sb + dd * p.out_sd + tg] =
+                    *reinterpret_cast<const IT*>(so + off);
+                if (want_y)
+                    static_cast<IT*>(p.y)[b * p.y_sb + dd * p.y_sd + tg] =
+                        *reinterpret_cast<const IT*>(sy + off);
+            }
+            __syncthreads();
+        }
+    }
+
+    // the last checkpoint of a sequence whose length is not a multiple of ckpt_len
+    if (p.ckpt && (Lq % p.ckpt_len) != 0) write_ckpt(p.nck - 1);
+    if (p.h_last && dvalid) {
+#pragma unroll
+        for (int s = 0; s < SPT; s++) {
+            const int n = g * SPT + s;
+            if (n < N) p.h_last[((int64_t)b * p.dim + d) * N + n] = h[s];
+        }
+    }
+    if (p.use_tma && tid == 0) tma_store_wait_all();
+}
+
+// ---------------------------------------------------------------------------------------
+// launch
+// ---------------------------------------------------------------------------------------
+template <typename IT, int LPC, int SPT>
+static cudaError_t launch_fwd_t(const FwdParams& p, const CUtensorMap* maps, cudaStream_t stream) {
+    auto kern = scan_fwd_kernel<IT, LPC, SPT>;
+    const FwdSmem L = fwd_smem_layout(p.dt, LPC * SPT, sizeof(IT), p.z != nullptr, p.y != nullptr);
+    const size_t smem = L.total;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    const int grid = p.batch * p.ntile_d;
+    kern<<<grid, p.dt * LPC, smem, stream>>>(p, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5],
+                                            maps[6]);
+    return cudaGetLastError();
+}
+
+// states-per-thread / lanes-per-channel for a padded state count
+cudaError_t launch_scan_fwd(const FwdParams& p, int is_bf16, int lpc, const CUtensorMap* maps,
+                            cudaStream_t stream) {
+#define SSM_FWD_CASE(LPC_, SPT_)                                                        \
+    if (lpc == LPC_) {                                                                  \
+        return is_bf16 ? launch_fwd_t<__nv_bfloat16, LPC_, SPT_>(p, maps, stream)       \
+                       : launch_fwd_t<float, LPC_, SPT_>(p, maps, stream);              \
+    }
+    SSM_FWD_CASE(1, 4)
+    SSM_FWD_CASE(2, 4)
+    SSM_FWD_CASE(4, 4)
+    SSM_FWD_CASE(8, 4)
+    SSM_FWD_CASE(16, 4)
+    SSM_FWD_CASE(32, 8)
+#undef SSM_FWD_CASE
+    return cudaErrorInvalidValue;
+}
+
+// Resident CTAs per SM for a CTA of dt channels (registers, shared memory, threads).
+int fwd_occupancy(int is_bf16, int lpc, int dt, int has_z, int has_y) {
+    const void* k = nullptr;
+    int spt = 4;
+#define SSM_FWD_K(LPC_, SPT_)                                                                 \
+    if (lpc == LPC_) {                                                                       \
+        k = is_bf16 ? (const void*)scan_fwd_kernel<__nv_bfloat16, LPC_, SPT_>                \
+                    : (const void*)scan_fwd_kernel<float, LPC_, SPT_>;                       \
+        spt = SPT_;                                                                          \
+    }
+    SSM_FWD_K(1, 4) SSM_FWD_K(2, 4) SSM_FWD_K(4, 4) SSM_FWD_K(8, 4) SSM_FWD_K(16, 4) SSM_FWD_K(32, 8)
+#undef SSM_FWD_K
+    if (!k) return 0;
+    const size_t smem = fwd_smem_layout(dt, lpc * spt, is_bf16 ? 2 : 4, has_z, has_y).total;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, dt * lpc, smem) != cudaSuccess) return 0;
+    return n;
+}
+
+}  // namespace ssm

@@ -1,0 +1,122 @@
+// Single-token selective state update (decode) for sm_100a.
+//
+// Replaces the reference update kernel (nmquan1503/ssm-mamba, csrc/selective_update/kernel.cu:17-91):
+// h' = exp(dt*A)*h + dt*x*B, out = sum_n C*h' + D*x, dt = softplus(dt + dt_bias).
+// The reference runs one 32-thread CTA per (batch, channel) with one state per thread, half
+// the lanes idle for d_state = 16, scalar loads, a CUB block reduction and a freshly
+// allocated output state.  Here a thread owns SPT consecutive states of one (batch,
+// channel) row, reads and writes them with 128-bit accesses (in place when state_out ==
+// state), the LPC lanes of a row reduce C*h' with shuffles, and a 256-thread CTA covers
+// 256/LPC consecutive rows, so a warp moves contiguous 512-byte state segments.  The gate
+// out *= silu(z) and the optional softplus are fused.
+#include "common.cuh"
+#include "params.h"
+#include "warp_reduce.cuh"
+
+namespace ssm {
+
+template <typename IT, int LPC, int SPT>
+__global__ void __launch_bounds__(256) state_update_kernel(const __grid_constant__ UpdParams p) {
+    const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t row = tid / LPC;
+    const int g = tid % LPC;
+    const int64_t nrows = (int64_t)p.batch * p.dim;
+    // rows past the end still take part in the shuffles, with their work masked off
+    const bool live = row < nrows;
+    const int64_t b = live ? row / p.dim : 0;
+    const int64_t d = live ? row % p.dim : 0;
+    const int N = p.dstate;
+    const int n0 = g * SPT;
+
+    float xv = 0.f, dtv = 0.f, zv = 0.f;
+    if (live) {
+        xv = to_f(static_cast<const IT*>(p.x)[b * p.x_sb + d]);
+        dtv = to_f(static_cast<const IT*>(p.dtv)[b * p.dt_sb + d]);
+        if (p.z) zv = to_f(static_cast<const IT*>(p.z)[b * p.z_sb + d]);
+        if (p.dt_bias) dtv += p.dt_bias[d];
+    }
+    const float dl = p.dt_softplus ? softplus20(dtv) : dtv;
+    const float dx = dl * xv;
+
+    const float* hin = p.state + b * p.st_sb + d * p.st_sd + n0;
+    float* hout = p.state_out + b * p.so_sb + d * p.so_sd + n0;
+    const float* Ar = p.A + d * p.A_sd + n0;
+    const IT* Br = static_cast<const IT*>(p.B) + b * p.B_sb + n0;
+    const IT* Cr = static_cast<const IT*>(p.C) + b * p.C_sb + n0;
+
+    float h[SPT], a[SPT], bv[SPT], cv[SPT];
+    const bool full = live && (n0 + SPT <= N);
+    const bool vec = full && ((reinterpret_cast<uintptr_t>(hin) | reinterpret_cast<uintptr_t>(hout) |
+                               reinterpret_cast<uintptr_t>(Ar)) & 15u) == 0;
+    if (vec) {
+#pragma unroll
+        for (int s4 = 0; s4 < SPT; s4 += 4) {
+            const float4 hv = *reinterpret_cast<const float4*>(hin + s4);
+            const float4 av = __ldg(reinterpret_cast<const float4*>(Ar + s4));
+            h[s4] = hv.x; h[s4 + 1] = hv.y; h[s4 + 2] = hv.z; h[s4 + 3] = hv.w;
+            a[s4] = av.x; a[s4 + 1] = av.y; a[s4 + 2] = av.z; a[s4 + 3] = av.w;
+        }
+    } else {
+#pragma unroll
+        for (int s = 0; s < SPT; s++) {
+            const bool ok = live && n0 + s < N;
+            h[s] = ok ? hin[s] : 0.f;
+            a[s] = ok ? Ar[s] : 0.f;
+        }
+    }
+#pragma unroll
+    for (int s = 0; s < SPT; s++) {
+        const bool ok = live && n0 + s < N;
+        bv[s] = ok ? to_f(Br[s]) : 0.f;
+        cv[s] = ok ? to_f(Cr[s]) : 0.f;
+    }
+
+    float y = 0.f;
+#pragma unroll
+    for (int s = 0; s < SPT; s++) {
+        h[s] = fmaf(ex2(dl * (a[s] * kLog2e)), h[s], dx * bv[s]);
+        y = fmaf(cv[s], h[s], y);
+    }
+    y = allreduce<LPC>(y);
+
+    if (vec) {
+#pragma unroll
+        for (int s4 = 0; s4 < SPT; s4 += 4)
+            *reinterpret_cast<float4*>(hout + s4) = make_float4(h[s4], h[s4 + 1], h[s4 + 2], h[s4 + 3]);
+    } else if (live) {
+#pragma unroll
+        for (int s = 0; s < SPT; s++)
+            if (n0 + s < N) hout[s] = h[s];
+    }
+    if (live && g == 0) {
+        float o = y + (p.D ? p.D[d] : 0.f) * xv;
+        if (p.z) o = o * zv * sigmoidf_fast(zv);
+        static_cast<IT*>(p.out)[b * p.out_sb + d] = from_f<IT>(o);
+    }
+}
+
+template <typename IT, int LPC, int SPT>
+static cudaError_t launch_upd_t(const UpdParams& p, cudaStream_t stream) {
+    const int64_t threads = (int64_t)p.batch * p.dim * LPC;
+    const int64_t blocks = (threads + 255) / 256;
+    state_update_kernel<IT, LPC, SPT><<<(unsigned)blocks, 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_state_update(const UpdParams& p, int is_bf16, int lpc, cudaStream_t stream) {
+#define SSM_UPD_CASE(LPC_, SPT_)                                                  \
+    if (lpc == LPC_) {                                                            \
+        return is_bf16 ? launch_upd_t<__nv_bfloat16, LPC_, SPT_>(p, stream)       \
+                       : launch_upd_t<float, LPC_, SPT_>(p, stream);              \
+    }
+    SSM_UPD_CASE(1, 4)
+    SSM_UPD_CASE(2, 4)
+    SSM_UPD_CASE(4, 4)
+    SSM_UPD_CASE(8, 4)
+    SSM_UPD_CASE(16, 4)
+    SSM_UPD_CASE(32, 8)
+#undef SSM_UPD_CASE
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace ssm

@@ -1,0 +1,313 @@
+// Thin torch binding of the C ABI (include/ssm_b200.h): checks tensors, allocates outputs
+// with the caching allocator, fills the argument structs and calls the library on the
+// current stream.  The checks follow the reference host glue (nmquan1503/ssm-mamba,
+// csrc/selective_scan/selective_scan.cpp:15-32, 229-268, 314-351) and raise the same kind
+// of RuntimeError; there is no CPU path -- non-CUDA tensors are rejected.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <optional>
+#include <vector>
+
+#include "../../include/ssm_b200.h"
+
+namespace {
+
+int32_t dtype_code(const at::Tensor& t) {
+    if (t.scalar_type() == at::kFloat) return SSM_F32;
+    if (t.scalar_type() == at::kBFloat16) return SSM_BF16;
+    TORCH_CHECK(false, "selective scan tensors must be float32 or bfloat16, got ", t.scalar_type());
+    return -1;
+}
+
+void check_cuda(const at::Tensor& t, const char* name) {
+    TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+
+// (batch, dim, seqlen) with unit innermost stride
+void check_bdl(const at::Tensor& t, const char* name, int64_t B, int64_t D, int64_t L, at::ScalarType st) {
+    check_cuda(t, name);
+    TORCH_CHECK(t.dim() == 3, name, " must be a 3D tensor");
+    TORCH_CHECK(t.size(0) == B && t.size(1) == D && t.size(2) == L, name, " must have shape (", B, ", ", D,
+                ", ", L, ")");
+    TORCH_CHECK(t.scalar_type() == st, name, " must have dtype ", st);
+    TORCH_CHECK(t.stride(2) == 1, name, " must be contiguous along the sequence");
+}
+
+void check_f32(const at::Tensor& t, const char* name, std::vector<int64_t> shape) {
+    check_cuda(t, name);
+    TORCH_CHECK(t.scalar_type() == at::kFloat, name, " must be float32 tensor");
+    TORCH_CHECK(t.sizes() == at::IntArrayRef(shape), name, " has the wrong shape");
+}
+
+void ok(int rc) {
+    if (rc != SSM_OK) TORCH_CHECK(false, ssm_last_error());
+}
+
+template <typename T>
+T* ptr(const std::optional<at::Tensor>& t) {
+    return t.has_value() ? static_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+struct Common {
+    int64_t B, D, L, N;
+    int32_t dt;
+};
+
+Common check_inputs(const at::Tensor& u, const at::Tensor& delta, const at::Tensor& A, const at::Tensor& Bm,
+                    const at::Tensor& Cm, const std::optional<at::Tensor>& D, const std::optional<at::Tensor>& z,
+                    const std::optional<at::Tensor>& delta_bias, const std::optional<at::Tensor>& h_init,
+                    const std::optional<at::Tensor>& length) {
+    check_cuda(u, "u");
+    TORCH_CHECK(u.dim() == 3, "u must be a 3D tensor");
+    Common c{u.size(0), u.size(1), u.size(2), 0, dtype_code(u)};
+    TORCH_CHECK(A.dim() == 2, "A must be a 2D tensor");
+    c.N = A.size(1);
+    TORCH_CHECK(c.N <= 256, "selective_scan only supports state_dim <= 256");
+    check_bdl(u, "u", c.B, c.D, c.L, u.scalar_type());
+    check_bdl(delta, "delta", c.B, c.D, c.L, u.scalar_type());
+    check_cuda(A, "A");
+    TORCH_CHECK(A.scalar_type() == at::kFloat && A.size(0) == c.D && A.stride(1) == 1,
+                "A must be float32 of shape (dim, state_dim) with unit state stride");
+    for (auto* bc : {&Bm, &Cm}) {
+        const char* nm = bc == &Bm ? "B" : "C";
+        check_cuda(*bc, nm);
+        TORCH_CHECK(bc->dim() == 3 && bc->size(0) == c.B && bc->size(1) == c.N && bc->size(2) == c.L, nm,
+                    " must have shape (batch, state_dim, seq_len)");
+        TORCH_CHECK(bc->scalar_type() == u.scalar_type(), nm, " must have the dtype of u");
+        TORCH_CHECK(bc->stride(2) == 1, nm, " must be contiguous along the sequence");
+    }
+    if (D) check_f32(*D, "D", {c.D});
+    if (D) TORCH_CHECK(D->is_contiguous(), "D must be contiguous");
+    if (delta_bias) check_f32(*delta_bias, "delta_bias", {c.D});
+    if (delta_bias) TORCH_CHECK(delta_bias->is_contiguous(), "delta_bias must be contiguous");
+    if (z) check_bdl(*z, "z", c.B, c.D, c.L, u.scalar_type());
+    if (h_init) {
+        check_f32(*h_init, "h_init", {c.B, c.D, c.N});
+        TORCH_CHECK(h_init->is_contiguous(), "h_init must be contiguous");
+    }
+    if (length) {
+        TORCH_CHECK(length->is_cuda(), "length must be a CUDA tensor");
+        TORCH_CHECK(length->scalar_type() == at::kLong, "length must be long tensor");
+        TORCH_CHECK(length->is_contiguous(), "length must be contiguous");
+        TORCH_CHECK(length->dim() == 1 && length->size(0) == c.B, "length must have shape (batch_size,)");
+    }
+    return c;
+}
+
+ssm_scan_fwd_args fwd_args(const Common& c, const at::Tensor& u, const at::Tensor& delta, const at::Tensor& A,
+                           const at::Tensor& Bm, const at::Tensor& Cm, const std::optional<at::Tensor>& D,
+                           const std::optional<at::Tensor>& z, const std::optional<at::Tensor>& delta_bias,
+                           const std::optional<at::Tensor>& h_init, const std::optional<at::Tensor>& length,
+                           bool padding_right, bool delta_softplus) {
+    ssm_scan_fwd_args a;
+    memset(&a, 0, sizeof(a));
+    a.batch = c.B; a.dim = c.D; a.seqlen = c.L; a.dstate = c.N; a.dtype = c.dt;
+    a.delta_softplus = delta_softplus; a.padding_right = padding_right;
+    a.u = u.data_ptr(); a.u_batch_stride = u.stride(0); a.u_dim_stride = u.stride(1);
+    a.delta = delta.data_ptr(); a.delta_batch_stride = delta.stride(0); a.delta_dim_stride = delta.stride(1);
+    a.A = A.data_ptr<float>(); a.A_dim_stride = A.stride(0);
+    a.B = Bm.data_ptr(); a.B_batch_stride = Bm.stride(0); a.B_state_stride = Bm.stride(1);
+    a.C = Cm.data_ptr(); a.C_batch_stride = Cm.stride(0); a.C_state_stride = Cm.stride(1);
+    a.D = ptr<const float>(D);
+    if (z) { a.z = z->data_ptr(); a.z_batch_stride = z->stride(0); a.z_dim_stride = z->stride(1); }
+    a.delta_bias = ptr<const float>(delta_bias);
+    a.h_init = ptr<const float>(h_init);
+    a.length = ptr<const int64_t>(length);
+    return a;
+}
+
+// Forward.  ckpt_mode: 0 none, 1 compact (for ssm_scan_bwd), 2 reference layout.
+// Returns [out, y or undefined, ckpt or undefined, h_last or undefined].
+std::vector<at::Tensor> scan_fwd(const at::Tensor& u, const at::Tensor& delta, const at::Tensor& A,
+                                 const at::Tensor& Bm, const at::Tensor& Cm, const std::optional<at::Tensor>& D,
+                                 const std::optional<at::Tensor>& z, const std::optional<at::Tensor>& delta_bias,
+                                 const std::optional<at::Tensor>& h_init, const std::optional<at::Tensor>& length,
+                                 bool padding_right, bool delta_softplus, bool want_y, int64_t ckpt_mode,
+                                 bool want_h_last) {
+    Common c = check_inputs(u, delta, A, Bm, Cm, D, z, delta_bias, h_init, length);
+    c10::cuda::CUDAGuard guard(u.device());
+    ssm_scan_fwd_args a = fwd_args(c, u, delta, A, Bm, Cm, D, z, delta_bias, h_init, length, padding_right,
+                                   delta_softplus);
+    at::Tensor out = at::empty({c.B, c.D, c.L}, u.options());
+    at::Tensor y, ck, hl;
+    a.out = out.data_ptr(); a.out_batch_stride = out.stride(0); a.out_dim_stride = out.stride(1);
+    if (want_y) {
+        y = at::empty({c.B, c.D, c.L}, u.options());
+        a.y = y.data_ptr(); a.y_batch_stride = y.stride(0); a.y_dim_stride = y.stride(1);
+    }
+    const auto f32 = u.options().dtype(at::kFloat);
+    if (ckpt_mode == 1) {
+        const int64_t k = ssm_scan_ckpt_len(c.N);
+        ck = at::empty({c.B, ssm_scan_num_ckpt(c.L, k), c.D, c.N}, f32);
+        a.ckpt = ck.data_ptr<float>(); a.ckpt_format = SSM_CKPT_COMPACT; a.ckpt_len = k;
+    } else if (ckpt_mode == 2) {
+        ck = at::empty({c.B, c.D, ssm_scan_num_ckpt(c.L, 128), 2 * c.N}, f32);
+        a.ckpt = ck.data_ptr<float>(); a.ckpt_format = SSM_CKPT_REFERENCE; a.ckpt_len = 128;
+    }
+    if (want_h_last) {
+        hl = at::empty({c.B, c.D, c.N}, f32);
+        a.h_last = hl.data_ptr<float>();
+    }
+    ok(ssm_scan_fwd(&a, at::cuda::getCurrentCUDAStream().stream()));
+    return {out, y, ck, hl};
+}
+
+// Compact checkpoints rebuilt from the reference-layout chunk states.
+at::Tensor ckpt_from_reference(const at::Tensor& u, const at::Tensor& delta, const at::Tensor& A,
+                               const at::Tensor& Bm, const at::Tensor& Cm,
+                               const std::optional<at::Tensor>& delta_bias, const std::optional<at::Tensor>& h_init,
+                               const std::optional<at::Tensor>& length, bool padding_right, bool delta_softplus,
+                               const at::Tensor& ref_ckpt) {
+    Common c = check_inputs(u, delta, A, Bm, Cm, std::nullopt, std::nullopt, delta_bias, h_init, length);
+    c10::cuda::CUDAGuard guard(u.device());
+    check_f32(ref_ckpt, "h", {c.B, c.D, ssm_scan_num_ckpt(c.L, 128), 2 * c.N});
+    TORCH_CHECK(ref_ckpt.is_contiguous(), "h must be contiguous");
+    ssm_scan_fwd_args a = fwd_args(c, u, delta, A, Bm, Cm, std::nullopt, std::nullopt, delta_bias, h_init, length,
+                                   padding_right, delta_softplus);
+    const int64_t k = ssm_scan_ckpt_len(c.N);
+    at::Tensor ck = at::empty({c.B, ssm_scan_num_ckpt(c.L, k), c.D, c.N}, u.options().dtype(at::kFloat));
+    a.ckpt = ck.data_ptr<float>(); a.ckpt_format = SSM_CKPT_COMPACT; a.ckpt_len = k;
+    ok(ssm_scan_ckpt_from_reference(&a, ref_ckpt.data_ptr<float>(), at::cuda::getCurrentCUDAStream().stream()));
+    return ck;
+}
+
+// Backward.  Returns [du, ddelta, dA, dB, dC, dD?, ddelta_bias?, dz?, dh_init?].
+std::vector<at::Tensor> scan_bwd(const at::Tensor& u, const at::Tensor& delta, const at::Tensor& A,
+                                 const at::Tensor& Bm, const at::Tensor& Cm, const std::optional<at::Tensor>& D,
+                                 const std::optional<at::Tensor>& z, const std::optional<at::Tensor>& delta_bias,
+                                 const std::optional<at::Tensor>& h_init, const std::optional<at::Tensor>& length,
+                                 bool padding_right, bool delta_softplus, const std::optional<at::Tensor>& y,
+                                 const at::Tensor& ckpt, const at::Tensor& dout,
+                                 const std::optional<at::Tensor>& dh_last) {
+    Common c = check_inputs(u, delta, A, Bm, Cm, D, z, delta_bias, h_init, length);
+    c10::cuda::CUDAGuard guard(u.device());
+    check_bdl(dout, "dout", c.B, c.D, c.L, u.scalar_type());
+    const int64_t k = ssm_scan_ckpt_len(c.N);
+    check_f32(ckpt, "ckpt", {c.B, ssm_scan_num_ckpt(c.L, k), c.D, c.N});
+    TORCH_CHECK(ckpt.is_contiguous(), "ckpt must be contiguous");
+    if (z) {
+        TORCH_CHECK(y.has_value(), "the pre-gate output y is needed when z is given");
+        check_bdl(*y, "y", c.B, c.D, c.L, u.scalar_type());
+    }
+    if (dh_last) {
+        check_f32(*dh_last, "dh_last", {c.B, c.D, c.N});
+        TORCH_CHECK(dh_last->is_contiguous(), "dh_last must be contiguous");
+    }
+    ssm_scan_bwd_args a;
+    memset(&a, 0, sizeof(a));
+    a.batch = c.B; a.dim = c.D; a.seqlen = c.L; a.dstate = c.N; a.dtype = c.dt;
+    a.delta_softplus = delta_softplus; a.padding_right = padding_right;
+    a.reference_length_semantics = 1;
+    a.u = u.data_ptr(); a.u_batch_stride = u.stride(0); a.u_dim_stride = u.stride(1);
+    a.delta = delta.data_ptr(); a.delta_batch_stride = delta.stride(0); a.delta_dim_stride = delta.stride(1);
+    a.A = A.data_ptr<float>(); a.A_dim_stride = A.stride(0);
+    a.B = Bm.data_ptr(); a.B_batch_stride = Bm.stride(0); a.B_state_stride = Bm.stride(1);
+    a.C = Cm.data_ptr(); a.C_batch_stride = Cm.stride(0); a.C_state_stride = Cm.stride(1);
+    a.D = ptr<const float>(D);
+    if (z) { a.z = z->data_ptr(); a.z_batch_stride = z->stride(0); a.z_dim_stride = z->stride(1); }
+    if (y) { a.y = y->data_ptr(); a.y_batch_stride = y->stride(0); a.y_dim_stride = y->stride(1); }
+    a.delta_bias = ptr<const float>(delta_bias);
+    a.h_init = ptr<const float>(h_init);
+    a.length = ptr<const int64_t>(length);
+    a.ckpt = ckpt.data_ptr<float>(); a.ckpt_format = SSM_CKPT_COMPACT; a.ckpt_len = k;
+    a.dout = dout.data_ptr(); a.dout_batch_stride = dout.stride(0); a.dout_dim_stride = dout.stride(1);
+    a.dh_last = ptr<const float>(dh_last);
+    at::Tensor du = at::empty({c.B, c.D, c.L}, u.options());
+    at::Tensor ddelta = at::empty({c.B, c.D, c.L}, u.options());
+    at::Tensor dA = at::empty({c.D, c.N}, A.options());
+    at::Tensor dB = at::empty({c.B, c.N, c.L}, u.options());
+    at::Tensor dC = at::empty({c.B, c.N, c.L}, u.options());
+    const auto f32 = u.options().dtype(at::kFloat);
+    at::Tensor dD = D ? at::empty({c.D}, f32) : at::Tensor();
+    at::Tensor dbias = delta_bias ? at::empty({c.D}, f32) : at::Tensor();
+    at::Tensor dz = z ? at::empty({c.B, c.D, c.L}, u.options()) : at::Tensor();
+    at::Tensor dh_init = h_init ? at::empty({c.B, c.D, c.N}, f32) : at::Tensor();
+    a.du = du.data_ptr(); a.du_batch_stride = du.stride(0); a.du_dim_stride = du.stride(1);
+    a.ddelta = ddelta.data_ptr(); a.ddelta_batch_stride = ddelta.stride(0); a.ddelta_dim_stride = ddelta.stride(1);
+    if (z) { a.dz = dz.data_ptr(); a.dz_batch_stride = dz.stride(0); a.dz_dim_stride = dz.stride(1); }
+    a.dA = dA.data_ptr<float>();
+    a.dB = dB.data_ptr(); a.dC = dC.data_ptr();
+    a.dD = D ? dD.data_ptr<float>() : nullptr;
+    a.ddelta_bias = delta_bias ? dbias.data_ptr<float>() : nullptr;
+    a.dh_init = h_init ? dh_init.data_ptr<float>() : nullptr;
+    const size_t ws_bytes = ssm_scan_bwd_workspace_size(&a);
+    TORCH_CHECK(ws_bytes > 0, ssm_last_error());
+    at::Tensor ws = at::empty({(int64_t)ws_bytes}, u.options().dtype(at::kByte));
+    ok(ssm_scan_bwd(&a, ws.data_ptr(), ws_bytes, at::cuda::getCurrentCUDAStream().stream()));
+    return {du, ddelta, dA, dB, dC, dD, dbias, dz, dh_init};
+}
+
+// One decode step; writes state_out (may be the same tensor as state) and returns out.
+at::Tensor state_update(const at::Tensor& state, const at::Tensor& state_out, const at::Tensor& x,
+                        const at::Tensor& dt, const at::Tensor& A, const at::Tensor& Bm, const at::Tensor& Cm,
+                        const std::optional<at::Tensor>& D, const std::optional<at::Tensor>& z,
+                        const std::optional<at::Tensor>& dt_bias, bool dt_softplus) {
+    check_cuda(state, "h");
+    TORCH_CHECK(state.dim() == 3, "h must be a 3D tensor");
+    const int64_t Bs = state.size(0), Dm = state.size(1), N = state.size(2);
+    TORCH_CHECK(N <= 256, "selective_update only supports state_dim <= 256");
+    TORCH_CHECK(state.scalar_type() == at::kFloat, "h must be float32 tensor");
+    TORCH_CHECK(state.stride(2) == 1, "h must be contiguous along the state dimension");
+    TORCH_CHECK(state_out.sizes() == state.sizes() && state_out.scalar_type() == at::kFloat &&
+                    state_out.stride(2) == 1 && state_out.is_cuda(),
+                "state_out must match h");
+    check_cuda(x, "u");
+    const int32_t dtc = dtype_code(x);
+    for (auto* t : {&x, &dt}) {
+        TORCH_CHECK(t->is_cuda() && t->dim() == 2 && t->size(0) == Bs && t->size(1) == Dm && t->stride(1) == 1,
+                    "u and delta must have shape (batch_size, num_channels)");
+        TORCH_CHECK(t->scalar_type() == x.scalar_type(), "u and delta must share a dtype");
+    }
+    TORCH_CHECK(A.is_cuda() && A.scalar_type() == at::kFloat && A.dim() == 2 && A.size(0) == Dm && A.size(1) == N &&
+                    A.stride(1) == 1,
+                "A must be float32 of shape (num_channels, state_dim)");
+    for (auto* t : {&Bm, &Cm}) {
+        TORCH_CHECK(t->is_cuda() && t->dim() == 2 && t->size(0) == Bs && t->size(1) == N && t->stride(1) == 1,
+                    "B and C must have shape (batch_size, state_dim)");
+        TORCH_CHECK(t->scalar_type() == x.scalar_type(), "B and C must have the dtype of u");
+    }
+    if (D) { check_f32(*D, "D", {Dm}); TORCH_CHECK(D->is_contiguous(), "D must be contiguous"); }
+    if (dt_bias) { check_f32(*dt_bias, "delta_bias", {Dm}); TORCH_CHECK(dt_bias->is_contiguous(), "delta_bias must be contiguous"); }
+    if (z) TORCH_CHECK(z->is_cuda() && z->sizes() == x.sizes() && z->stride(1) == 1 && z->scalar_type() == x.scalar_type(),
+                       "z must match x");
+    c10::cuda::CUDAGuard guard(state.device());
+    at::Tensor out = at::empty({Bs, Dm}, x.options());
+    ssm_state_update_args a;
+    memset(&a, 0, sizeof(a));
+    a.batch = Bs; a.dim = Dm; a.dstate = N; a.dtype = dtc; a.dt_softplus = dt_softplus;
+    a.state = state.data_ptr<float>(); a.state_batch_stride = state.stride(0); a.state_dim_stride = state.stride(1);
+    a.state_out = state_out.data_ptr<float>();
+    a.state_out_batch_stride = state_out.stride(0); a.state_out_dim_stride = state_out.stride(1);
+    a.x = x.data_ptr(); a.x_batch_stride = x.stride(0);
+    a.dt = dt.data_ptr(); a.dt_batch_stride = dt.stride(0);
+    a.A = A.data_ptr<float>(); a.A_dim_stride = A.stride(0);
+    a.B = Bm.data_ptr(); a.B_batch_stride = Bm.stride(0);
+    a.C = Cm.data_ptr(); a.C_batch_stride = Cm.stride(0);
+    a.D = ptr<const float>(D);
+    if (z) { a.z = z->data_ptr(); a.z_batch_stride = z->stride(0); }
+    a.dt_bias = ptr<const float>(dt_bias);
+    a.out = out.data_ptr(); a.out_batch_stride = out.stride(0);
+    ok(ssm_state_update(&a, at::cuda::getCurrentCUDAStream().stream()));
+    return out;
+}
+
+int64_t check_device_error() {
+    int code = 0;
+    ssm_check_device_error(&code, at::cuda::getCurrentCUDAStream().stream());
+    return code;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(_C, m) {
+    m.doc() = "torch binding of the ssm_b200 C ABI";
+    m.def("scan_fwd", &scan_fwd, "selective scan forward");
+    m.def("scan_bwd", &scan_bwd, "selective scan backward");
+    m.def("ckpt_from_reference", &ckpt_from_reference, "compact checkpoints from reference chunk states");
+    m.def("state_update", &state_update, "one decode step");
+    m.def("ckpt_len", [](int64_t n) { return ssm_scan_ckpt_len(n); });
+    m.def("version", []() { return std::string(ssm_version()); });
+    m.def("check_device_error", &check_device_error, "read and clear the device error word");
+}

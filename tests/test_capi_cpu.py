@@ -1,0 +1,81 @@
+"""CPU tests of the C-ABI library: it loads, exports every entry point the header
+declares, its argument structs match the header's layout, and host-side validation
+answers without touching a GPU."""
+import ctypes
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+from ssm_mamba_b200 import capi  # noqa: E402
+
+
+def test_library_exports_every_declared_symbol():
+    names = capi.declared_functions()
+    assert len(names) >= 10, names
+    lib = capi.lib()
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/ssm_b200.h but not exported"
+    out = subprocess.run(["nm", "-D", "--defined-only", capi.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert set(names) <= exported
+    # nothing but the C ABI leaks out of the library
+    assert all(e.startswith("ssm_") for e in exported), sorted(e for e in exported if not e.startswith("ssm_"))
+
+
+def test_struct_layout_matches_header(tmp_path):
+    """Compile a probe against the header and compare sizeof/offsetof with ctypes."""
+    src = tmp_path / "probe.c"
+    fields = {"ssm_scan_fwd_args": ("ScanFwdArgs", ["u", "B", "ckpt", "ckpt_len", "h_last"]),
+              "ssm_scan_bwd_args": ("ScanBwdArgs", ["y", "ckpt_len", "dout", "dz", "dh_init"]),
+              "ssm_state_update_args": ("StateUpdateArgs", ["state", "x", "z", "out"])}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "ssm_b200.h"', "int main(void){"]
+    for cs, (_, fl) in fields.items():
+        lines.append(f'printf("{cs} %zu\\n", sizeof({cs}));')
+        for f in fl:
+            lines.append(f'printf("{cs}.{f} %zu\\n", offsetof({cs}, {f}));')
+    lines.append("return 0;}")
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "probe"
+    subprocess.check_call(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)])
+    got = dict(line.split() for line in subprocess.check_output([str(exe)], text=True).splitlines())
+    for cs, (py, fl) in fields.items():
+        st = getattr(capi, py)
+        assert int(got[cs]) == ctypes.sizeof(st), cs
+        for f in fl:
+            assert int(got[f"{cs}.{f}"]) == getattr(st, f).offset, f"{cs}.{f}"
+
+
+def test_pure_host_entry_points():
+    lib = capi.lib()
+    assert b"sm_100a" in lib.ssm_version()
+    assert lib.ssm_scan_num_ckpt(2048, 8) == 256
+    assert lib.ssm_scan_num_ckpt(2049, 8) == 257
+    assert lib.ssm_scan_ckpt_len(16) == 8
+    assert lib.ssm_scan_ckpt_len(256) == 4
+
+
+def test_validation_errors_without_gpu():
+    lib = capi.lib()
+    assert lib.ssm_scan_fwd(None, None) == capi.SSM_ERR_INVALID
+    a = capi.ScanFwdArgs()
+    a.batch, a.dim, a.seqlen, a.dstate = 1, 1, 1, 300
+    assert lib.ssm_scan_fwd(ctypes.byref(a), None) == capi.SSM_ERR_INVALID
+    assert b"state_dim <= 256" in lib.ssm_last_error()
+    a.dstate = 0
+    assert lib.ssm_scan_fwd(ctypes.byref(a), None) == capi.SSM_ERR_INVALID
+    u = capi.StateUpdateArgs()
+    u.batch, u.dim, u.dstate, u.dtype = 1, 1, 16, 7
+    assert lib.ssm_state_update(ctypes.byref(u), None) == capi.SSM_ERR_INVALID
+    assert b"dtype" in lib.ssm_last_error()
+
+
+def test_torch_binding_imports():
+    import torch  # noqa: F401
+    from ssm_mamba_b200 import _ext
+    assert "sm_100a" in _ext._C.version()
+    assert _ext._C.ckpt_len(16) == 8
