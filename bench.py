@@ -193,12 +193,58 @@ def cpu_baseline_sample(target_s=10.0, batch=1, dim=96):
             (CFG2["batch"] * CFG2["dim"]) / (batch * dim)}
 
 
+def run_decode(args, world, rank, local, pg, peak):
+    """Config 3: 1024 decode steps in one CUDA graph, state rotated over 8 layer buffers
+    (168 MB > L2) so every step reads and writes its state in HBM."""
+    import torch
+    from ssm_mamba_b200 import selective_state_update
+    from ssm_mamba_b200.workloads import decode_inputs
+    dev = torch.device("cuda", local)
+    Bd, Dd, Nd, S, Ly = CFG3["batch"], CFG3["dim"], CFG3["dstate"], CFG3["steps"], CFG3["layers"]
+    dec = decode_inputs(Bd, Dd, Nd, S, torch.bfloat16, seed=2 + rank, device=dev)
+    states = [dec.state.clone() for _ in range(Ly)]
+
+    def loop():
+        for s in range(S):
+            selective_state_update(states[s % Ly], dec.x[s], dec.dt[s], dec.A, dec.B[s], dec.C[s], dec.D,
+                                   dec.z[s], dec.dt_bias, dt_softplus=True)
+
+    loop()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        loop()
+    for _ in range(2):
+        graph.replay()
+    barrier(pg)
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    d0.record()
+    for _ in range(reps):
+        graph.replay()
+    d1.record()
+    torch.cuda.synchronize()
+    barrier(pg)
+    dec_ms = max_over_ranks(d0.elapsed_time(d1), pg) / (reps * S)
+    step_bytes = 2 * Bd * Dd * Nd * 4 + 4 * Bd * Dd * 2 + Dd * Nd * 4 + 2 * Bd * Nd * 2 + 2 * Dd * 4
+    del graph
+    return {"metric": "decode tokens/s (one Mamba-2.8B-width layer)", "value": Bd * world / (dec_ms / 1e3),
+            "unit": "tokens/s", "us_per_step": dec_ms * 1e3, "gpu_launches_per_step": 1,
+            "roofline": {"bound": "hbm", "achieved": step_bytes / (dec_ms / 1e3) / 1e9, "peak": peak,
+                         "unit": "GB/s", "frac": step_bytes / (dec_ms / 1e3) / 1e9 / peak,
+                         "bytes_per_step": step_bytes},
+            "config": "batch 64, d_inner 5120, d_state 16 fp32 state, bf16 x/dt/z/B/C, 1024 steps in "
+                      "one CUDA graph, state rotated over 8 layer buffers"}
+
+
 def run_ours(args, world, rank, local, pg):
     import torch
     from ssm_mamba_b200._ext import _C
     from ssm_mamba_b200 import selective_scan_fn, selective_state_update
     from ssm_mamba_b200.workloads import scan_inputs
     dev = torch.device("cuda", local)
+    if args.decode_only:
+        return {"decode": run_decode(args, world, rank, local, pg, measured_peaks()[0])}
     B, D, L, N = CFG2["batch"], CFG2["dim"], CFG2["seqlen"], CFG2["dstate"]
     inp = scan_inputs(B, D, L, N, torch.bfloat16, seed=1 + rank, device=dev, with_z=True)
     fwd_bytes, bwd_bytes = scan_bytes(B, D, L, N)
@@ -242,7 +288,10 @@ def run_ours(args, world, rank, local, pg):
     peak, peak_kind = measured_peaks()
 
     # ---- end to end through the public API: pinned host inputs in, gradients out -------
+    e2e = None
     e2e_steps = min(args.steps, 10)
+    if args.no_e2e:
+        e2e_steps = 0
     f = lambda t: t.detach().to("cpu").pin_memory()  # noqa: E731
     host_in = {k: f(getattr(inp, k)) for k in ("u", "delta", "z", "B", "C", "dout")}
     A = inp.A.clone().requires_grad_()
@@ -260,62 +309,25 @@ def run_ours(args, world, rank, local, pg):
         for k in host_out:
             host_out[k].copy_(leaves[k].grad, non_blocking=True)
 
-    for _ in range(3):
-        e2e_step()
-    barrier(pg)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    barrier(pg)
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), pg)
-    h2d = sum(v.numel() * v.element_size() for v in host_in.values())
-    d2h = sum(v.numel() * v.element_size() for v in host_out.values())
-    e2e = {"value": (fwd_bytes + bwd_bytes) * e2e_steps * world / (e2e_ms / 1e3) / 1e12, "unit": "TB/s",
-           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / e2e_steps,
-           "api": "ssm_mamba_b200.selective_scan_fn forward + autograd backward"}
-
-    # ---- decode (config 3), state rotated over 8 layer buffers (168 MB > L2) -------------
-    decode = None
-    if not args.no_decode:
-        from ssm_mamba_b200.workloads import decode_inputs
-        Bd, Dd, Nd, S, Ly = CFG3["batch"], CFG3["dim"], CFG3["dstate"], CFG3["steps"], CFG3["layers"]
-        dec = decode_inputs(Bd, Dd, Nd, S, torch.bfloat16, seed=2 + rank, device=dev)
-        states = [dec.state.clone() for _ in range(Ly)]
-
-        def loop():
-            for s in range(S):
-                selective_state_update(states[s % Ly], dec.x[s], dec.dt[s], dec.A, dec.B[s], dec.C[s], dec.D,
-                                       dec.z[s], dec.dt_bias, dt_softplus=True)
-
-        loop()
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            loop()
-        for _ in range(2):
-            graph.replay()
+    if e2e_steps:
+        for _ in range(3):
+            e2e_step()
         barrier(pg)
-        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = 3
-        d0.record()
-        for _ in range(reps):
-            graph.replay()
-        d1.record()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record()
         torch.cuda.synchronize()
         barrier(pg)
-        dec_ms = max_over_ranks(d0.elapsed_time(d1), pg) / (reps * S)
-        step_bytes = 2 * Bd * Dd * Nd * 4 + 4 * Bd * Dd * 2 + Dd * Nd * 4 + 2 * Bd * Nd * 2 + 2 * Dd * 4
-        decode = {"metric": "decode tokens/s (one Mamba-2.8B-width layer)", "value": Bd * world / (dec_ms / 1e3),
-                  "unit": "tokens/s", "us_per_step": dec_ms * 1e3, "gpu_launches_per_step": 1,
-                  "roofline": {"bound": "hbm", "achieved": step_bytes / (dec_ms / 1e3) / 1e9, "peak": peak,
-                               "unit": "GB/s", "frac": step_bytes / (dec_ms / 1e3) / 1e9 / peak,
-                               "bytes_per_step": step_bytes},
-                  "config": "batch 64, d_inner 5120, d_state 16 fp32 state, bf16 x/dt/z/B/C, 1024 steps in "
-                            "one CUDA graph, state rotated over 8 layer buffers"}
-        del graph
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1), pg)
+        h2d = sum(v.numel() * v.element_size() for v in host_in.values())
+        d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+        e2e = {"value": (fwd_bytes + bwd_bytes) * e2e_steps * world / (e2e_ms / 1e3) / 1e12, "unit": "TB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / e2e_steps,
+               "api": "ssm_mamba_b200.selective_scan_fn forward + autograd backward"}
+
+    decode = None if args.no_decode else run_decode(args, world, rank, local, pg, peak)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -431,6 +443,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ref-cuda", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--decode-only", action="store_true", help="profiling aid: only the decode loop")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

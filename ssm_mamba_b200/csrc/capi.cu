@@ -225,8 +225,8 @@ static int fwd_impl(const ssm_scan_fwd_args* a, const float* restart, void* stre
     if (a->ckpt) {
         if (a->ckpt_format != SSM_CKPT_COMPACT && a->ckpt_format != SSM_CKPT_REFERENCE)
             return fail(SSM_ERR_INVALID, "ssm_scan_fwd: unknown checkpoint format");
-        if (a->ckpt_len < 4 || (a->ckpt_len % 4) != 0)
-            return fail(SSM_ERR_INVALID, "ssm_scan_fwd: ckpt_len must be a positive multiple of 4");
+        if (a->ckpt_len < 4 || (a->ckpt_len & (a->ckpt_len - 1)) != 0 || a->ckpt_len > (1 << 20))
+            return fail(SSM_ERR_INVALID, "ssm_scan_fwd: ckpt_len must be a power of two >= 4");
     }
     const int is_bf16 = a->dtype == SSM_BF16;
     const int64_t es = is_bf16 ? 2 : 4;
@@ -240,7 +240,9 @@ static int fwd_impl(const ssm_scan_fwd_args* a, const float* restart, void* stre
     memset(&p, 0, sizeof(p));
     p.batch = (int)a->batch; p.dim = (int)a->dim; p.seqlen = (int)a->seqlen; p.dstate = (int)a->dstate;
     p.delta_softplus = a->delta_softplus; p.padding_right = a->padding_right;
-    p.ckpt_format = a->ckpt_format; p.ckpt_len = (int)a->ckpt_len;
+    p.ckpt_format = a->ckpt_format;
+    p.ckpt_len = a->ckpt ? (int)a->ckpt_len : 4;
+    while ((1 << p.ckpt_shift) < p.ckpt_len) p.ckpt_shift++;
     p.nck = a->ckpt ? (int)ssm_scan_num_ckpt(a->seqlen, a->ckpt_len) : 0;
     p.u = a->u; p.u_sb = a->u_batch_stride; p.u_sd = a->u_dim_stride;
     p.delta = a->delta; p.delta_sb = a->delta_batch_stride; p.delta_sd = a->delta_dim_stride;
@@ -456,8 +458,8 @@ int ssm_state_update(const ssm_state_update_args* a, void* stream_) {
     if (!a->state || !a->state_out || !a->x || !a->dt || !a->A || !a->B || !a->C || !a->out)
         return fail(SSM_ERR_INVALID, "ssm_state_update: state, state_out, x, dt, A, B, C and out are required");
     const StateSplit sp = split_states(a->dstate);
-    const int64_t threads = a->batch * a->dim * sp.lpc;
-    if ((threads + 255) / 256 > 0x7fffffff) return fail(SSM_ERR_INVALID, "ssm_state_update: too many rows");
+    if (a->batch > 65535 || a->dim > (1 << 30))
+        return fail(SSM_ERR_INVALID, "ssm_state_update: batch must be <= 65535");
     UpdParams p;
     memset(&p, 0, sizeof(p));
     p.batch = (int)a->batch; p.dim = (int)a->dim; p.dstate = (int)a->dstate;

@@ -52,6 +52,59 @@ __device__ __forceinline__ float sigmoidf_fast(float x) {
     return __fdividef(1.f, 1.f + __expf(-x));
 }
 
+// log(1 + e^x) = max(x, 0) + log1p(t), t = e^-|x| in (0, 1], with log1p(t) = 2 atanh(s),
+// s = t / (2 + t) in (0, 1/3], from the series 2 atanh(s) = 2 s (1 + s^2/3 + s^4/5 + ...).
+// Truncated after s^12/13 the series error is below (1/3)^14/15 ~ 1.4e-8 relative; the
+// MUFU exp2 and the fast division add ~3e-7.  For x > 20 the correction rounds away and
+// the result is x, as in the reference's threshold.  `t_out` returns e^-|x| for reuse.
+__device__ __forceinline__ float softplus_series(float x, float* t_out = nullptr) {
+    const float t = ex2(-fabsf(x) * kLog2e);
+    const float s = __fdividef(t, 2.f + t);
+    const float s2 = s * s;
+    float p = 1.f / 13.f;
+    p = fmaf(p, s2, 1.f / 11.f);
+    p = fmaf(p, s2, 1.f / 9.f);
+    p = fmaf(p, s2, 1.f / 7.f);
+    p = fmaf(p, s2, 1.f / 5.f);
+    p = fmaf(p, s2, 1.f / 3.f);
+    p = fmaf(p, s2, 1.f);
+    if (t_out) *t_out = t;
+    return fmaxf(x, 0.f) + 2.f * s * p;
+}
+
+// logistic sigmoid from t = e^-|x| (as returned by softplus_series)
+__device__ __forceinline__ float sigmoid_from_t(float x, float t) {
+    const float r = __fdividef(1.f, 1.f + t);
+    return x >= 0.f ? r : t * r;
+}
+
+// four consecutive elements as float (from 8 or 16 bytes of shared memory)
+template <typename T> struct Vec4;
+template <> struct Vec4<float> {
+    static __device__ __forceinline__ void load(const void* p, float (&v)[4]) {
+        const float4 x = *reinterpret_cast<const float4*>(p);
+        v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    }
+    static __device__ __forceinline__ void store(void* p, const float (&v)[4]) {
+        *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+};
+template <> struct Vec4<__nv_bfloat16> {
+    static __device__ __forceinline__ void load(const void* p, float (&v)[4]) {
+        const uint2 x = *reinterpret_cast<const uint2*>(p);
+        v[0] = __uint_as_float(x.x << 16); v[1] = __uint_as_float(x.x & 0xffff0000u);
+        v[2] = __uint_as_float(x.y << 16); v[3] = __uint_as_float(x.y & 0xffff0000u);
+    }
+    static __device__ __forceinline__ void store(void* p, const float (&v)[4]) {
+        const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+        const __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+        uint2 x;
+        x.x = *reinterpret_cast<const uint32_t*>(&a);
+        x.y = *reinterpret_cast<const uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(p) = x;
+    }
+};
+
 // ---------------------------------------------------------------------------------------
 // 128-byte swizzle (CU_TENSOR_MAP_SWIZZLE_128B): inside each 1024-byte block of eight
 // 128-byte rows, 16-byte chunk j of row r sits at chunk position j ^ (r & 7).  Tiles whose

@@ -13,7 +13,7 @@ struct FwdParams {
     int use_tma;         // 1: TMA tensor-map path, 0: plain-load fallback
     int delta_softplus, padding_right;
     int ckpt_format;     // 0 compact, 1 reference
-    int ckpt_len, nck;
+    int ckpt_len, ckpt_shift, nck;   // ckpt_len = 1 << ckpt_shift
     const void* u; int64_t u_sb, u_sd;
     const void* delta; int64_t delta_sb, delta_sd;
     const float* A; int64_t A_sd;

@@ -30,6 +30,8 @@
 #include "scan_layout.h"
 #include "warp_reduce.cuh"
 
+#include <type_traits>
+
 namespace ssm {
 
 template <typename IT, int LPC, int SPT, int K>
@@ -51,7 +53,6 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
     constexpr int NSUB = TB / K;
     constexpr int RS = TB + 4;
     constexpr int V = 2 * K;                      // S1 and S2 per sub-tile token
-    constexpr int RR = LPC < V ? LPC : V;
     static_assert(TB % K == 0 && K % 4 == 0, "sub-tiles must be whole float4 groups");
 
     extern __shared__ __align__(1024) unsigned char smem[];
@@ -93,8 +94,9 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
     const int mlo = (ref && !p.padding_right) ? Lq - len : 0;         // masked: t < mlo
     const int mhi = (ref && p.padding_right) ? len : Lq;              //      or t >= mhi
 
-    // ---- per-thread constants ----------------------------------------------------------------
-    float A2[SPT], An[SPT], G[SPT], an[SPT], dAacc[SPT];
+    // ---- per-thread constants, packed in pairs of states ---------------------------------------
+    constexpr int NP = SPT / 2;
+    float2 A2[NP], An[NP], Gp[NP], anp[NP], dAp[NP];
     int nidx[SPT];
 #pragma unroll
     for (int s = 0; s < SPT; s++) {
@@ -102,16 +104,25 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
         nidx[s] = n;
         const bool ok = dvalid && n < N;
         const float a = ok ? p.A[(int64_t)d * p.A_sd + n] : 0.f;
-        An[s] = a;
-        A2[s] = a * kLog2e;
-        G[s] = (ok && p.dh_last) ? p.dh_last[((int64_t)b * p.dim + d) * N + n] : 0.f;
-        an[s] = 1.f;
-        dAacc[s] = 0.f;
+        const float gl = (ok && p.dh_last) ? p.dh_last[((int64_t)b * p.dim + d) * N + n] : 0.f;
+        if (s & 1) {
+            An[s / 2].y = a; A2[s / 2].y = a * kLog2e; Gp[s / 2].y = gl;
+        } else {
+            An[s / 2].x = a; A2[s / 2].x = a * kLog2e; Gp[s / 2].x = gl;
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < NP; q++) {
+        anp[q] = make_float2(1.f, 1.f);
+        dAp[q] = make_float2(0.f, 0.f);
     }
     const float Dd = (dvalid && p.D) ? p.D[d] : 0.f;
     float dD_acc = 0.f, db_acc = 0.f;
+    float* sBias = reinterpret_cast<float*>(smem + S.bias);
+    for (int i = tid; i < DT; i += nthr)
+        sBias[i] = (d0 + i < p.dim && p.delta_bias) ? p.delta_bias[d0 + i] : 0.f;
 
-    auto load_ckpt = [&](int ts, float (&hv)[SPT]) {
+    auto load_ckpt = [&](int ts, float2 (&hv)[NP]) {
 #pragma unroll
         for (int s = 0; s < SPT; s++) {
             const int n = nidx[s];
@@ -123,7 +134,7 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                     v = p.ckpt[(((int64_t)b * p.nck + (ts / K - 1)) * p.dim + d) * N + n];
                 }
             }
-            hv[s] = v;
+            if (s & 1) hv[s / 2].y = v; else hv[s / 2].x = v;
         }
     };
 
@@ -190,11 +201,8 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
     if (p.use_tma && tid == 0) issue(ntiles - 1);
 
     // checkpoint of the first sub-tile processed, then prefetched one sub-tile ahead
-    float h0[SPT], h0n[SPT];
-    {
-        const int last_ts = ((Lq - 1) / K) * K;
-        load_ckpt(last_ts, h0);
-    }
+    float2 h0[NP], h0n[NP];
+    load_ckpt(((Lq - 1) / K) * K, h0);
 
     for (int it = ntiles - 1; it >= 0; it--) {
         const int t0 = it * TB;
@@ -210,35 +218,52 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
             return;
         }
 
-        // ---- prologue ------------------------------------------------------------------------
-        for (int i = tid; i < DT * TB; i += nthr) {
-            const int cc = i / TB, tt = i % TB, tg = t0 + tt;
-            const uint32_t off = (uint32_t)(cc * TB + tt) * ES;
-            const bool ld = tg < Lload;
-            const float uv = ld ? to_f(*reinterpret_cast<const IT*>(smem + S.u + off)) : 0.f;
-            const float dr = ld ? to_f(*reinterpret_cast<const IT*>(smem + S.delta + off)) : 0.f;
-            float dv = ld ? to_f(*reinterpret_cast<const IT*>(smem + S.dout + off)) : 0.f;
-            const float x = dr + ((d0 + cc < p.dim && p.delta_bias) ? p.delta_bias[d0 + cc] : 0.f);
-            float dl = x, spg = 1.f;
-            if (p.delta_softplus && x <= 20.f) {
-                const float e = __expf(x);
-                dl = log1pf(e);
-                spg = __fdividef(e, 1.f + e);
+        // ---- prologue: 4 tokens of one channel per work item ------------------------------
+        const bool tile_short = t0 + TB > Lload;
+        for (int i = tid; i < DT * (TB / 4); i += nthr) {
+            const int cc = i / (TB / 4), t4 = (i % (TB / 4)) * 4;
+            const uint32_t off = (uint32_t)(cc * TB + t4) * ES;
+            float uv[4], dr[4], dv[4];
+            Vec4<IT>::load(smem + S.u + off, uv);
+            Vec4<IT>::load(smem + S.delta + off, dr);
+            Vec4<IT>::load(smem + S.dout + off, dv);
+            if (tile_short) {
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    if (t0 + t4 + j >= Lload) { uv[j] = 0.f; dr[j] = 0.f; dv[j] = 0.f; }
+            }
+            const float bias = sBias[cc];
+            float dl[4], du[4], spg[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float x = dr[j] + bias;
+                if (p.delta_softplus) {
+                    float t;
+                    dl[j] = softplus_series(x, &t);
+                    spg[j] = sigmoid_from_t(x, t);
+                } else {
+                    dl[j] = x;
+                    spg[j] = 1.f;
+                }
+                du[j] = dl[j] * uv[j];
             }
             if (has_z) {
-                const float zv = to_f(*reinterpret_cast<const IT*>(smem + S.z + off));
-                const float yv = to_f(*reinterpret_cast<const IT*>(smem + S.y + off));
-                const float sg = sigmoidf_fast(zv);
-                const float dzv = dv * yv * sg * (1.f + zv * (1.f - sg));
-                dv = dv * zv * sg;
-                *reinterpret_cast<IT*>(smem + S.dz + out_off(cc, tt)) =
-                    from_f<IT>(tg < Rskip ? dzv : 0.f);
+                float zv[4], yv[4], dz[4];
+                Vec4<IT>::load(smem + S.z + off, zv);
+                Vec4<IT>::load(smem + S.y + off, yv);
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const float sg = sigmoidf_fast(zv[j]);
+                    dz[j] = t0 + t4 + j < Rskip ? dv[j] * yv[j] * sg * (1.f + zv[j] * (1.f - sg)) : 0.f;
+                    dv[j] = dv[j] * zv[j] * sg;
+                }
+                Vec4<IT>::store(smem + S.dz + out_off(cc, t4), dz);
             }
-            sD[cc * RS + tt] = dl;
-            sDU[cc * RS + tt] = dl * uv;
-            sG[cc * RS + tt] = dv;
-            sSP[cc * RS + tt] = spg;
-            sU[cc * RS + tt] = uv;
+            *reinterpret_cast<float4*>(sD + cc * RS + t4) = make_float4(dl[0], dl[1], dl[2], dl[3]);
+            *reinterpret_cast<float4*>(sDU + cc * RS + t4) = make_float4(du[0], du[1], du[2], du[3]);
+            *reinterpret_cast<float4*>(sG + cc * RS + t4) = make_float4(dv[0], dv[1], dv[2], dv[3]);
+            *reinterpret_cast<float4*>(sSP + cc * RS + t4) = make_float4(spg[0], spg[1], spg[2], spg[3]);
+            *reinterpret_cast<float4*>(sU + cc * RS + t4) = make_float4(uv[0], uv[1], uv[2], uv[3]);
         }
         for (int i = tid; i < Q * TB; i += nthr) {
             const int q = i / TB, tt = i % TB, tg = t0 + tt;
@@ -267,6 +292,8 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
         unsigned char* odu = smem + S.du;
         unsigned char* odd = smem + S.ddelta;
         float* wslot = slots + warp * S.slot_stride;
+        const float* sBr = sB + rot * (int)S.rot_stride;
+        const float* sCr = sC + rot * (int)S.rot_stride;
 #pragma unroll 1
         for (int sub = NSUB - 1; sub >= 0; sub--) {
             const int tl0 = sub * K;
@@ -274,9 +301,10 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
             if (ts >= Lq) continue;  // past the end of the sequence: nothing to do
             // prefetch the checkpoint of the next sub-tile (one step earlier in time)
             if (ts > 0) load_ckpt(ts - K, h0n);
+            const bool skipped = ts >= Rskip;
 
             float v[V];
-            if (ts >= Rskip) {
+            if (skipped) {
                 // reference: a 128-token chunk that starts at or after len is skipped
 #pragma unroll
                 for (int j = 0; j < V; j++) v[j] = 0.f;
@@ -303,133 +331,150 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                 }
             } else {
                 const bool general = (ts + K > Lq) || (ref && !(ts + K <= len && ts >= mlo && ts + K <= mhi));
-                float av[K][SPT], hv[K][SPT];
-                // recompute the K states from the checkpoint
+                auto body = [&](auto gen_tag) {
+                    constexpr bool GEN = decltype(gen_tag)::value;
+                    float2 av[K][NP], hv[K][NP];
+                    // recompute the K states from the checkpoint
 #pragma unroll
-                for (int k4 = 0; k4 < K; k4 += 4) {
-                    const float4 dl4 = lds128(sD + c * RS + tl0 + k4);
-                    const float4 du4 = lds128(sDU + c * RS + tl0 + k4);
-                    const float dls[4] = {dl4.x, dl4.y, dl4.z, dl4.w};
-                    const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
+                    for (int k4 = 0; k4 < K; k4 += 4) {
+                        const float4 dl4 = lds128(sD + c * RS + tl0 + k4);
+                        const float4 du4 = lds128(sDU + c * RS + tl0 + k4);
+                        const float dls[4] = {dl4.x, dl4.y, dl4.z, dl4.w};
+                        const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const int k = k4 + j, t = tl0 + k;
-                        float Bv[SPT];
+                        for (int j = 0; j < 4; j++) {
+                            const int k = k4 + j, t = tl0 + k;
+                            bool msk = false;
+                            if (GEN) {
+                                const int tg = ts + k;
+                                msk = tg >= Lq || tg < mlo || tg >= mhi;
+                            }
+                            const float2 dl2 = make_float2(dls[j], dls[j]);
+                            const float2 du2 = make_float2(dus[j], dus[j]);
 #pragma unroll
-                        for (int s4 = 0; s4 < SPT / 4; s4++) {
-                            const int qq = g * (SPT / 4) + s4;
-                            const float4 b4 = lds128(sB + rot * (int)S.rot_stride + t * NS + ((qq ^ (t & QM)) << 2));
-                            Bv[s4 * 4 + 0] = b4.x; Bv[s4 * 4 + 1] = b4.y;
-                            Bv[s4 * 4 + 2] = b4.z; Bv[s4 * 4 + 3] = b4.w;
-                        }
-                        bool msk = false;
-                        if (general) {
-                            const int tg = ts + k;
-                            msk = tg >= Lq || tg < mlo || tg >= mhi;
-                        }
+                            for (int s4 = 0; s4 < SPT / 4; s4++) {
+                                const int qq = g * (SPT / 4) + s4;
+                                const float4 b4 = lds128(sBr + t * NS + ((qq ^ (t & QM)) << 2));
+                                const float2 bp[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
 #pragma unroll
-                        for (int s = 0; s < SPT; s++) {
-                            const float prev = k == 0 ? h0[s] : hv[k - 1][s];
-                            float a = ex2(dls[j] * A2[s]);
-                            float bb = dus[j] * Bv[s];
-                            if (msk) { a = 1.f; bb = 0.f; }
-                            av[k][s] = a;
-                            hv[k][s] = fmaf(a, prev, bb);
+                                for (int e = 0; e < 2; e++) {
+                                    const int pi = s4 * 2 + e;
+                                    const float2 prev = k == 0 ? h0[pi] : hv[k - 1][pi];
+                                    const float2 x = __fmul2_rn(dl2, A2[pi]);
+                                    float2 a = make_float2(ex2(x.x), ex2(x.y));
+                                    float2 bb = __fmul2_rn(du2, bp[e]);
+                                    if (GEN && msk) {
+                                        a = make_float2(1.f, 1.f);
+                                        bb = make_float2(0.f, 0.f);
+                                    }
+                                    av[k][pi] = a;
+                                    hv[k][pi] = __ffma2_rn(a, prev, bb);
+                                }
+                            }
                         }
                     }
-                }
-                // reverse recurrence and gradient terms
+                    // reverse recurrence and gradient terms
 #pragma unroll
-                for (int k4 = K - 4; k4 >= 0; k4 -= 4) {
-                    const float4 dl4 = lds128(sD + c * RS + tl0 + k4);
-                    const float4 du4 = lds128(sDU + c * RS + tl0 + k4);
-                    const float4 dg4 = lds128(sG + c * RS + tl0 + k4);
-                    const float dls[4] = {dl4.x, dl4.y, dl4.z, dl4.w};
-                    const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
-                    const float dgs[4] = {dg4.x, dg4.y, dg4.z, dg4.w};
+                    for (int k4 = K - 4; k4 >= 0; k4 -= 4) {
+                        const float4 dl4 = lds128(sD + c * RS + tl0 + k4);
+                        const float4 du4 = lds128(sDU + c * RS + tl0 + k4);
+                        const float4 dg4 = lds128(sG + c * RS + tl0 + k4);
+                        const float dls[4] = {dl4.x, dl4.y, dl4.z, dl4.w};
+                        const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
+                        const float dgs[4] = {dg4.x, dg4.y, dg4.z, dg4.w};
 #pragma unroll
-                    for (int j = 3; j >= 0; j--) {
-                        const int k = k4 + j, t = tl0 + k;
-                        float Bv[SPT], Cv[SPT];
-#pragma unroll
-                        for (int s4 = 0; s4 < SPT / 4; s4++) {
-                            const int qq = g * (SPT / 4) + s4;
-                            const int pos = rot * (int)S.rot_stride + t * NS + ((qq ^ (t & QM)) << 2);
-                            const float4 b4 = lds128(sB + pos);
-                            const float4 c4 = lds128(sC + pos);
-                            Bv[s4 * 4 + 0] = b4.x; Bv[s4 * 4 + 1] = b4.y;
-                            Bv[s4 * 4 + 2] = b4.z; Bv[s4 * 4 + 3] = b4.w;
-                            Cv[s4 * 4 + 0] = c4.x; Cv[s4 * 4 + 1] = c4.y;
-                            Cv[s4 * 4 + 2] = c4.z; Cv[s4 * 4 + 3] = c4.w;
-                        }
-                        bool msk = false, vld = true;
-                        if (general) {
-                            const int tg = ts + k;
-                            msk = tg >= Lq || tg < mlo || tg >= mhi;
-                            vld = tg < len;
-                        }
-                        const float dl = dls[j], du = dus[j], dg = dgs[j];
-                        const float dlv = vld ? dl : 0.f;
-                        float s1 = 0.f, s2 = 0.f;
-                        float dBv[SPT], dCv[SPT];
-#pragma unroll
-                        for (int s = 0; s < SPT; s++) {
-                            const float inj = msk ? 0.f : dg * Cv[s];
-                            const float Gs = fmaf(an[s], G[s], inj);
-                            G[s] = Gs;
-                            an[s] = av[k][s];
-                            const float qv = fmaf(-du, Bv[s], hv[k][s]);
-                            s1 = fmaf(Gs, Bv[s], s1);
-                            const float w = Gs * qv;
-                            s2 = fmaf(An[s], w, s2);
-                            dAacc[s] = fmaf(dlv, w, dAacc[s]);
-                            dBv[s] = vld ? Gs * du : 0.f;
-                            dCv[s] = vld ? dg * hv[k][s] : 0.f;
-                        }
-                        v[k] = s1;
-                        v[K + k] = vld ? s2 : 0.f;
-                        // dB, dC: sum over the channels of this warp
-                        if (ROT) {
-                            float rb = dBv[0], rc = dCv[0];
-#pragma unroll
-                            for (int i = 1; i < 4; i++) {
-                                rb += __shfl_xor_sync(0xffffffffu, dBv[i], LPC * i);
-                                rc += __shfl_xor_sync(0xffffffffu, dCv[i], LPC * i);
+                        for (int j = 3; j >= 0; j--) {
+                            const int k = k4 + j, t = tl0 + k;
+                            bool msk = false, vld = true;
+                            if (GEN) {
+                                const int tg = ts + k;
+                                msk = tg >= Lq || tg < mlo || tg >= mhi;
+                                vld = tg < len;
                             }
+                            const float2 dg2 = make_float2(dgs[j], dgs[j]);
+                            const float2 du2 = make_float2(dus[j], dus[j]);
+                            const float2 ndu2 = make_float2(-dus[j], -dus[j]);
+                            const float dlv = (GEN && !vld) ? 0.f : dls[j];
+                            const float2 dl2 = make_float2(dlv, dlv);
+                            float2 s12 = make_float2(0.f, 0.f), s22 = make_float2(0.f, 0.f);
+                            float dBv[SPT], dCv[SPT];
 #pragma unroll
-                            for (int m = 4; m < CPW; m *= 2) {
-                                rb += __shfl_xor_sync(0xffffffffu, rb, LPC * m);
-                                rc += __shfl_xor_sync(0xffffffffu, rc, LPC * m);
-                            }
-                            if (cw < 4) {
-                                const int n = g * 4 + cw;
-                                if (n < N) {
-                                    wslot[n * (TB + 1) + t] = rb;
-                                    wslot[(NS + n) * (TB + 1) + t] = rc;
+                            for (int s4 = 0; s4 < SPT / 4; s4++) {
+                                const int qq = g * (SPT / 4) + s4;
+                                const int pos = t * NS + ((qq ^ (t & QM)) << 2);
+                                const float4 b4 = lds128(sBr + pos);
+                                const float4 c4 = lds128(sCr + pos);
+                                const float2 bp[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
+                                const float2 cp[2] = {make_float2(c4.x, c4.y), make_float2(c4.z, c4.w)};
+#pragma unroll
+                                for (int e = 0; e < 2; e++) {
+                                    const int pi = s4 * 2 + e;
+                                    float2 inj = __fmul2_rn(dg2, cp[e]);
+                                    if (GEN && msk) inj = make_float2(0.f, 0.f);
+                                    const float2 Gs = __ffma2_rn(anp[pi], Gp[pi], inj);
+                                    Gp[pi] = Gs;
+                                    anp[pi] = av[k][pi];
+                                    const float2 qv = __ffma2_rn(ndu2, bp[e], hv[k][pi]);
+                                    s12 = __ffma2_rn(Gs, bp[e], s12);
+                                    const float2 w = __fmul2_rn(Gs, qv);
+                                    s22 = __ffma2_rn(An[pi], w, s22);
+                                    dAp[pi] = __ffma2_rn(dl2, w, dAp[pi]);
+                                    float2 db = __fmul2_rn(Gs, du2);
+                                    float2 dc = __fmul2_rn(dg2, hv[k][pi]);
+                                    if (GEN && !vld) {
+                                        db = make_float2(0.f, 0.f);
+                                        dc = make_float2(0.f, 0.f);
+                                    }
+                                    dBv[pi * 2] = db.x; dBv[pi * 2 + 1] = db.y;
+                                    dCv[pi * 2] = dc.x; dCv[pi * 2 + 1] = dc.y;
                                 }
                             }
-                        } else {
+                            v[k] = s12.x + s12.y;
+                            v[K + k] = (GEN && !vld) ? 0.f : s22.x + s22.y;
+                            // dB, dC: sum over the channels of this warp
+                            if (ROT) {
+                                float rb = dBv[0], rc = dCv[0];
 #pragma unroll
-                            for (int m = 1; m < CPW; m *= 2) {
-#pragma unroll
-                                for (int s = 0; s < SPT; s++) {
-                                    dBv[s] += __shfl_xor_sync(0xffffffffu, dBv[s], LPC * m);
-                                    dCv[s] += __shfl_xor_sync(0xffffffffu, dCv[s], LPC * m);
+                                for (int i = 1; i < 4; i++) {
+                                    rb += __shfl_xor_sync(0xffffffffu, dBv[i], LPC * i);
+                                    rc += __shfl_xor_sync(0xffffffffu, dCv[i], LPC * i);
                                 }
-                            }
-                            if (cw == 0) {
 #pragma unroll
-                                for (int s = 0; s < SPT; s++) {
-                                    const int n = nidx[s];
+                                for (int m = 4; m < CPW; m *= 2) {
+                                    rb += __shfl_xor_sync(0xffffffffu, rb, LPC * m);
+                                    rc += __shfl_xor_sync(0xffffffffu, rc, LPC * m);
+                                }
+                                if (cw < 4) {
+                                    const int n = g * 4 + cw;
                                     if (n < N) {
-                                        wslot[n * (TB + 1) + t] = dBv[s];
-                                        wslot[(NS + n) * (TB + 1) + t] = dCv[s];
+                                        wslot[n * (TB + 1) + t] = rb;
+                                        wslot[(NS + n) * (TB + 1) + t] = rc;
+                                    }
+                                }
+                            } else {
+#pragma unroll
+                                for (int m = 1; m < CPW; m *= 2) {
+#pragma unroll
+                                    for (int s = 0; s < SPT; s++) {
+                                        dBv[s] += __shfl_xor_sync(0xffffffffu, dBv[s], LPC * m);
+                                        dCv[s] += __shfl_xor_sync(0xffffffffu, dCv[s], LPC * m);
+                                    }
+                                }
+                                if (cw == 0) {
+#pragma unroll
+                                    for (int s = 0; s < SPT; s++) {
+                                        const int n = nidx[s];
+                                        if (n < N) {
+                                            wslot[n * (TB + 1) + t] = dBv[s];
+                                            wslot[(NS + n) * (TB + 1) + t] = dCv[s];
+                                        }
                                     }
                                 }
                             }
                         }
                     }
-                }
+                };
+                if (general) body(std::true_type{}); else body(std::false_type{});
             }
             // gradient of the initial state: decay of token 0 times dh_0 (dh_last when the
             // whole row was skipped)
@@ -437,13 +482,12 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
 #pragma unroll
                 for (int s = 0; s < SPT; s++) {
                     const int n = nidx[s];
-                    if (n < N) p.dh_init[((int64_t)b * p.dim + d) * N + n] = an[s] * G[s];
+                    const float val = (s & 1) ? anp[s / 2].y * Gp[s / 2].y : anp[s / 2].x * Gp[s / 2].x;
+                    if (n < N) p.dh_init[((int64_t)b * p.dim + d) * N + n] = val;
                 }
             }
 
             // ---- per-token sums over states, then finish the tokens this lane owns ---------
-            reduce_scatter<LPC, V>(v, g);
-            const bool skipped = ts >= Rskip;
             auto finish = [&](int k, float s1, float s2) {
                 const int t = tl0 + k, tg = ts + k;
                 float du = 0.f, ddl = 0.f;
@@ -457,16 +501,25 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                 *reinterpret_cast<IT*>(odu + out_off(c, t)) = from_f<IT>(du);
                 *reinterpret_cast<IT*>(odd + out_off(c, t)) = from_f<IT>(ddl);
             };
-            if (LPC <= K) {
+            if constexpr (LPC <= K) {
+                // S1 of token k sits at index k, S2 at K + k; lane g keeps K/LPC consecutive
+                // tokens of each
+                constexpr int RK = K / LPC;
+                float s1v[K], s2v[K];
 #pragma unroll
-                for (int r = 0; r < K / LPC; r++) finish(g + LPC * r, v[LPC * r], v[K + LPC * r]);
+                for (int k = 0; k < K; k++) { s1v[k] = v[k]; s2v[k] = v[K + k]; }
+                reduce_scatter_contig<LPC, K>(s1v, g);
+                reduce_scatter_contig<LPC, K>(s2v, g);
+#pragma unroll
+                for (int r = 0; r < RK; r++) finish(g * RK + r, s1v[r], s2v[r]);
             } else {
+                reduce_scatter<LPC, V>(v, g);
                 const float other = __shfl_xor_sync(0xffffffffu, v[0], K);
                 if (g < K) finish(g, v[0], other);
             }
             if (ts > 0) {
 #pragma unroll
-                for (int s = 0; s < SPT; s++) h0[s] = h0n[s];
+                for (int q = 0; q < NP; q++) h0[q] = h0n[q];
             }
         }
         __syncthreads();
@@ -510,7 +563,8 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
 #pragma unroll
     for (int s = 0; s < SPT; s++) {
         const int n = nidx[s];
-        if (dvalid && n < N) p.ws_a[((int64_t)b * p.dim + d) * N + n] = dAacc[s];
+        const float val = (s & 1) ? dAp[s / 2].y : dAp[s / 2].x;
+        if (dvalid && n < N) p.ws_a[((int64_t)b * p.dim + d) * N + n] = val;
     }
     dD_acc = allreduce<LPC>(dD_acc);
     db_acc = allreduce<LPC>(db_acc);

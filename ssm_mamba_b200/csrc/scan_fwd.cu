@@ -38,10 +38,13 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     constexpr int ES = sizeof(IT);
     constexpr int T = 128 / ES;              // tokens per tile
     constexpr int NS = LPC * SPT;            // padded state count
-    constexpr int G = LPC > 4 ? LPC : 4;     // tokens per reduce group
+    constexpr int NP = SPT / 2;              // state pairs per thread (packed f32x2 math)
+    constexpr int G = LPC > 16 ? LPC : 16;   // tokens per group (one reduce-scatter each)
+    constexpr int RL = G / LPC;              // consecutive tokens a lane finishes per group
     constexpr int Q = NS / 4;                // float4 groups per B/C row
     constexpr int QM = (Q < 8 ? Q : 8) - 1;  // swizzle mask for the f32 B/C rows
-    static_assert(T % G == 0, "tile must hold whole reduce groups");
+    constexpr int RS = T + 4;                // padded row of sD / sDU (floats)
+    static_assert(T % G == 0 && SPT % 4 == 0, "tile must hold whole groups");
 
     extern __shared__ __align__(1024) unsigned char smem[];
     if ((smem_u32(smem) & 1023u) != 0u) {  // the swizzled TMA tiles need a 1024-byte base
@@ -55,7 +58,7 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     float* sDU = reinterpret_cast<float*>(smem + L.sDU);
     float* sB = reinterpret_cast<float*>(smem + L.sB);
     float* sC = reinterpret_cast<float*>(smem + L.sC);
-    constexpr int RS = T + 4;                // padded row of sD / sDU (floats)
+    float* sBias = reinterpret_cast<float*>(smem + L.bias);
 
     const int tid = threadIdx.x;
     const int nthr = DT * LPC;
@@ -69,6 +72,7 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     const bool has_z = p.z != nullptr;
     const bool want_y = p.y != nullptr;
     const bool want_prod = p.ckpt != nullptr && p.ckpt_format == 1;
+    const int ck_mask = p.ckpt_len - 1;     // checkpoint interval is a power of two
 
     int len = Lq;
     if (p.length) {
@@ -81,18 +85,24 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     // rechunk mode loads as the reference backward does: zero-filled from len on when
     // seqlen % 128 != 0 (backward_kernel.cu:242-246)
     const int Lload = (rechunk && has_len && (Lq % 128) != 0) ? len : Lq;
+    // tokens outside [mlo, mhi) are padding: identity steps
+    const int mlo = (has_len && !p.padding_right) ? Lq - len : 0;
+    const int mhi = (has_len && p.padding_right) ? len : Lq;
 
-    // per-thread constants and state
-    float A2[SPT], h[SPT];
+    // per-thread constants and state, packed in pairs of states
+    float2 A2[NP], h[NP];
 #pragma unroll
     for (int s = 0; s < SPT; s++) {
         const int n = g * SPT + s;
         const bool ok = dvalid && n < N;
-        A2[s] = ok ? p.A[(int64_t)d * p.A_sd + n] * kLog2e : 0.f;
-        h[s] = (ok && p.h_init) ? p.h_init[((int64_t)b * p.dim + d) * N + n] : 0.f;
+        const float a = ok ? p.A[(int64_t)d * p.A_sd + n] * kLog2e : 0.f;
+        const float h0 = (ok && p.h_init) ? p.h_init[((int64_t)b * p.dim + d) * N + n] : 0.f;
+        if (s & 1) { A2[s / 2].y = a; h[s / 2].y = h0; } else { A2[s / 2].x = a; h[s / 2].x = h0; }
     }
     const float Dd = (dvalid && p.D) ? p.D[d] : 0.f;
     float Ssum = 0.f;  // running sum of effective delta (for the reference checkpoint product)
+    for (int i = tid; i < DT; i += nthr)
+        sBias[i] = (d0 + i < p.dim && p.delta_bias) ? p.delta_bias[d0 + i] : 0.f;
 
     const uint32_t tile_bytes = (uint32_t)DT * 128u;
     const uint32_t bc_bytes = (uint32_t)N * 128u;
@@ -136,14 +146,22 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
         }
     };
 
+    auto hval = [&](int s) -> float { return (s & 1) ? h[s / 2].y : h[s / 2].x; };
+    auto aval = [&](int s) -> float { return (s & 1) ? A2[s / 2].y : A2[s / 2].x; };
+
     auto write_ckpt = [&](int k) {
         if (!dvalid) return;
         if (p.ckpt_format == 0) {
-            float* dst = p.ckpt + (((int64_t)b * p.nck + k) * p.dim + d) * N;
+            float* dst = p.ckpt + (((int64_t)b * p.nck + k) * p.dim + d) * N + g * SPT;
+            if (g * SPT + SPT <= N && (N & 3) == 0) {
 #pragma unroll
-            for (int s = 0; s < SPT; s++) {
-                const int n = g * SPT + s;
-                if (n < N) dst[n] = h[s];
+                for (int s4 = 0; s4 < SPT; s4 += 4)
+                    *reinterpret_cast<float4*>(dst + s4) =
+                        make_float4(h[s4 / 2].x, h[s4 / 2].y, h[s4 / 2 + 1].x, h[s4 / 2 + 1].y);
+            } else {
+#pragma unroll
+                for (int s = 0; s < SPT; s++)
+                    if (g * SPT + s < N) dst[s] = hval(s);
             }
         } else {
             float* dst = p.ckpt + (((int64_t)b * p.dim + d) * p.nck + k) * 2 * N;
@@ -151,8 +169,8 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
             for (int s = 0; s < SPT; s++) {
                 const int n = g * SPT + s;
                 if (n < N) {
-                    dst[2 * n] = ex2(A2[s] * Ssum);
-                    dst[2 * n + 1] = h[s];
+                    dst[2 * n] = ex2(aval(s) * Ssum);
+                    dst[2 * n + 1] = hval(s);
                 }
             }
         }
@@ -187,21 +205,32 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
             return;
         }
 
-        // ---- prologue: per (channel, token) values, B/C to f32 rows --------------------
+        // ---- prologue: 4 tokens of one channel per work item ------------------------------
         const unsigned char* su = smem + L.u[st];
         const unsigned char* sdl = smem + L.delta[st];
-        for (int i = tid; i < DT * T; i += nthr) {
-            const int cc = i / T, tt = i % T, tg = t0 + tt;
-            const uint32_t off = swz128(cc, tt * ES);
-            const bool ld = tg < Lload;
-            const float x = (ld ? to_f(*reinterpret_cast<const IT*>(sdl + off)) : 0.f) +
-                            ((d0 + cc < p.dim && p.delta_bias) ? p.delta_bias[d0 + cc] : 0.f);
-            const float dl = p.delta_softplus ? softplus20(x) : x;
-            const float uv = ld ? to_f(*reinterpret_cast<const IT*>(su + off)) : 0.f;
-            bool masked = tg >= Lq;
-            if (has_len) masked |= p.padding_right ? (tg >= len) : (tg < Lq - len);
-            sD[cc * RS + tt] = masked ? 0.f : dl;
-            sDU[cc * RS + tt] = masked ? 0.f : dl * uv;
+        const bool tile_masked = (t0 + T > Lload) || (t0 < mlo) || (t0 + T > mhi);
+        for (int i = tid; i < DT * (T / 4); i += nthr) {
+            const int cc = i / (T / 4), t4 = (i % (T / 4)) * 4;
+            const uint32_t off = swz128(cc, t4 * ES);
+            float dr[4], uv[4], dl[4], du[4];
+            Vec4<IT>::load(sdl + off, dr);
+            Vec4<IT>::load(su + off, uv);
+            const float bias = sBias[cc];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                float x = dr[j];
+                float u = uv[j];
+                if (tile_masked && t0 + t4 + j >= Lload) { x = 0.f; u = 0.f; }
+                x += bias;
+                dl[j] = p.delta_softplus ? softplus_series(x) : x;
+                du[j] = dl[j] * u;
+                if (tile_masked) {
+                    const int tg = t0 + t4 + j;
+                    if (tg >= Lq || tg < mlo || tg >= mhi) { dl[j] = 0.f; du[j] = 0.f; }
+                }
+            }
+            *reinterpret_cast<float4*>(sD + cc * RS + t4) = make_float4(dl[0], dl[1], dl[2], dl[3]);
+            *reinterpret_cast<float4*>(sDU + cc * RS + t4) = make_float4(du[0], du[1], du[2], du[3]);
         }
         const unsigned char* sBr = smem + L.B[st];
         const unsigned char* sCr = smem + L.C[st];
@@ -224,7 +253,7 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
         if (p.use_tma && tid == 0) tma_store_wait_read_all();
         __syncthreads();
 
-        // ---- scan ------------------------------------------------------------------------
+        // ---- scan: groups of G tokens, then one reduce-scatter and the epilogue ----------
         const unsigned char* sz = smem + L.z[st];
         unsigned char* so = smem + L.out;
         unsigned char* sy = smem + L.y;
@@ -240,61 +269,83 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
                 const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
+                    // q0 is a multiple of 16, so the swizzle term is a compile-time constant
                     const int t = tl + j;
-                    float Bv[SPT], Cv[SPT];
+                    const int sw = (sb + j) & QM;
+                    const float2 dl2 = make_float2(dls[j], dls[j]);
+                    const float2 du2 = make_float2(dus[j], dus[j]);
+                    float2 y2 = make_float2(0.f, 0.f);
 #pragma unroll
                     for (int s4 = 0; s4 < SPT / 4; s4++) {
                         const int qq = g * (SPT / 4) + s4;
-                        const int pos = t * NS + ((qq ^ (t & QM)) << 2);
+                        const int pos = t * NS + ((qq ^ sw) << 2);
                         const float4 b4 = lds128(sB + pos);
                         const float4 c4 = lds128(sC + pos);
-                        Bv[s4 * 4 + 0] = b4.x; Bv[s4 * 4 + 1] = b4.y;
-                        Bv[s4 * 4 + 2] = b4.z; Bv[s4 * 4 + 3] = b4.w;
-                        Cv[s4 * 4 + 0] = c4.x; Cv[s4 * 4 + 1] = c4.y;
-                        Cv[s4 * 4 + 2] = c4.z; Cv[s4 * 4 + 3] = c4.w;
-                    }
-                    float yacc = 0.f;
+                        const float2 bp[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
+                        const float2 cp[2] = {make_float2(c4.x, c4.y), make_float2(c4.z, c4.w)};
 #pragma unroll
-                    for (int s = 0; s < SPT; s++) {
-                        const float a = ex2(dls[j] * A2[s]);
-                        h[s] = fmaf(a, h[s], dus[j] * Bv[s]);
-                        yacc = fmaf(Cv[s], h[s], yacc);
+                        for (int k = 0; k < 2; k++) {
+                            const int pi = s4 * 2 + k;
+                            const float2 x = __fmul2_rn(dl2, A2[pi]);
+                            const float2 a = make_float2(ex2(x.x), ex2(x.y));
+                            h[pi] = __ffma2_rn(a, h[pi], __fmul2_rn(du2, bp[k]));
+                            y2 = __ffma2_rn(cp[k], h[pi], y2);
+                        }
                     }
-                    yv[sb + j] = yacc;
+                    yv[sb + j] = y2.x + y2.y;
                 }
                 if (want_prod) Ssum += (dls[0] + dls[1]) + (dls[2] + dls[3]);
                 const int tg_end = t0 + tl + 4;
-                if (rechunk && tg_end < Lq && (tg_end % p.restart_len) == 0 && dvalid) {
+                if (rechunk && tg_end < Lq && (tg_end & 127) == 0 && dvalid) {
                     // the reference backward restarts every chunk from the forward's state
                     const float* src = p.restart +
-                        (((int64_t)b * p.dim + d) * p.restart_nck + (tg_end / p.restart_len - 1)) * 2 * N;
+                        (((int64_t)b * p.dim + d) * p.restart_nck + (tg_end / 128 - 1)) * 2 * N;
 #pragma unroll
                     for (int s = 0; s < SPT; s++) {
                         const int n = g * SPT + s;
-                        if (n < N) h[s] = src[2 * n + 1];
+                        const float v = n < N ? src[2 * n + 1] : 0.f;
+                        if (s & 1) h[s / 2].y = v; else h[s / 2].x = v;
                     }
                 }
-                if (p.ckpt && tg_end <= Lq && (tg_end % p.ckpt_len) == 0)
-                    write_ckpt(tg_end / p.ckpt_len - 1);
+                if (p.ckpt && tg_end <= Lq && (tg_end & ck_mask) == 0) write_ckpt((tg_end >> p.ckpt_shift) - 1);
             }
-            // reduce-scatter y over the LPC lanes of this channel: afterwards slot LPC*r
-            // holds the full sum for token q0 + LPC*r + g.
-            reduce_scatter<LPC, G>(yv, g);
-            // epilogue: skip term, gate, pre-gate copy
+            // lane g now finishes the RL consecutive tokens q0 + g*RL ...
+            reduce_scatter_contig<LPC, G>(yv, g);
+            if (want_out) {
 #pragma unroll
-            for (int r = 0; r < G / LPC; r++) {
-                const int tl = q0 + LPC * r + g;
-                const uint32_t off = swz128(c, tl * ES);
-                const float uv = to_f(*reinterpret_cast<const IT*>(su + off));
-                if (!want_out) continue;
-                const float yt = fmaf(Dd, uv, yv[LPC * r]);
-                float o = yt;
-                if (has_z) {
-                    const float zv = to_f(*reinterpret_cast<const IT*>(sz + off));
-                    o = yt * zv * sigmoidf_fast(zv);
+                for (int r4 = 0; r4 < RL; r4 += 4) {
+                    if (RL >= 4) {
+                        const int tl = q0 + g * RL + r4;
+                        const uint32_t off = swz128(c, tl * ES);
+                        float uv[4], o[4], yt[4];
+                        Vec4<IT>::load(su + off, uv);
+                        float zv[4];
+                        if (has_z) Vec4<IT>::load(sz + off, zv);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            yt[j] = fmaf(Dd, uv[j], yv[r4 + j]);
+                            o[j] = has_z ? yt[j] * zv[j] * sigmoidf_fast(zv[j]) : yt[j];
+                        }
+                        Vec4<IT>::store(so + off, o);
+                        if (want_y) Vec4<IT>::store(sy + off, yt);
+                    }
                 }
-                *reinterpret_cast<IT*>(so + off) = from_f<IT>(o);
-                if (want_y) *reinterpret_cast<IT*>(sy + off) = from_f<IT>(yt);
+                if (RL < 4) {
+#pragma unroll
+                    for (int r = 0; r < RL; r++) {
+                        const int tl = q0 + g * RL + r;
+                        const uint32_t off = swz128(c, tl * ES);
+                        const float uv = to_f(*reinterpret_cast<const IT*>(su + off));
+                        const float yt = fmaf(Dd, uv, yv[r]);
+                        float o = yt;
+                        if (has_z) {
+                            const float zv = to_f(*reinterpret_cast<const IT*>(sz + off));
+                            o = yt * zv * sigmoidf_fast(zv);
+                        }
+                        *reinterpret_cast<IT*>(so + off) = from_f<IT>(o);
+                        if (want_y) *reinterpret_cast<IT*>(sy + off) = from_f<IT>(yt);
+                    }
+                }
             }
         }
         __syncthreads();
@@ -326,12 +377,12 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     }
 
     // the last checkpoint of a sequence whose length is not a multiple of ckpt_len
-    if (p.ckpt && (Lq % p.ckpt_len) != 0) write_ckpt(p.nck - 1);
+    if (p.ckpt && (Lq & ck_mask) != 0) write_ckpt(p.nck - 1);
     if (p.h_last && dvalid) {
 #pragma unroll
         for (int s = 0; s < SPT; s++) {
             const int n = g * SPT + s;
-            if (n < N) p.h_last[((int64_t)b * p.dim + d) * N + n] = h[s];
+            if (n < N) p.h_last[((int64_t)b * p.dim + d) * N + n] = hval(s);
         }
     }
     if (p.use_tma && tid == 0) tma_store_wait_all();

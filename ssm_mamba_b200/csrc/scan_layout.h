@@ -11,7 +11,7 @@ __host__ __device__ inline uint32_t align_up(uint32_t x, uint32_t a) { return (x
 // ---- forward: 2 raw stages of 128-byte rows (TMA 128B swizzle), f32 work rows ----------
 struct FwdSmem {
     uint32_t u[2], delta[2], z[2], B[2], C[2];
-    uint32_t out, y, sD, sDU, sB, sC, bar, total;
+    uint32_t out, y, sD, sDU, sB, sC, bias, bar, total;
 };
 
 __host__ __device__ inline FwdSmem fwd_smem_layout(int dt, int ns, int es, int has_z, int has_y) {
@@ -34,6 +34,7 @@ __host__ __device__ inline FwdSmem fwd_smem_layout(int dt, int ns, int es, int h
     L.sDU = o; o += rows;
     L.sB = o; o += (uint32_t)T * ns * 4u;
     L.sC = o; o += (uint32_t)T * ns * 4u;
+    L.bias = o; o += align_up((uint32_t)dt * 4u, 16u);
     L.bar = align_up(o, 8u); o = L.bar + 16u;
     L.total = o;
     return L;
@@ -48,6 +49,7 @@ struct BwdSmem {
     uint32_t sD, sDU, sG, sSP, sU;                    // f32 [dt][TB+4]
     uint32_t sB, sC;                                  // f32 [nrot][TB*ns + 16]
     uint32_t slots;                                   // f32 [nwarps][2][ns][TB+1]
+    uint32_t bias;                                    // f32 [dt]
     uint32_t bar, total;
     uint32_t rot_stride;                              // floats between rotated copies
     uint32_t slot_stride;                             // floats between warp slots
@@ -83,6 +85,7 @@ __host__ __device__ inline BwdSmem bwd_smem_layout(int dt, int ns, int n, int es
     L.sC = o; o += align_up((uint32_t)nrot * L.rot_stride * 4u, 128u);
     L.slot_stride = 2u * ns * (TB + 1);
     L.slots = o; o += align_up((uint32_t)nwarps * L.slot_stride * 4u, 128u);
+    L.bias = o; o += align_up((uint32_t)dt * 4u, 16u);
     L.bar = align_up(o, 8u); o = L.bar + 8u;
     L.total = o;
     return L;

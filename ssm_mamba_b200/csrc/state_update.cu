@@ -17,33 +17,24 @@ namespace ssm {
 
 template <typename IT, int LPC, int SPT>
 __global__ void __launch_bounds__(256) state_update_kernel(const __grid_constant__ UpdParams p) {
-    const int tid = blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t row = tid / LPC;
-    const int g = tid % LPC;
-    const int64_t nrows = (int64_t)p.batch * p.dim;
-    // rows past the end still take part in the shuffles, with their work masked off
-    const bool live = row < nrows;
-    const int64_t b = live ? row / p.dim : 0;
-    const int64_t d = live ? row % p.dim : 0;
+    // grid: x = channel tiles of 256/LPC channels, y = batch rows; no integer division
+    constexpr int RPB = 256 / LPC;
+    const int g = threadIdx.x % LPC;
+    const int d = blockIdx.x * RPB + threadIdx.x / LPC;
+    const int b = blockIdx.y;
+    // lanes past the last channel still take part in the shuffles, with their work masked off
+    const bool live = d < p.dim;
+    const int dd = live ? d : 0;
     const int N = p.dstate;
     const int n0 = g * SPT;
 
-    float xv = 0.f, dtv = 0.f, zv = 0.f;
-    if (live) {
-        xv = to_f(static_cast<const IT*>(p.x)[b * p.x_sb + d]);
-        dtv = to_f(static_cast<const IT*>(p.dtv)[b * p.dt_sb + d]);
-        if (p.z) zv = to_f(static_cast<const IT*>(p.z)[b * p.z_sb + d]);
-        if (p.dt_bias) dtv += p.dt_bias[d];
-    }
-    const float dl = p.dt_softplus ? softplus20(dtv) : dtv;
-    const float dx = dl * xv;
+    const float* hin = p.state + (int64_t)b * p.st_sb + (int64_t)dd * p.st_sd + n0;
+    float* hout = p.state_out + (int64_t)b * p.so_sb + (int64_t)dd * p.so_sd + n0;
+    const float* Ar = p.A + (int64_t)dd * p.A_sd + n0;
+    const IT* Br = static_cast<const IT*>(p.B) + (int64_t)b * p.B_sb + n0;
+    const IT* Cr = static_cast<const IT*>(p.C) + (int64_t)b * p.C_sb + n0;
 
-    const float* hin = p.state + b * p.st_sb + d * p.st_sd + n0;
-    float* hout = p.state_out + b * p.so_sb + d * p.so_sd + n0;
-    const float* Ar = p.A + d * p.A_sd + n0;
-    const IT* Br = static_cast<const IT*>(p.B) + b * p.B_sb + n0;
-    const IT* Cr = static_cast<const IT*>(p.C) + b * p.C_sb + n0;
-
+    // issue every load before any arithmetic
     float h[SPT], a[SPT], bv[SPT], cv[SPT];
     const bool full = live && (n0 + SPT <= N);
     const bool vec = full && ((reinterpret_cast<uintptr_t>(hin) | reinterpret_cast<uintptr_t>(hout) |
@@ -67,9 +58,20 @@ __global__ void __launch_bounds__(256) state_update_kernel(const __grid_constant
 #pragma unroll
     for (int s = 0; s < SPT; s++) {
         const bool ok = live && n0 + s < N;
-        bv[s] = ok ? to_f(Br[s]) : 0.f;
-        cv[s] = ok ? to_f(Cr[s]) : 0.f;
+        bv[s] = ok ? to_f(__ldg(Br + s)) : 0.f;
+        cv[s] = ok ? to_f(__ldg(Cr + s)) : 0.f;
     }
+    float xv = 0.f, dtv = 0.f, zv = 0.f, bias = 0.f, Dv = 0.f;
+    if (live) {
+        xv = to_f(static_cast<const IT*>(p.x)[(int64_t)b * p.x_sb + dd]);
+        dtv = to_f(static_cast<const IT*>(p.dtv)[(int64_t)b * p.dt_sb + dd]);
+        if (p.z) zv = to_f(static_cast<const IT*>(p.z)[(int64_t)b * p.z_sb + dd]);
+        if (p.dt_bias) bias = __ldg(p.dt_bias + dd);
+        if (p.D) Dv = __ldg(p.D + dd);
+    }
+    const float x = dtv + bias;
+    const float dl = p.dt_softplus ? softplus_series(x) : x;
+    const float dx = dl * xv;
 
     float y = 0.f;
 #pragma unroll
@@ -89,17 +91,17 @@ __global__ void __launch_bounds__(256) state_update_kernel(const __grid_constant
             if (n0 + s < N) hout[s] = h[s];
     }
     if (live && g == 0) {
-        float o = y + (p.D ? p.D[d] : 0.f) * xv;
+        float o = fmaf(Dv, xv, y);
         if (p.z) o = o * zv * sigmoidf_fast(zv);
-        static_cast<IT*>(p.out)[b * p.out_sb + d] = from_f<IT>(o);
+        static_cast<IT*>(p.out)[(int64_t)b * p.out_sb + dd] = from_f<IT>(o);
     }
 }
 
 template <typename IT, int LPC, int SPT>
 static cudaError_t launch_upd_t(const UpdParams& p, cudaStream_t stream) {
-    const int64_t threads = (int64_t)p.batch * p.dim * LPC;
-    const int64_t blocks = (threads + 255) / 256;
-    state_update_kernel<IT, LPC, SPT><<<(unsigned)blocks, 256, 0, stream>>>(p);
+    constexpr int RPB = 256 / LPC;
+    dim3 grid((unsigned)((p.dim + RPB - 1) / RPB), (unsigned)p.batch);
+    state_update_kernel<IT, LPC, SPT><<<grid, 256, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
