@@ -175,6 +175,17 @@ SSM_API size_t ssm_scan_bwd_workspace_size(const ssm_scan_bwd_args* args);
 SSM_API int ssm_scan_bwd(const ssm_scan_bwd_args* args, void* workspace, size_t workspace_bytes,
                  void* stream);
 
+/* Backward selective scan that allocates nothing.  No counterpart in the reference.
+ * For callers that cannot allocate device memory when they run the backward (inside a
+ * CUDA-graph capture, under a framework that owns all device memory, or through an FFI
+ * with no allocation API): instead of a caller-provided workspace it uses a 16 MiB
+ * scratch array compiled into the library (held on every GPU that loads the library until
+ * exit).  Shapes whose ssm_scan_bwd_workspace_size exceeds 16 MiB - 256 bytes are rejected
+ * with SSM_ERR_WORKSPACE.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make it before any stream capture.  Every call on a device shares
+ * the array: calls whose kernels overlap on the GPU race and must be serialised. */
+SSM_API int ssm_scan_bwd_noalloc(const ssm_scan_bwd_args* args, void* stream);
+
 /* One decode step (replaces selective_update.apply).  state_out may alias state. */
 SSM_API int ssm_state_update(const ssm_state_update_args* args, void* stream);
 

@@ -118,6 +118,8 @@ def lib() -> ctypes.CDLL:
         L.ssm_scan_bwd_workspace_size.restype = ctypes.c_size_t
         L.ssm_scan_bwd.argtypes = [ctypes.POINTER(ScanBwdArgs), _p, ctypes.c_size_t, _p]
         L.ssm_scan_bwd.restype = ctypes.c_int
+        L.ssm_scan_bwd_noalloc.argtypes = [ctypes.POINTER(ScanBwdArgs), _p]
+        L.ssm_scan_bwd_noalloc.restype = ctypes.c_int
         L.ssm_state_update.argtypes = [ctypes.POINTER(StateUpdateArgs), _p]
         L.ssm_state_update.restype = ctypes.c_int
         L.ssm_check_device_error.argtypes = [ctypes.POINTER(ctypes.c_int), _p]
@@ -241,6 +243,12 @@ def call_bwd(args: ScanBwdArgs, workspace=None, stream=None):
         workspace = torch.empty(n, dtype=torch.uint8, device="cuda")
     _check(lib().ssm_scan_bwd(ctypes.byref(args), _t(workspace), workspace.numel(),
                               stream if stream is not None else _stream()))
+
+
+def call_bwd_noalloc(args: ScanBwdArgs, stream=None):
+    """Runs ssm_scan_bwd_noalloc: the backward on the library's built-in scratch, for
+    callers that cannot allocate device memory."""
+    _check(lib().ssm_scan_bwd_noalloc(ctypes.byref(args), stream if stream is not None else _stream()))
 
 
 def fill_update(state, state_out, x, dt, A, B, C, out, D=None, z=None, dt_bias=None,

@@ -302,15 +302,14 @@ int ssm_scan_ckpt_from_reference(const ssm_scan_fwd_args* a, const float* ref_ck
     return fwd_impl(a, ref_ckpt, stream);
 }
 
-static int bwd_common(const ssm_scan_bwd_args* a, DevInfo** di, StateSplit* sp, int* dt) {
+// Shape checks and CTA sizing of the backward; touches no device memory.
+static int bwd_shape(const ssm_scan_bwd_args* a, int sms, StateSplit* sp, int* dt) {
     if (a->batch < 1 || a->dim < 1 || a->seqlen < 1 || a->dstate < 1)
         return fail(SSM_ERR_INVALID, "ssm_scan_bwd: sizes must be positive");
     if (a->dstate > 256) return fail(SSM_ERR_INVALID, "selective_scan only supports state_dim <= 256");
     if (a->seqlen > (1 << 30) || a->dim > (1 << 30) || a->batch > (1 << 30))
         return fail(SSM_ERR_INVALID, "ssm_scan_bwd: sizes too large");
     if (!valid_dtype(a->dtype)) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: dtype must be SSM_F32 or SSM_BF16");
-    int rc = device_info(di);
-    if (rc) return rc;
     *sp = split_states(a->dstate);
     const int is_bf16 = a->dtype == SSM_BF16;
     const int has_z = a->z != nullptr;
@@ -321,9 +320,15 @@ static int bwd_common(const ssm_scan_bwd_args* a, DevInfo** di, StateSplit* sp, 
     memset(&key, 0, sizeof(key));
     key.dev = dev; key.kind = 1; key.is_bf16 = is_bf16; key.lpc = s.lpc; key.dstate = (int)a->dstate;
     key.has_z = has_z; key.has_y = 0; key.batch = a->batch; key.dim = a->dim;
-    *dt = cached_dt(key, (*di)->sms, [&](int d) { return bwd_occupancy(is_bf16, s.lpc, d, (int)a->dstate, has_z); });
+    *dt = cached_dt(key, sms, [&](int d) { return bwd_occupancy(is_bf16, s.lpc, d, (int)a->dstate, has_z); });
     if (*dt < 1) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: no CTA shape fits shared memory");
     return SSM_OK;
+}
+
+static int bwd_common(const ssm_scan_bwd_args* a, DevInfo** di, StateSplit* sp, int* dt) {
+    int rc = device_info(di);
+    if (rc) return rc;
+    return bwd_shape(a, (*di)->sms, sp, dt);
 }
 
 struct WsLayout { size_t bc, a, dd, total; };
@@ -351,13 +356,28 @@ size_t ssm_scan_bwd_workspace_size(const ssm_scan_bwd_args* a) {
     return ws_layout(a, dt).total;
 }
 
-int ssm_scan_bwd(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, void* stream_) {
-    if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: args is NULL");
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-    DevInfo* di;
+}  // extern "C"
+
+namespace ssm {
+
+// Workspace bytes of the backward for these arguments on a device with `sms` SMs (0 on a
+// shape error); touches no device memory.
+size_t scan_bwd_workspace_bytes(const ssm_scan_bwd_args* a, int sms) {
     StateSplit sp;
     int dt;
-    int rc = bwd_common(a, &di, &sp, &dt);
+    if (!a || bwd_shape(a, sms, &sp, &dt)) return 0;
+    return ws_layout(a, dt).total;
+}
+
+// The backward proper: validation, tensor maps and the two launches, with the caller's
+// workspace and device error word.  Allocates nothing.
+int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, int* err_word, int sms,
+                 void* stream_) {
+    if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: args is NULL");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    StateSplit sp;
+    int dt;
+    int rc = bwd_shape(a, sms, &sp, &dt);
     if (rc) return rc;
     if (!a->u || !a->delta || !a->A || !a->B || !a->C || !a->dout || !a->ckpt || !a->du ||
         !a->ddelta || !a->dA || !a->dB || !a->dC)
@@ -402,7 +422,7 @@ int ssm_scan_bwd(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, v
     p.ws_bc = reinterpret_cast<float*>(ws + w.bc);
     p.ws_a = reinterpret_cast<float*>(ws + w.a);
     p.ws_dd = reinterpret_cast<float*>(ws + w.dd);
-    p.err = di->err;
+    p.err = err_word;
 
     p.use_tma = tma_ok(a->u, a->u_dim_stride, a->u_batch_stride, es) &&
                 tma_ok(a->delta, a->delta_dim_stride, a->delta_batch_stride, es) &&
@@ -446,6 +466,20 @@ int ssm_scan_bwd(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, v
     e = launch_scan_reduce(r, stream);
     if (e != cudaSuccess) return cuda_fail(e, "scan_reduce launch");
     return SSM_OK;
+}
+
+void set_last_error(const char* msg) { g_err = msg; }
+
+}  // namespace ssm
+
+extern "C" {
+
+int ssm_scan_bwd(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, void* stream) {
+    if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: args is NULL");
+    DevInfo* di = nullptr;
+    int rc = device_info(&di);
+    if (rc) return rc;
+    return scan_bwd_run(a, workspace, ws_bytes, di->err, di->sms, stream);
 }
 
 int ssm_state_update(const ssm_state_update_args* a, void* stream_) {
