@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -18,15 +19,15 @@
 #include "scan_layout.h"
 
 namespace ssm {
-cudaError_t launch_scan_fwd(const FwdParams& p, int is_bf16, int lpc, const CUtensorMap* maps,
+cudaError_t launch_scan_fwd(const FwdParams& p, int is_bf16, int lpc, int spt, const CUtensorMap* maps,
                             cudaStream_t stream);
-cudaError_t launch_scan_bwd(const BwdParams& p, int is_bf16, int lpc, const CUtensorMap* maps,
+cudaError_t launch_scan_bwd(const BwdParams& p, int is_bf16, int lpc, int spt, const CUtensorMap* maps,
                             cudaStream_t stream);
 cudaError_t launch_scan_reduce(const ReduceParams& p, cudaStream_t stream);
 cudaError_t launch_state_update(const UpdParams& p, int is_bf16, int lpc, cudaStream_t stream);
 size_t bwd_smem_bytes(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
-int fwd_occupancy(int is_bf16, int lpc, int dt, int has_z, int has_y);
-int bwd_occupancy(int is_bf16, int lpc, int dt, int dstate, int has_z);
+int fwd_occupancy(int is_bf16, int lpc, int spt, int dt, int has_z, int has_y);
+int bwd_occupancy(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
 }  // namespace ssm
 
 using namespace ssm;
@@ -52,11 +53,32 @@ int cuda_fail(cudaError_t e, const char* what) {
 // ---- lanes per channel / states per thread / backward sub-tile for a state count ----------
 struct StateSplit { int lpc, spt, k; };
 
+// Decode kernel: 4 states per thread (8 above 128 states).
 StateSplit split_states(int64_t n) {
     if (n > 128) return {32, 8, 4};
     int ns = 4;
     while (ns < n) ns *= 2;
     return {ns / 4, 4, 8};
+}
+
+// Scan kernels: 4 states per thread; 2 only when 4 would leave fewer than 4 warps per SM
+// (measured on B200 at config 2: 4 states per thread is 1.5x faster than 2 at 10 warps per
+// SM -- the extra per-state reductions outweigh the extra warps).  The environment
+// variable named by `env` (SSM_FWD_SPT / SSM_BWD_SPT) may force 2 or 4 for experiments.
+// The backward's checkpoint interval k depends on dstate only, so forward and backward
+// always agree.
+StateSplit scan_split(int64_t n, int64_t rows, int sms, const char* env) {
+    if (n > 128) return {32, 8, 4};
+    int ns = 4;
+    while (ns < n) ns *= 2;
+    const StateSplit s4{ns / 4, 4, 8};
+    const StateSplit s2{ns / 2, 2, 8};
+    const bool s2_ok = ns / 2 <= 32;
+    const char* e = getenv(env);
+    if (e && e[0] == '2' && s2_ok) return s2;
+    if (e && e[0] == '4') return s4;
+    const double warps4 = (double)rows * (ns / 4) / 32.0 / (sms > 0 ? sms : 148);
+    return (warps4 < 4.0 && s2_ok) ? s2 : s4;
 }
 
 // ---- device attributes and the per-device error word ----------------------------------------
@@ -136,10 +158,12 @@ int encode3d(CUtensorMap* map, const void* ptr, int is_bf16, int64_t d0, int64_t
 // ---- CTA sizing: channels per CTA ---------------------------------------------------------------
 // Picks dt (a multiple of the channels a warp holds, at most 128 threads per CTA) that
 // minimises the estimated time on the busiest SM: CTAs are spread evenly over the SMs and
-// run `res` at a time (res from the occupancy calculator), and an SM is assumed to reach
-// full throughput at 8 resident warps.  Results are cached per shape.
+// run `res` at a time (res from the occupancy calculator), an SM is assumed to reach full
+// throughput at 8 resident warps, and every CTA pays a fixed cost worth `ovh` channels
+// (staging B and C for its batch row; in the backward also its dB/dC partials).  Results
+// are cached per shape.
 template <typename OccFn>
-int choose_dt(int64_t batch, int64_t dim, int lpc, int sms, OccFn occupancy) {
+int choose_dt(int64_t batch, int64_t dim, int lpc, int sms, double ovh, OccFn occupancy) {
     const int cpw = 32 / lpc;
     const int dtmax = 128 / lpc;
     int best = -1;
@@ -154,7 +178,7 @@ int choose_dt(int64_t batch, int64_t dim, int lpc, int sms, OccFn occupancy) {
         for (int64_t left = per_sm; left > 0; left -= res) {
             const int64_t m = left < res ? left : res;
             const double thr = (m * warps) >= 8 ? 1.0 : (double)(m * warps) / 8.0;
-            t += (double)m * dt / thr;
+            t += (double)m * (dt + ovh) / thr;
         }
         t *= (double)(((dim + dt - 1) / dt) * dt) / (double)dim;  // ragged last channel tile
         if (t < best_t * 0.999) {
@@ -166,7 +190,7 @@ int choose_dt(int64_t batch, int64_t dim, int lpc, int sms, OccFn occupancy) {
 }
 
 struct DtKey {
-    int dev, kind, is_bf16, lpc, dstate, has_z, has_y;
+    int dev, kind, is_bf16, lpc, spt, dstate, has_z, has_y;
     int64_t batch, dim;
     bool operator==(const DtKey& o) const { return memcmp(this, &o, sizeof(*this)) == 0; }
 };
@@ -182,7 +206,7 @@ int cached_dt(DtKey key, int sms, OccFn occ) {
         for (int i = 0; i < g_dt_n; i++)
             if (g_dt_keys[i] == key) return g_dt_vals[i];
     }
-    const int dt = choose_dt(key.batch, key.dim, key.lpc, sms, occ);
+    const int dt = choose_dt(key.batch, key.dim, key.lpc, sms, key.kind == 0 ? 4.0 : 8.0, occ);
     std::lock_guard<std::mutex> lk(g_dt_mu);
     const int slot = g_dt_n < 64 ? g_dt_n++ : (int)(key.dim % 64);
     g_dt_keys[slot] = key;
@@ -233,7 +257,7 @@ static int fwd_impl(const ssm_scan_fwd_args* a, const float* restart, void* stre
     DevInfo* di = nullptr;
     int rc = device_info(&di);
     if (rc) return rc;
-    const StateSplit sp = split_states(a->dstate);
+    const StateSplit sp = scan_split(a->dstate, a->batch * a->dim, di->sms, "SSM_FWD_SPT");
     const int T = (int)(128 / es);
 
     FwdParams p;
@@ -263,9 +287,9 @@ static int fwd_impl(const ssm_scan_fwd_args* a, const float* restart, void* stre
     cudaGetDevice(&dev);
     DtKey key;
     memset(&key, 0, sizeof(key));
-    key.dev = dev; key.kind = 0; key.is_bf16 = is_bf16; key.lpc = sp.lpc; key.dstate = 0;
+    key.dev = dev; key.kind = 0; key.is_bf16 = is_bf16; key.lpc = sp.lpc; key.spt = sp.spt; key.dstate = 0;
     key.has_z = has_z; key.has_y = has_y; key.batch = a->batch; key.dim = a->dim;
-    p.dt = cached_dt(key, di->sms, [&](int dt) { return fwd_occupancy(is_bf16, sp.lpc, dt, has_z, has_y); });
+    p.dt = cached_dt(key, di->sms, [&](int dt) { return fwd_occupancy(is_bf16, sp.lpc, sp.spt, dt, has_z, has_y); });
     if (p.dt < 1) return fail(SSM_ERR_INVALID, "ssm_scan_fwd: no CTA shape fits shared memory");
     p.ntile_d = (int)((a->dim + p.dt - 1) / p.dt);
 
@@ -290,7 +314,7 @@ static int fwd_impl(const ssm_scan_fwd_args* a, const float* restart, void* stre
             (rc = encode3d(&maps[6], a->y, is_bf16, a->seqlen, a->dim, a->batch, a->y_dim_stride, a->y_batch_stride, T, p.dt, sw)))
             return rc;
     }
-    cudaError_t e = launch_scan_fwd(p, is_bf16, sp.lpc, maps, stream);
+    cudaError_t e = launch_scan_fwd(p, is_bf16, sp.lpc, sp.spt, maps, stream);
     if (e != cudaSuccess) return cuda_fail(e, "scan_fwd launch");
     return SSM_OK;
 }
@@ -310,7 +334,7 @@ static int bwd_shape(const ssm_scan_bwd_args* a, int sms, StateSplit* sp, int* d
     if (a->seqlen > (1 << 30) || a->dim > (1 << 30) || a->batch > (1 << 30))
         return fail(SSM_ERR_INVALID, "ssm_scan_bwd: sizes too large");
     if (!valid_dtype(a->dtype)) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: dtype must be SSM_F32 or SSM_BF16");
-    *sp = split_states(a->dstate);
+    *sp = scan_split(a->dstate, a->batch * a->dim, sms, "SSM_BWD_SPT");
     const int is_bf16 = a->dtype == SSM_BF16;
     const int has_z = a->z != nullptr;
     const StateSplit s = *sp;
@@ -318,9 +342,9 @@ static int bwd_shape(const ssm_scan_bwd_args* a, int sms, StateSplit* sp, int* d
     cudaGetDevice(&dev);
     DtKey key;
     memset(&key, 0, sizeof(key));
-    key.dev = dev; key.kind = 1; key.is_bf16 = is_bf16; key.lpc = s.lpc; key.dstate = (int)a->dstate;
+    key.dev = dev; key.kind = 1; key.is_bf16 = is_bf16; key.lpc = s.lpc; key.spt = s.spt; key.dstate = (int)a->dstate;
     key.has_z = has_z; key.has_y = 0; key.batch = a->batch; key.dim = a->dim;
-    *dt = cached_dt(key, sms, [&](int d) { return bwd_occupancy(is_bf16, s.lpc, d, (int)a->dstate, has_z); });
+    *dt = cached_dt(key, sms, [&](int d) { return bwd_occupancy(is_bf16, s.lpc, s.spt, d, (int)a->dstate, has_z); });
     if (*dt < 1) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: no CTA shape fits shared memory");
     return SSM_OK;
 }
@@ -440,7 +464,8 @@ int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, i
         if ((rc = get_encoder())) return rc;
         const int TB = kBwdTile;
         const CUtensorMapSwizzle none = CU_TENSOR_MAP_SWIZZLE_NONE;
-        const CUtensorMapSwizzle osw = is_bf16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+        // output rows are TB * element bytes: 32 (bf16) or 64 (f32) bytes
+        const CUtensorMapSwizzle osw = is_bf16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
         const int64_t L = a->seqlen, Dm = a->dim, Bs = a->batch, N = a->dstate;
         if ((rc = encode3d(&maps[0], a->u, is_bf16, L, Dm, Bs, a->u_dim_stride, a->u_batch_stride, TB, dt, none)) ||
             (rc = encode3d(&maps[1], a->delta, is_bf16, L, Dm, Bs, a->delta_dim_stride, a->delta_batch_stride, TB, dt, none)) ||
@@ -454,7 +479,7 @@ int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, i
             (rc = encode3d(&maps[9], a->dz, is_bf16, L, Dm, Bs, a->dz_dim_stride, a->dz_batch_stride, TB, dt, osw)))
             return rc;
     }
-    cudaError_t e = launch_scan_bwd(p, is_bf16, sp.lpc, maps, stream);
+    cudaError_t e = launch_scan_bwd(p, is_bf16, sp.lpc, sp.spt, maps, stream);
     if (e != cudaSuccess) return cuda_fail(e, "scan_bwd launch");
 
     ReduceParams r;

@@ -78,6 +78,26 @@ __device__ __forceinline__ float sigmoid_from_t(float x, float t) {
     return x >= 0.f ? r : t * r;
 }
 
+// The SPT consecutive states a lane owns at token t of a float32 [T][NS] B/C row whose
+// float4 groups are XOR-swizzled by `sw` (group q of row t sits at position q ^ sw), as
+// SPT/2 packed pairs.  SPT = 2 reads half of a group, SPT >= 4 whole groups.
+template <int SPT, int NS>
+__device__ __forceinline__ void load_state_pairs(const float* rows, int t, int g, int sw,
+                                                 float2 (&out)[SPT / 2]) {
+    if constexpr (SPT == 2) {
+        const int pos = t * NS + (((g >> 1) ^ sw) << 2) + ((g & 1) << 1);
+        out[0] = *reinterpret_cast<const float2*>(rows + pos);
+    } else {
+#pragma unroll
+        for (int s4 = 0; s4 < SPT / 4; s4++) {
+            const int qq = g * (SPT / 4) + s4;
+            const float4 v = *reinterpret_cast<const float4*>(rows + t * NS + ((qq ^ sw) << 2));
+            out[2 * s4] = make_float2(v.x, v.y);
+            out[2 * s4 + 1] = make_float2(v.z, v.w);
+        }
+    }
+}
+
 // four consecutive elements as float (from 8 or 16 bytes of shared memory)
 template <typename T> struct Vec4;
 template <> struct Vec4<float> {
@@ -113,6 +133,12 @@ template <> struct Vec4<__nv_bfloat16> {
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t byte_in_row) {
     return row * 128u + ((((byte_in_row >> 4) ^ row) & 7u) << 4) + (byte_in_row & 15u);
+}
+
+// 32-byte swizzle (CU_TENSOR_MAP_SWIZZLE_32B) for 32-byte rows: 16-byte chunk j of row r
+// sits at chunk position j ^ ((r >> 2) & 1) (address bit 4 ^= bit 7).
+__device__ __forceinline__ uint32_t swz32(uint32_t row, uint32_t byte_in_row) {
+    return row * 32u + ((((byte_in_row >> 4) ^ (row >> 2)) & 1u) << 4) + (byte_in_row & 15u);
 }
 
 // 64-byte swizzle (CU_TENSOR_MAP_SWIZZLE_64B) for 64-byte rows: 16-byte chunk j of row r

@@ -46,14 +46,16 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
     constexpr int TB = kBwdTile;
     constexpr int NS = LPC * SPT;
     constexpr int CPW = 32 / LPC;                 // channel lanes per warp
-    constexpr bool ROT = (CPW >= 4) && (SPT == 4);
-    constexpr int NROT = ROT ? 4 : 1;
+    // XOR-rotated state order across SPT channel lanes (SPT = 2 or 4) for the dB/dC sums
+    constexpr bool ROT = (CPW >= SPT) && (SPT == 2 || SPT == 4);
+    constexpr int NROT = ROT ? SPT : 1;
     constexpr int Q = NS / 4;
     constexpr int QM = (Q < 8 ? Q : 8) - 1;
     constexpr int NSUB = TB / K;
     constexpr int RS = TB + 4;
     constexpr int V = 2 * K;                      // S1 and S2 per sub-tile token
     static_assert(TB % K == 0 && K % 4 == 0, "sub-tiles must be whole float4 groups");
+    static_assert(SPT == 2 || SPT % 4 == 0, "states per thread: 2 or a multiple of 4");
 
     extern __shared__ __align__(1024) unsigned char smem[];
     if ((smem_u32(smem) & 1023u) != 0u) {
@@ -65,13 +67,13 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
     const int lane = tid & 31, warp = tid >> 5;
     const int c = tid / LPC, g = tid % LPC;
     const int cw = lane / LPC;
-    const int rot = ROT ? (cw & 3) : 0;
+    const int rot = ROT ? (cw & (SPT - 1)) : 0;
     const int b = blockIdx.x / p.ntile_d, tile_d = blockIdx.x % p.ntile_d;
     const int d0 = tile_d * DT, d = d0 + c;
     const bool dvalid = d < p.dim;
     const int N = p.dstate, Lq = p.seqlen;
     const bool has_z = p.z != nullptr;
-    const BwdSmem S = bwd_smem_layout(DT, NS, N, ES, NROT, nthr / 32, has_z ? 1 : 0);
+    const BwdSmem S = bwd_smem_layout(DT, NS, N, ES, NROT, nthr / 32, has_z ? 1 : 0, K);
     float* sD = reinterpret_cast<float*>(smem + S.sD);
     float* sDU = reinterpret_cast<float*>(smem + S.sDU);
     float* sG = reinterpret_cast<float*>(smem + S.sG);
@@ -80,6 +82,9 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
     float* sB = reinterpret_cast<float*>(smem + S.sB);
     float* sC = reinterpret_cast<float*>(smem + S.sC);
     float* slots = reinterpret_cast<float*>(smem + S.slots);
+    float* xch = reinterpret_cast<float*>(smem + S.xch);
+    float* xwarp = xch + (tid >> 5) * 32 * (int)S.xch_stride;   // this warp's exchange area
+    float* xmine = xwarp + (tid & 31) * (int)S.xch_stride;      // this lane's block
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S.bar);
 
     // ---- per-batch length rules (reference semantics when length is given) ----------------
@@ -190,7 +195,7 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
 
     // byte offset of (channel row, token) in a swizzled output tile
     auto out_off = [&](int row, int t) -> uint32_t {
-        return ES == 2 ? swz64(row, t * ES) : swz128(row, t * ES);
+        return ES == 2 ? swz32(row, t * ES) : swz64(row, t * ES);
     };
 
     if (p.use_tma && tid == 0) {
@@ -303,16 +308,21 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
             if (ts > 0) load_ckpt(ts - K, h0n);
             const bool skipped = ts >= Rskip;
 
-            float v[V];
+            float v[LPC <= K ? 1 : V];
             if (skipped) {
                 // reference: a 128-token chunk that starts at or after len is skipped
+                if constexpr (LPC <= K) {
 #pragma unroll
-                for (int j = 0; j < V; j++) v[j] = 0.f;
+                    for (int k = 0; k < K; k++) *reinterpret_cast<float2*>(xmine + 2 * k) = make_float2(0.f, 0.f);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < V; j++) v[j] = 0.f;
+                }
 #pragma unroll
                 for (int k = 0; k < K; k++) {
                     if (ROT) {
-                        if (cw < 4) {
-                            const int n = g * 4 + cw;
+                        if (cw < SPT) {
+                            const int n = g * SPT + cw;
                             if (n < N) {
                                 wslot[n * (TB + 1) + tl0 + k] = 0.f;
                                 wslot[(NS + n) * (TB + 1) + tl0 + k] = 0.f;
@@ -351,25 +361,20 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                             }
                             const float2 dl2 = make_float2(dls[j], dls[j]);
                             const float2 du2 = make_float2(dus[j], dus[j]);
+                            float2 bp[NP];
+                            load_state_pairs<SPT, NS>(sBr, t, g, t & QM, bp);
 #pragma unroll
-                            for (int s4 = 0; s4 < SPT / 4; s4++) {
-                                const int qq = g * (SPT / 4) + s4;
-                                const float4 b4 = lds128(sBr + t * NS + ((qq ^ (t & QM)) << 2));
-                                const float2 bp[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
-#pragma unroll
-                                for (int e = 0; e < 2; e++) {
-                                    const int pi = s4 * 2 + e;
-                                    const float2 prev = k == 0 ? h0[pi] : hv[k - 1][pi];
-                                    const float2 x = __fmul2_rn(dl2, A2[pi]);
-                                    float2 a = make_float2(ex2(x.x), ex2(x.y));
-                                    float2 bb = __fmul2_rn(du2, bp[e]);
-                                    if (GEN && msk) {
-                                        a = make_float2(1.f, 1.f);
-                                        bb = make_float2(0.f, 0.f);
-                                    }
-                                    av[k][pi] = a;
-                                    hv[k][pi] = __ffma2_rn(a, prev, bb);
+                            for (int pi = 0; pi < NP; pi++) {
+                                const float2 prev = k == 0 ? h0[pi] : hv[k - 1][pi];
+                                const float2 x = __fmul2_rn(dl2, A2[pi]);
+                                float2 a = make_float2(ex2(x.x), ex2(x.y));
+                                float2 bb = __fmul2_rn(du2, bp[pi]);
+                                if (GEN && msk) {
+                                    a = make_float2(1.f, 1.f);
+                                    bb = make_float2(0.f, 0.f);
                                 }
+                                av[k][pi] = a;
+                                hv[k][pi] = __ffma2_rn(a, prev, bb);
                             }
                         }
                     }
@@ -398,57 +403,60 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                             const float2 dl2 = make_float2(dlv, dlv);
                             float2 s12 = make_float2(0.f, 0.f), s22 = make_float2(0.f, 0.f);
                             float dBv[SPT], dCv[SPT];
+                            float2 bp[NP], cp[NP];
+                            load_state_pairs<SPT, NS>(sBr, t, g, t & QM, bp);
+                            load_state_pairs<SPT, NS>(sCr, t, g, t & QM, cp);
 #pragma unroll
-                            for (int s4 = 0; s4 < SPT / 4; s4++) {
-                                const int qq = g * (SPT / 4) + s4;
-                                const int pos = t * NS + ((qq ^ (t & QM)) << 2);
-                                const float4 b4 = lds128(sBr + pos);
-                                const float4 c4 = lds128(sCr + pos);
-                                const float2 bp[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
-                                const float2 cp[2] = {make_float2(c4.x, c4.y), make_float2(c4.z, c4.w)};
-#pragma unroll
-                                for (int e = 0; e < 2; e++) {
-                                    const int pi = s4 * 2 + e;
-                                    float2 inj = __fmul2_rn(dg2, cp[e]);
-                                    if (GEN && msk) inj = make_float2(0.f, 0.f);
-                                    const float2 Gs = __ffma2_rn(anp[pi], Gp[pi], inj);
-                                    Gp[pi] = Gs;
-                                    anp[pi] = av[k][pi];
-                                    const float2 qv = __ffma2_rn(ndu2, bp[e], hv[k][pi]);
-                                    s12 = __ffma2_rn(Gs, bp[e], s12);
-                                    const float2 w = __fmul2_rn(Gs, qv);
-                                    s22 = __ffma2_rn(An[pi], w, s22);
-                                    dAp[pi] = __ffma2_rn(dl2, w, dAp[pi]);
-                                    float2 db = __fmul2_rn(Gs, du2);
-                                    float2 dc = __fmul2_rn(dg2, hv[k][pi]);
-                                    if (GEN && !vld) {
-                                        db = make_float2(0.f, 0.f);
-                                        dc = make_float2(0.f, 0.f);
-                                    }
-                                    dBv[pi * 2] = db.x; dBv[pi * 2 + 1] = db.y;
-                                    dCv[pi * 2] = dc.x; dCv[pi * 2 + 1] = dc.y;
+                            for (int pi = 0; pi < NP; pi++) {
+                                float2 inj = __fmul2_rn(dg2, cp[pi]);
+                                if (GEN && msk) inj = make_float2(0.f, 0.f);
+                                const float2 Gs = __ffma2_rn(anp[pi], Gp[pi], inj);
+                                Gp[pi] = Gs;
+                                anp[pi] = av[k][pi];
+                                // q = h_t - delta*u*B (the reference's at_ht); without padding it
+                                // equals decay * h_{t-1}, one multiply
+                                const float2 qv = GEN ? __ffma2_rn(ndu2, bp[pi], hv[k][pi])
+                                                      : __fmul2_rn(av[k][pi], k == 0 ? h0[pi] : hv[k - 1][pi]);
+                                s12 = __ffma2_rn(Gs, bp[pi], s12);
+                                const float2 w = __fmul2_rn(Gs, qv);
+                                s22 = __ffma2_rn(An[pi], w, s22);
+                                dAp[pi] = __ffma2_rn(dl2, w, dAp[pi]);
+                                float2 db = __fmul2_rn(Gs, du2);
+                                float2 dc = __fmul2_rn(dg2, hv[k][pi]);
+                                if (GEN && !vld) {
+                                    db = make_float2(0.f, 0.f);
+                                    dc = make_float2(0.f, 0.f);
+                                }
+                                dBv[pi * 2] = db.x; dBv[pi * 2 + 1] = db.y;
+                                dCv[pi * 2] = dc.x; dCv[pi * 2 + 1] = dc.y;
+                            }
+                            {
+                                const float s1t = s12.x + s12.y;
+                                const float s2t = (GEN && !vld) ? 0.f : s22.x + s22.y;
+                                if constexpr (LPC <= K) {
+                                    // this lane's partial sums of token k, interleaved (S1, S2)
+                                    *reinterpret_cast<float2*>(xmine + 2 * k) = make_float2(s1t, s2t);
+                                } else {
+                                    v[k] = s1t;
+                                    v[K + k] = s2t;
                                 }
                             }
-                            v[k] = s12.x + s12.y;
-                            v[K + k] = (GEN && !vld) ? 0.f : s22.x + s22.y;
                             // dB, dC: sum over the channels of this warp
                             if (ROT) {
-                                float rb = dBv[0], rc = dCv[0];
+                                float2 r2 = make_float2(dBv[0], dCv[0]);
 #pragma unroll
-                                for (int i = 1; i < 4; i++) {
-                                    rb += __shfl_xor_sync(0xffffffffu, dBv[i], LPC * i);
-                                    rc += __shfl_xor_sync(0xffffffffu, dCv[i], LPC * i);
-                                }
+                                for (int i = 1; i < SPT; i++)
+                                    r2 = __fadd2_rn(r2, make_float2(__shfl_xor_sync(0xffffffffu, dBv[i], LPC * i),
+                                                                    __shfl_xor_sync(0xffffffffu, dCv[i], LPC * i)));
 #pragma unroll
-                                for (int m = 4; m < CPW; m *= 2) {
-                                    rb += __shfl_xor_sync(0xffffffffu, rb, LPC * m);
-                                    rc += __shfl_xor_sync(0xffffffffu, rc, LPC * m);
-                                }
-                                if (cw < 4) {
-                                    const int n = g * 4 + cw;
+                                for (int m = SPT; m < CPW; m *= 2)
+                                    r2 = __fadd2_rn(r2, make_float2(__shfl_xor_sync(0xffffffffu, r2.x, LPC * m),
+                                                                    __shfl_xor_sync(0xffffffffu, r2.y, LPC * m)));
+                                if (cw < SPT) {
+                                    const int n = g * SPT + cw;
                                     if (n < N) {
-                                        wslot[n * (TB + 1) + t] = rb;
-                                        wslot[(NS + n) * (TB + 1) + t] = rc;
+                                        wslot[n * (TB + 1) + t] = r2.x;
+                                        wslot[(NS + n) * (TB + 1) + t] = r2.y;
                                     }
                                 }
                             } else {
@@ -502,16 +510,24 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                 *reinterpret_cast<IT*>(odd + out_off(c, t)) = from_f<IT>(ddl);
             };
             if constexpr (LPC <= K) {
-                // S1 of token k sits at index k, S2 at K + k; lane g keeps K/LPC consecutive
-                // tokens of each
+                // each lane stored (S1, S2) of token k at xmine[2k]; the lanes of a channel
+                // swap them through this warp's exchange area and lane g sums the LPC
+                // partials of the RK consecutive tokens g*RK ... and finishes them
                 constexpr int RK = K / LPC;
-                float s1v[K], s2v[K];
+                __syncwarp();
+                float2 sr[RK];
 #pragma unroll
-                for (int k = 0; k < K; k++) { s1v[k] = v[k]; s2v[k] = v[K + k]; }
-                reduce_scatter_contig<LPC, K>(s1v, g);
-                reduce_scatter_contig<LPC, K>(s2v, g);
+                for (int r = 0; r < RK; r++) sr[r] = make_float2(0.f, 0.f);
 #pragma unroll
-                for (int r = 0; r < RK; r++) finish(g * RK + r, s1v[r], s2v[r]);
+                for (int gg = 0; gg < LPC; gg++) {
+                    const float* src = xwarp + ((lane & ~(LPC - 1)) + gg) * (int)S.xch_stride + 2 * g * RK;
+#pragma unroll
+                    for (int r = 0; r < RK; r++)
+                        sr[r] = __fadd2_rn(sr[r], *reinterpret_cast<const float2*>(src + 2 * r));
+                }
+                __syncwarp();
+#pragma unroll
+                for (int r = 0; r < RK; r++) finish(g * RK + r, sr[r].x, sr[r].y);
             } else {
                 reduce_scatter<LPC, V>(v, g);
                 const float other = __shfl_xor_sync(0xffffffffu, v[0], K);
@@ -526,13 +542,18 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
 
         // ---- CTA sum of the warp dB/dC slots -> workspace; store du, ddelta, dz -------------
         const int nw = nthr / 32;
-        for (int i = tid; i < 2 * N * TB; i += nthr) {
-            const int q = i / (N * TB), rem = i % (N * TB), n = rem / TB, t = rem % TB;
+        {
+            // rows r = q * N + n of TB tokens; thread (tid % TB) walks token t of rows tid / TB, ...
+            const int t = tid % TB;
             const int tg = t0 + t;
-            float acc = 0.f;
-            for (int w = 0; w < nw; w++) acc += slots[w * S.slot_stride + (q * NS + n) * (TB + 1) + t];
-            if (tg < Lq)
-                p.ws_bc[((((int64_t)tile_d * p.batch + b) * 2 + q) * N + n) * Lq + tg] = acc;
+            float* dst = p.ws_bc + (((int64_t)tile_d * p.batch + b) * 2) * N * (int64_t)Lq + tg;
+            for (int r = tid / TB; r < 2 * N; r += nthr / TB) {
+                const int q = r >= N ? 1 : 0, n = r - q * N;
+                const float* src = slots + (q * NS + n) * (TB + 1) + t;
+                float acc = 0.f;
+                for (int w = 0; w < nw; w++) acc += src[w * S.slot_stride];
+                if (tg < Lq) dst[(int64_t)r * Lq] = acc;
+            }
         }
         if (p.use_tma) {
             if (tid == 0) {
@@ -620,9 +641,9 @@ template <typename IT, int LPC, int SPT, int K>
 static cudaError_t launch_bwd_t(const BwdParams& p, const CUtensorMap* maps, cudaStream_t stream) {
     auto kern = scan_bwd_kernel<IT, LPC, SPT, K>;
     constexpr int CPW = 32 / LPC;
-    constexpr int NROT = ((CPW >= 4) && (SPT == 4)) ? 4 : 1;
+    constexpr int NROT = ((CPW >= SPT) && (SPT == 2 || SPT == 4)) ? SPT : 1;
     const BwdSmem L = bwd_smem_layout(p.dt, LPC * SPT, p.dstate, sizeof(IT), NROT,
-                                      p.dt * LPC / 32, p.z != nullptr);
+                                      p.dt * LPC / 32, p.z != nullptr, K);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
     if (e != cudaSuccess) return e;
     kern<<<p.batch * p.ntile_d, p.dt * LPC, L.total, stream>>>(p, maps[0], maps[1], maps[2], maps[3],
@@ -631,22 +652,21 @@ static cudaError_t launch_bwd_t(const BwdParams& p, const CUtensorMap* maps, cud
     return cudaGetLastError();
 }
 
-int bwd_occupancy(int is_bf16, int lpc, int dt, int dstate, int has_z) {
+size_t bwd_smem_bytes(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
+
+int bwd_occupancy(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z) {
     const void* k = nullptr;
-    int spt = 4;
 #define SSM_BWD_K(LPC_, SPT_, K_)                                                             \
-    if (lpc == LPC_) {                                                                       \
+    if (lpc == LPC_ && spt == SPT_) {                                                        \
         k = is_bf16 ? (const void*)scan_bwd_kernel<__nv_bfloat16, LPC_, SPT_, K_>            \
                     : (const void*)scan_bwd_kernel<float, LPC_, SPT_, K_>;                   \
-        spt = SPT_;                                                                          \
     }
     SSM_BWD_K(1, 4, 8) SSM_BWD_K(2, 4, 8) SSM_BWD_K(4, 4, 8) SSM_BWD_K(8, 4, 8) SSM_BWD_K(16, 4, 8)
-    SSM_BWD_K(32, 8, 4)
+    SSM_BWD_K(32, 4, 8) SSM_BWD_K(32, 8, 4) SSM_BWD_K(2, 2, 8) SSM_BWD_K(4, 2, 8) SSM_BWD_K(8, 2, 8) SSM_BWD_K(16, 2, 8)
+    SSM_BWD_K(32, 2, 8)
 #undef SSM_BWD_K
     if (!k) return 0;
-    const int cpw = 32 / lpc;
-    const int nrot = (cpw >= 4 && spt == 4) ? 4 : 1;
-    const size_t smem = bwd_smem_layout(dt, lpc * spt, dstate, is_bf16 ? 2 : 4, nrot, dt * lpc / 32, has_z).total;
+    const size_t smem = bwd_smem_bytes(is_bf16, lpc, spt, dt, dstate, has_z);
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, dt * lpc, smem) != cudaSuccess) return 0;
@@ -655,14 +675,15 @@ int bwd_occupancy(int is_bf16, int lpc, int dt, int dstate, int has_z) {
 
 size_t bwd_smem_bytes(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z) {
     const int cpw = 32 / lpc;
-    const int nrot = (cpw >= 4 && spt == 4) ? 4 : 1;
-    return bwd_smem_layout(dt, lpc * spt, dstate, is_bf16 ? 2 : 4, nrot, dt * lpc / 32, has_z).total;
+    const int nrot = (cpw >= spt && (spt == 2 || spt == 4)) ? spt : 1;
+    const int ksub = spt == 8 ? 4 : 8;
+    return bwd_smem_layout(dt, lpc * spt, dstate, is_bf16 ? 2 : 4, nrot, dt * lpc / 32, has_z, ksub).total;
 }
 
-cudaError_t launch_scan_bwd(const BwdParams& p, int is_bf16, int lpc, const CUtensorMap* maps,
+cudaError_t launch_scan_bwd(const BwdParams& p, int is_bf16, int lpc, int spt, const CUtensorMap* maps,
                             cudaStream_t stream) {
 #define SSM_BWD_CASE(LPC_, SPT_, K_)                                                     \
-    if (lpc == LPC_) {                                                                   \
+    if (lpc == LPC_ && spt == SPT_) {                                                    \
         return is_bf16 ? launch_bwd_t<__nv_bfloat16, LPC_, SPT_, K_>(p, maps, stream)    \
                        : launch_bwd_t<float, LPC_, SPT_, K_>(p, maps, stream);           \
     }
@@ -671,7 +692,13 @@ cudaError_t launch_scan_bwd(const BwdParams& p, int is_bf16, int lpc, const CUte
     SSM_BWD_CASE(4, 4, 8)
     SSM_BWD_CASE(8, 4, 8)
     SSM_BWD_CASE(16, 4, 8)
+    SSM_BWD_CASE(32, 4, 8)
     SSM_BWD_CASE(32, 8, 4)
+    SSM_BWD_CASE(2, 2, 8)
+    SSM_BWD_CASE(4, 2, 8)
+    SSM_BWD_CASE(8, 2, 8)
+    SSM_BWD_CASE(16, 2, 8)
+    SSM_BWD_CASE(32, 2, 8)
 #undef SSM_BWD_CASE
     return cudaErrorInvalidValue;
 }

@@ -44,7 +44,7 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     constexpr int Q = NS / 4;                // float4 groups per B/C row
     constexpr int QM = (Q < 8 ? Q : 8) - 1;  // swizzle mask for the f32 B/C rows
     constexpr int RS = T + 4;                // padded row of sD / sDU (floats)
-    static_assert(T % G == 0 && SPT % 4 == 0, "tile must hold whole groups");
+    static_assert(T % G == 0 && (SPT == 2 || SPT % 4 == 0), "tile must hold whole groups");
 
     extern __shared__ __align__(1024) unsigned char smem[];
     if ((smem_u32(smem) & 1023u) != 0u) {  // the swizzled TMA tiles need a 1024-byte base
@@ -155,9 +155,7 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
             float* dst = p.ckpt + (((int64_t)b * p.nck + k) * p.dim + d) * N + g * SPT;
             if (g * SPT + SPT <= N && (N & 3) == 0) {
 #pragma unroll
-                for (int s4 = 0; s4 < SPT; s4 += 4)
-                    *reinterpret_cast<float4*>(dst + s4) =
-                        make_float4(h[s4 / 2].x, h[s4 / 2].y, h[s4 / 2 + 1].x, h[s4 / 2 + 1].y);
+                for (int q = 0; q < NP; q++) *reinterpret_cast<float2*>(dst + 2 * q) = h[q];
             } else {
 #pragma unroll
                 for (int s = 0; s < SPT; s++)
@@ -274,23 +272,16 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
                     const int sw = (sb + j) & QM;
                     const float2 dl2 = make_float2(dls[j], dls[j]);
                     const float2 du2 = make_float2(dus[j], dus[j]);
+                    float2 bp[NP], cp[NP];
+                    load_state_pairs<SPT, NS>(sB, t, g, sw, bp);
+                    load_state_pairs<SPT, NS>(sC, t, g, sw, cp);
                     float2 y2 = make_float2(0.f, 0.f);
 #pragma unroll
-                    for (int s4 = 0; s4 < SPT / 4; s4++) {
-                        const int qq = g * (SPT / 4) + s4;
-                        const int pos = t * NS + ((qq ^ sw) << 2);
-                        const float4 b4 = lds128(sB + pos);
-                        const float4 c4 = lds128(sC + pos);
-                        const float2 bp[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
-                        const float2 cp[2] = {make_float2(c4.x, c4.y), make_float2(c4.z, c4.w)};
-#pragma unroll
-                        for (int k = 0; k < 2; k++) {
-                            const int pi = s4 * 2 + k;
-                            const float2 x = __fmul2_rn(dl2, A2[pi]);
-                            const float2 a = make_float2(ex2(x.x), ex2(x.y));
-                            h[pi] = __ffma2_rn(a, h[pi], __fmul2_rn(du2, bp[k]));
-                            y2 = __ffma2_rn(cp[k], h[pi], y2);
-                        }
+                    for (int pi = 0; pi < NP; pi++) {
+                        const float2 x = __fmul2_rn(dl2, A2[pi]);
+                        const float2 a = make_float2(ex2(x.x), ex2(x.y));
+                        h[pi] = __ffma2_rn(a, h[pi], __fmul2_rn(du2, bp[pi]));
+                        y2 = __ffma2_rn(cp[pi], h[pi], y2);
                     }
                     yv[sb + j] = y2.x + y2.y;
                 }
@@ -405,10 +396,10 @@ static cudaError_t launch_fwd_t(const FwdParams& p, const CUtensorMap* maps, cud
 }
 
 // states-per-thread / lanes-per-channel for a padded state count
-cudaError_t launch_scan_fwd(const FwdParams& p, int is_bf16, int lpc, const CUtensorMap* maps,
+cudaError_t launch_scan_fwd(const FwdParams& p, int is_bf16, int lpc, int spt, const CUtensorMap* maps,
                             cudaStream_t stream) {
 #define SSM_FWD_CASE(LPC_, SPT_)                                                        \
-    if (lpc == LPC_) {                                                                  \
+    if (lpc == LPC_ && spt == SPT_) {                                                   \
         return is_bf16 ? launch_fwd_t<__nv_bfloat16, LPC_, SPT_>(p, maps, stream)       \
                        : launch_fwd_t<float, LPC_, SPT_>(p, maps, stream);              \
     }
@@ -417,22 +408,27 @@ cudaError_t launch_scan_fwd(const FwdParams& p, int is_bf16, int lpc, const CUte
     SSM_FWD_CASE(4, 4)
     SSM_FWD_CASE(8, 4)
     SSM_FWD_CASE(16, 4)
+    SSM_FWD_CASE(32, 4)
     SSM_FWD_CASE(32, 8)
+    SSM_FWD_CASE(2, 2)
+    SSM_FWD_CASE(4, 2)
+    SSM_FWD_CASE(8, 2)
+    SSM_FWD_CASE(16, 2)
+    SSM_FWD_CASE(32, 2)
 #undef SSM_FWD_CASE
     return cudaErrorInvalidValue;
 }
 
 // Resident CTAs per SM for a CTA of dt channels (registers, shared memory, threads).
-int fwd_occupancy(int is_bf16, int lpc, int dt, int has_z, int has_y) {
+int fwd_occupancy(int is_bf16, int lpc, int spt, int dt, int has_z, int has_y) {
     const void* k = nullptr;
-    int spt = 4;
 #define SSM_FWD_K(LPC_, SPT_)                                                                 \
-    if (lpc == LPC_) {                                                                       \
+    if (lpc == LPC_ && spt == SPT_) {                                                        \
         k = is_bf16 ? (const void*)scan_fwd_kernel<__nv_bfloat16, LPC_, SPT_>                \
                     : (const void*)scan_fwd_kernel<float, LPC_, SPT_>;                       \
-        spt = SPT_;                                                                          \
     }
-    SSM_FWD_K(1, 4) SSM_FWD_K(2, 4) SSM_FWD_K(4, 4) SSM_FWD_K(8, 4) SSM_FWD_K(16, 4) SSM_FWD_K(32, 8)
+    SSM_FWD_K(1, 4) SSM_FWD_K(2, 4) SSM_FWD_K(4, 4) SSM_FWD_K(8, 4) SSM_FWD_K(16, 4) SSM_FWD_K(32, 4) SSM_FWD_K(32, 8)
+    SSM_FWD_K(2, 2) SSM_FWD_K(4, 2) SSM_FWD_K(8, 2) SSM_FWD_K(16, 2) SSM_FWD_K(32, 2)
 #undef SSM_FWD_K
     if (!k) return 0;
     const size_t smem = fwd_smem_layout(dt, lpc * spt, is_bf16 ? 2 : 4, has_z, has_y).total;

@@ -41,7 +41,7 @@ __host__ __device__ inline FwdSmem fwd_smem_layout(int dt, int ns, int es, int h
 }
 
 // ---- backward: one raw stage of 32-token tiles, f32 work rows, rotated B/C copies ------
-constexpr int kBwdTile = 32;   // tokens per backward tile
+constexpr int kBwdTile = 16;   // tokens per backward tile
 
 struct BwdSmem {
     uint32_t du, ddelta, dz;                          // output tiles (TMA store, swizzled)
@@ -49,18 +49,20 @@ struct BwdSmem {
     uint32_t sD, sDU, sG, sSP, sU;                    // f32 [dt][TB+4]
     uint32_t sB, sC;                                  // f32 [nrot][TB*ns + 16]
     uint32_t slots;                                   // f32 [nwarps][2][ns][TB+1]
+    uint32_t xch;                                     // f32 [nwarps][32][xch_stride]
     uint32_t bias;                                    // f32 [dt]
     uint32_t bar, total;
     uint32_t rot_stride;                              // floats between rotated copies
     uint32_t slot_stride;                             // floats between warp slots
+    uint32_t xch_stride;                              // floats per lane in the exchange area
 };
 
 __host__ __device__ inline BwdSmem bwd_smem_layout(int dt, int ns, int n, int es, int nrot,
-                                                   int nwarps, int has_z) {
+                                                   int nwarps, int has_z, int ksub) {
     BwdSmem L;
     const int TB = kBwdTile;
     const uint32_t row = (uint32_t)TB * es;               // 64 (bf16) or 128 (f32) bytes
-    const uint32_t otile = align_up((uint32_t)dt * row, 1024u);
+    const uint32_t otile = align_up((uint32_t)dt * row, 512u);
     const uint32_t tile = align_up((uint32_t)dt * row, 128u);
     const uint32_t bc = align_up((uint32_t)n * row, 128u);
     uint32_t o = 0;
@@ -85,6 +87,8 @@ __host__ __device__ inline BwdSmem bwd_smem_layout(int dt, int ns, int n, int es
     L.sC = o; o += align_up((uint32_t)nrot * L.rot_stride * 4u, 128u);
     L.slot_stride = 2u * ns * (TB + 1);
     L.slots = o; o += align_up((uint32_t)nwarps * L.slot_stride * 4u, 128u);
+    L.xch_stride = 2u * ksub + 2u;   // 18 floats for ksub = 8: 8-byte stores by 32 lanes hit 2 wavefronts
+    L.xch = o; o += align_up((uint32_t)nwarps * 32u * L.xch_stride * 4u, 128u);
     L.bias = o; o += align_up((uint32_t)dt * 4u, 16u);
     L.bar = align_up(o, 8u); o = L.bar + 8u;
     L.total = o;

@@ -27,6 +27,17 @@ CASES = [
     (1, 64, 1000, 16, BF16, True, True),
     (1, 32, 257, 16, BF16, False, False),   # bf16 plain-load path
     (3, 40, 192, 16, BF16, True, False),    # channels not a multiple of the CTA tile
+    (1, 8, 96, 100, F32, True, True),       # dstate 100 (padded to 128)
+]
+
+# cases run with each split of the states over a channel's lanes (2 or 4 per thread)
+SPLIT_CASES = [
+    (2, 64, 256, 16, F32, True, True),
+    (2, 128, 512, 16, BF16, True, False),
+    (1, 24, 300, 16, F32, False, True),
+    (1, 24, 136, 17, F32, True, False),
+    (1, 16, 128, 64, BF16, True, True),
+    (1, 8, 64, 4, F32, True, True),
 ]
 
 
@@ -79,6 +90,14 @@ def test_scan_capi_matches_oracle(cuda, case):
     for name in ["du", "ddelta", "dA", "dB", "dC", "dD", "ddelta_bias"] + (["dz"] if with_z else []) + (
             ["dh_init"] if with_h else []):
         assert_grad_close(got[name], g[name], name)
+
+
+@pytest.mark.parametrize("spt", ["2", "4"])
+@pytest.mark.parametrize("case", SPLIT_CASES, ids=_ids)
+def test_scan_state_splits_match_oracle(cuda, case, spt, monkeypatch):
+    monkeypatch.setenv("SSM_FWD_SPT", spt)
+    monkeypatch.setenv("SSM_BWD_SPT", spt)
+    test_scan_capi_matches_oracle(cuda, case)
 
 
 def test_selective_scan_fn_autograd(cuda):
