@@ -75,7 +75,7 @@ def traffic_from_profiles(name):
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -100,7 +100,18 @@ class ClockSampler:
         time.sleep(0.3)
 
     def mark(self, which):
+        """mark("t0") / mark("t1") bracket the timed region; only samples inside it count."""
         setattr(self, which, time.time())
+
+    def _inside(self, stamp):
+        if self.t0 is None or self.t1 is None:
+            return True
+        try:
+            import datetime
+            t = datetime.datetime.strptime(stamp.strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return True
+        return self.t0 - 0.05 <= t <= self.t1 + 0.05
 
     def stop(self):
         if self.proc is None:
@@ -113,13 +124,12 @@ class ClockSampler:
             self.proc.kill()
             out, _ = self.proc.communicate()
         rows = [r.split(", ") for r in out.strip().splitlines() if r.strip()]
-        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
-        smax = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        rows = [r[1:] for r in rows if len(r) >= 10 and self._inside(r[0])] or [r[1:] for r in rows if len(r) >= 10]
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = set()
         for r in rows:
-            if len(r) < 9:
-                continue
             for n, v in zip(names, r[5:9]):
                 if v.strip() == "Active":
                     reasons.add(n)
@@ -258,17 +268,19 @@ def run_ours(args, world, rank, local, pg):
                         True, y, ck, inp.dout, None)
         return ev_mid, out, g
 
+    clocks = ClockSampler(local)
+    clocks.start()
     for _ in range(args.warmup):
         step()
     barrier(pg)
-    clocks = ClockSampler(local)
-    clocks.start()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     mids = []
+    torch.cuda.synchronize()
     barrier(pg)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    clocks.mark("t0")
     t_start.record()
     for i in range(args.steps):
         starts[i].record()
@@ -277,11 +289,14 @@ def run_ours(args, world, rank, local, pg):
         ends[i].record()
     t_end.record()
     torch.cuda.synchronize()
+    clocks.mark("t1")
     barrier(pg)
     clk = clocks.stop()
     elapsed_ms = t_start.elapsed_time(t_end)
-    fwd_ms = statistics.mean(starts[i].elapsed_time(mids[i]) for i in range(args.steps))
-    bwd_ms = statistics.mean(mids[i].elapsed_time(ends[i]) for i in range(args.steps))
+    fwd_each = [starts[i].elapsed_time(mids[i]) for i in range(args.steps)]
+    bwd_each = [mids[i].elapsed_time(ends[i]) for i in range(args.steps)]
+    fwd_ms, bwd_ms = statistics.mean(fwd_each), statistics.mean(bwd_each)
+    step_each = [a + b for a, b in zip(fwd_each, bwd_each)]
     elapsed_ms = max_over_ranks(elapsed_ms, pg)
     total_bytes = (fwd_bytes + bwd_bytes) * args.steps * world
     value = total_bytes / (elapsed_ms / 1e3) / 1e12
@@ -346,6 +361,7 @@ def run_ours(args, world, rank, local, pg):
                    "l2": "inputs larger than L2 (~330 MB read per step)",
                    "frac_of_hbm_peak": value / world * 1e3 / peak},
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+        "step_ms_min_median_max": [min(step_each), statistics.median(step_each), max(step_each)],
         "roofline": {"bound": "hbm", "kernel": "ssm_scan_bwd (scan_bwd_kernel + scan_reduce_kernel)",
                      "achieved": bwd_gbs, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": bwd_gbs / peak, "traffic": traffic_from_profiles("scan_bwd_kernel"),

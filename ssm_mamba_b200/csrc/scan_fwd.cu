@@ -29,6 +29,41 @@
 
 namespace ssm {
 
+// Offset of pipeline stage st (0 or 1) in a two-stage layout array.  A select rather than
+// an index, so the layout struct stays in registers.
+__device__ __forceinline__ uint32_t stage_off(const uint32_t (&a)[2], int st) { return st ? a[1] : a[0]; }
+
+// State checkpoint k of channel d: compact (batch, nck, dim, dstate) fp32 states, or the
+// reference's interleaved (prod, state) chunk carries.  A free function rather than a
+// capturing lambda so that h and A2 stay in registers.
+template <int SPT>
+__device__ __forceinline__ void fwd_write_ckpt(const FwdParams& p, const float2 (&h)[SPT / 2],
+                                               const float2 (&A2)[SPT / 2], float Ssum, int b, int d, int g,
+                                               int k) {
+    const int N = p.dstate;
+    if (p.ckpt_format == 0) {
+        float* dst = p.ckpt + (((int64_t)b * p.nck + k) * p.dim + d) * N + g * SPT;
+        if (g * SPT + SPT <= N && (N & 3) == 0) {
+#pragma unroll
+            for (int q = 0; q < SPT / 2; q++) *reinterpret_cast<float2*>(dst + 2 * q) = h[q];
+        } else {
+#pragma unroll
+            for (int s = 0; s < SPT; s++)
+                if (g * SPT + s < N) dst[s] = (s & 1) ? h[s / 2].y : h[s / 2].x;
+        }
+    } else {
+        float* dst = p.ckpt + (((int64_t)b * p.dim + d) * p.nck + k) * 2 * N;
+#pragma unroll
+        for (int s = 0; s < SPT; s++) {
+            const int n = g * SPT + s;
+            if (n < N) {
+                dst[2 * n] = ex2(((s & 1) ? A2[s / 2].y : A2[s / 2].x) * Ssum);
+                dst[2 * n + 1] = (s & 1) ? h[s / 2].y : h[s / 2].x;
+            }
+        }
+    }
+}
+
 template <typename IT, int LPC, int SPT>
 __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     const __grid_constant__ FwdParams p, const __grid_constant__ CUtensorMap tm_u,
@@ -111,11 +146,11 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     auto issue = [&](int tile, int st) {
         const int t0 = tile * T;
         mbar_arrive_expect_tx(&bar[st], stage_bytes);
-        tma_load_3d(smem + L.u[st], &tm_u, &bar[st], t0, d0, b);
-        tma_load_3d(smem + L.delta[st], &tm_delta, &bar[st], t0, d0, b);
-        if (has_z) tma_load_3d(smem + L.z[st], &tm_z, &bar[st], t0, d0, b);
-        tma_load_3d(smem + L.B[st], &tm_B, &bar[st], t0, 0, b);
-        tma_load_3d(smem + L.C[st], &tm_C, &bar[st], t0, 0, b);
+        tma_load_3d(smem + stage_off(L.u, st), &tm_u, &bar[st], t0, d0, b);
+        tma_load_3d(smem + stage_off(L.delta, st), &tm_delta, &bar[st], t0, d0, b);
+        if (has_z) tma_load_3d(smem + stage_off(L.z, st), &tm_z, &bar[st], t0, d0, b);
+        tma_load_3d(smem + stage_off(L.B, st), &tm_B, &bar[st], t0, 0, b);
+        tma_load_3d(smem + stage_off(L.C, st), &tm_C, &bar[st], t0, 0, b);
     };
 
     // plain-load fallback into the same swizzled layout (zero fill out of range)
@@ -126,12 +161,12 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
             const bool in = dd < p.dim && tg < Lq;
             const uint32_t off = swz128(cc, tt * ES);
             const IT zero = from_f<IT>(0.f);
-            *reinterpret_cast<IT*>(smem + L.u[st] + off) =
+            *reinterpret_cast<IT*>(smem + stage_off(L.u, st) + off) =
                 in ? static_cast<const IT*>(p.u)[b * p.u_sb + dd * p.u_sd + tg] : zero;
-            *reinterpret_cast<IT*>(smem + L.delta[st] + off) =
+            *reinterpret_cast<IT*>(smem + stage_off(L.delta, st) + off) =
                 in ? static_cast<const IT*>(p.delta)[b * p.delta_sb + dd * p.delta_sd + tg] : zero;
             if (has_z)
-                *reinterpret_cast<IT*>(smem + L.z[st] + off) =
+                *reinterpret_cast<IT*>(smem + stage_off(L.z, st) + off) =
                     in ? static_cast<const IT*>(p.z)[b * p.z_sb + dd * p.z_sd + tg] : zero;
         }
         for (int i = tid; i < N * T; i += nthr) {
@@ -139,40 +174,15 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
             const bool in = tg < Lq;
             const uint32_t off = swz128(n, tt * ES);
             const IT zero = from_f<IT>(0.f);
-            *reinterpret_cast<IT*>(smem + L.B[st] + off) =
+            *reinterpret_cast<IT*>(smem + stage_off(L.B, st) + off) =
                 in ? static_cast<const IT*>(p.B)[b * p.B_sb + n * p.B_sn + tg] : zero;
-            *reinterpret_cast<IT*>(smem + L.C[st] + off) =
+            *reinterpret_cast<IT*>(smem + stage_off(L.C, st) + off) =
                 in ? static_cast<const IT*>(p.C)[b * p.C_sb + n * p.C_sn + tg] : zero;
         }
     };
 
     auto hval = [&](int s) -> float { return (s & 1) ? h[s / 2].y : h[s / 2].x; };
     auto aval = [&](int s) -> float { return (s & 1) ? A2[s / 2].y : A2[s / 2].x; };
-
-    auto write_ckpt = [&](int k) {
-        if (!dvalid) return;
-        if (p.ckpt_format == 0) {
-            float* dst = p.ckpt + (((int64_t)b * p.nck + k) * p.dim + d) * N + g * SPT;
-            if (g * SPT + SPT <= N && (N & 3) == 0) {
-#pragma unroll
-                for (int q = 0; q < NP; q++) *reinterpret_cast<float2*>(dst + 2 * q) = h[q];
-            } else {
-#pragma unroll
-                for (int s = 0; s < SPT; s++)
-                    if (g * SPT + s < N) dst[s] = hval(s);
-            }
-        } else {
-            float* dst = p.ckpt + (((int64_t)b * p.dim + d) * p.nck + k) * 2 * N;
-#pragma unroll
-            for (int s = 0; s < SPT; s++) {
-                const int n = g * SPT + s;
-                if (n < N) {
-                    dst[2 * n] = ex2(aval(s) * Ssum);
-                    dst[2 * n + 1] = hval(s);
-                }
-            }
-        }
-    };
 
     if (p.use_tma && tid == 0) {
         mbar_init(&bar[0], 1);
@@ -204,8 +214,8 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
         }
 
         // ---- prologue: 4 tokens of one channel per work item ------------------------------
-        const unsigned char* su = smem + L.u[st];
-        const unsigned char* sdl = smem + L.delta[st];
+        const unsigned char* su = smem + stage_off(L.u, st);
+        const unsigned char* sdl = smem + stage_off(L.delta, st);
         const bool tile_masked = (t0 + T > Lload) || (t0 < mlo) || (t0 + T > mhi);
         for (int i = tid; i < DT * (T / 4); i += nthr) {
             const int cc = i / (T / 4), t4 = (i % (T / 4)) * 4;
@@ -230,8 +240,8 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
             *reinterpret_cast<float4*>(sD + cc * RS + t4) = make_float4(dl[0], dl[1], dl[2], dl[3]);
             *reinterpret_cast<float4*>(sDU + cc * RS + t4) = make_float4(du[0], du[1], du[2], du[3]);
         }
-        const unsigned char* sBr = smem + L.B[st];
-        const unsigned char* sCr = smem + L.C[st];
+        const unsigned char* sBr = smem + stage_off(L.B, st);
+        const unsigned char* sCr = smem + stage_off(L.C, st);
         for (int i = tid; i < Q * T; i += nthr) {
             const int q = i / T, tt = i % T;
             const bool ld = t0 + tt < Lload;
@@ -252,7 +262,7 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
         __syncthreads();
 
         // ---- scan: groups of G tokens, then one reduce-scatter and the epilogue ----------
-        const unsigned char* sz = smem + L.z[st];
+        const unsigned char* sz = smem + stage_off(L.z, st);
         unsigned char* so = smem + L.out;
         unsigned char* sy = smem + L.y;
 #pragma unroll 1
@@ -298,7 +308,7 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
                         if (s & 1) h[s / 2].y = v; else h[s / 2].x = v;
                     }
                 }
-                if (p.ckpt && tg_end <= Lq && (tg_end & ck_mask) == 0) write_ckpt((tg_end >> p.ckpt_shift) - 1);
+                if (p.ckpt && tg_end <= Lq && (tg_end & ck_mask) == 0 && dvalid) fwd_write_ckpt<SPT>(p, h, A2, Ssum, b, d, g, (tg_end >> p.ckpt_shift) - 1);
             }
             // lane g now finishes the RL consecutive tokens q0 + g*RL ...
             reduce_scatter_contig<LPC, G>(yv, g);
@@ -368,7 +378,7 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     }
 
     // the last checkpoint of a sequence whose length is not a multiple of ckpt_len
-    if (p.ckpt && (Lq & ck_mask) != 0) write_ckpt(p.nck - 1);
+    if (p.ckpt && (Lq & ck_mask) != 0 && dvalid) fwd_write_ckpt<SPT>(p, h, A2, Ssum, b, d, g, p.nck - 1);
     if (p.h_last && dvalid) {
 #pragma unroll
         for (int s = 0; s < SPT; s++) {
