@@ -117,7 +117,24 @@ typedef struct ssm_scan_bwd_args {
     float* dD;                     /* may be NULL */
     float* ddelta_bias;            /* may be NULL */
     float* dh_init;                /* may be NULL; written iff h_init != NULL */
+    /* element strides of dB and dC; 0 and 0 mean contiguous (dstate * seqlen, seqlen) */
+    int64_t dB_batch_stride, dB_state_stride;
+    int64_t dC_batch_stride, dC_state_stride;
 } ssm_scan_bwd_args;
+
+/* Folding of per-slice carries (ssm_scan_carry_compose). */
+typedef struct ssm_carry_args {
+    int64_t batch, dim, dstate;
+    int64_t nslices;               /* slices in sequence order */
+    int32_t reverse;               /* 0: states (forward), 1: gradients (backward) */
+    int32_t nstart;                /* number of `start` arrays summed (0 when start is NULL) */
+    const float* A;      int64_t A_dim_stride;
+    const float* carry;  int64_t carry_slice_stride;      /* (nslices, batch, dim, dstate) */
+    const float* delta_sum; int64_t delta_sum_slice_stride; /* (nslices, batch, dim) */
+    const float* start;  int64_t start_stride;            /* nstart x (batch, dim, dstate) */
+    float* result;                 /* forward: (nslices + 1, batch, dim, dstate);
+                                      reverse: (nslices, batch, dim, dstate); contiguous */
+} ssm_carry_args;
 
 typedef struct ssm_state_update_args {
     int64_t batch, dim, dstate;
@@ -188,6 +205,39 @@ SSM_API int ssm_scan_bwd_noalloc(const ssm_scan_bwd_args* args, void* stream);
 
 /* One decode step (replaces selective_update.apply).  state_out may alias state. */
 SSM_API int ssm_state_update(const ssm_state_update_args* args, void* stream);
+
+/* ---- sequence slices ---------------------------------------------------------------------
+ * A long sequence can be scanned as S independent slices -- segments of one GPU's
+ * sequence viewed as a batch of S rows (batch stride = segment length), or the slices the
+ * ranks of a sequence-parallel group hold -- because the recurrence is linear in the state:
+ *   1. ssm_scan_chunk_state_fwd: every slice's end state from a zero start and its sum of
+ *      delta (its decay is exp(A * delta_sum));
+ *   2. ssm_scan_carry_compose (reverse = 0): the state entering every slice;
+ *   3. ssm_scan_fwd per slice with h_init = that state;
+ * and for the backward
+ *   4. ssm_scan_chunk_state_bwd: every slice's gradient into the state before it, from a
+ *      zero incoming gradient;
+ *   5. ssm_scan_carry_compose (reverse = 1): the gradient leaving every slice's end;
+ *   6. ssm_scan_bwd per slice with dh_last = that gradient and h_init from step 2.
+ * None of these has a reference counterpart: the reference scans each sequence serially
+ * (forward_kernel.cu:208-228, backward_kernel.cu:341-366). */
+
+/* Step 1.  Uses u, delta, A, B, delta_bias, delta_softplus and their strides from args;
+ * C, D and z are ignored; out, y, ckpt, h_init, h_last and length must be NULL.
+ * Writes h_end (batch, dim, dstate) and delta_sum (batch, dim), both float32 contiguous. */
+SSM_API int ssm_scan_chunk_state_fwd(const ssm_scan_fwd_args* args, float* h_end, float* delta_sum,
+                                     void* stream);
+
+/* Step 4.  Uses delta, A, C, dout, z, delta_bias, delta_softplus and their strides; u, B,
+ * y, ckpt and the gradient outputs are ignored; length must be NULL.  Writes g_start
+ * (batch, dim, dstate) float32 contiguous. */
+SSM_API int ssm_scan_chunk_state_bwd(const ssm_scan_bwd_args* args, float* g_start, void* stream);
+
+/* Steps 2 and 5.  Forward: result[0] = start (h_init, or 0), result[q + 1] =
+ * exp(A * delta_sum[q]) * result[q] + carry[q] (carry = h_end); result[nslices] is the
+ * final state.  Reverse: result[nslices - 1] = start (dh_last, or 0), result[q - 1] =
+ * exp(A * delta_sum[q]) * result[q] + carry[q] (carry = g_start). */
+SSM_API int ssm_scan_carry_compose(const ssm_carry_args* args, void* stream);
 
 /* Reads and clears the device-side error word of the current device (synchronizes
  * `stream`).  Returns SSM_OK, or SSM_ERR_DEVICE with *code set to the kernel's code. */

@@ -73,6 +73,20 @@ class ScanBwdArgs(ctypes.Structure):
         ("ddelta", _p), ("ddelta_batch_stride", _i64), ("ddelta_dim_stride", _i64),
         ("dz", _p), ("dz_batch_stride", _i64), ("dz_dim_stride", _i64),
         ("dA", _p), ("dB", _p), ("dC", _p), ("dD", _p), ("ddelta_bias", _p), ("dh_init", _p),
+        ("dB_batch_stride", _i64), ("dB_state_stride", _i64),
+        ("dC_batch_stride", _i64), ("dC_state_stride", _i64),
+    ]
+
+
+class CarryArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64), ("dim", _i64), ("dstate", _i64), ("nslices", _i64),
+        ("reverse", _i32), ("nstart", _i32),
+        ("A", _p), ("A_dim_stride", _i64),
+        ("carry", _p), ("carry_slice_stride", _i64),
+        ("delta_sum", _p), ("delta_sum_slice_stride", _i64),
+        ("start", _p), ("start_stride", _i64),
+        ("result", _p),
     ]
 
 
@@ -122,6 +136,12 @@ def lib() -> ctypes.CDLL:
         L.ssm_scan_bwd_noalloc.restype = ctypes.c_int
         L.ssm_state_update.argtypes = [ctypes.POINTER(StateUpdateArgs), _p]
         L.ssm_state_update.restype = ctypes.c_int
+        L.ssm_scan_chunk_state_fwd.argtypes = [ctypes.POINTER(ScanFwdArgs), _p, _p, _p]
+        L.ssm_scan_chunk_state_fwd.restype = ctypes.c_int
+        L.ssm_scan_chunk_state_bwd.argtypes = [ctypes.POINTER(ScanBwdArgs), _p, _p]
+        L.ssm_scan_chunk_state_bwd.restype = ctypes.c_int
+        L.ssm_scan_carry_compose.argtypes = [ctypes.POINTER(CarryArgs), _p]
+        L.ssm_scan_carry_compose.restype = ctypes.c_int
         L.ssm_check_device_error.argtypes = [ctypes.POINTER(ctypes.c_int), _p]
         L.ssm_check_device_error.restype = ctypes.c_int
         _lib = L
@@ -224,6 +244,10 @@ def fill_bwd(u, delta, A, B, C, dout, ckpt, du, ddelta, dA, dB, dC, D=None, z=No
     if dz is not None:
         a.dz, a.dz_batch_stride, a.dz_dim_stride = _t(dz), dz.stride(0), dz.stride(1)
     a.dA, a.dB, a.dC = _t(dA), _t(dB), _t(dC)
+    if dB is not None:
+        a.dB_batch_stride, a.dB_state_stride = dB.stride(0), dB.stride(1)
+    if dC is not None:
+        a.dC_batch_stride, a.dC_state_stride = dC.stride(0), dC.stride(1)
     a.dD, a.ddelta_bias, a.dh_init = _t(dD), _t(ddelta_bias), _t(dh_init)
     return a
 
@@ -277,6 +301,35 @@ def call_update(args: StateUpdateArgs, stream=None):
     _check(lib().ssm_state_update(ctypes.byref(args), stream if stream is not None else _stream()))
 
 
+def call_chunk_state_fwd(args: ScanFwdArgs, h_end, delta_sum, stream=None):
+    """ssm_scan_chunk_state_fwd: end state from a zero start and sum of delta per row."""
+    _check(lib().ssm_scan_chunk_state_fwd(ctypes.byref(args), _t(h_end), _t(delta_sum),
+                                          stream if stream is not None else _stream()))
+
+
+def call_chunk_state_bwd(args: ScanBwdArgs, g_start, stream=None):
+    """ssm_scan_chunk_state_bwd: gradient into the state before each row."""
+    _check(lib().ssm_scan_chunk_state_bwd(ctypes.byref(args), _t(g_start),
+                                          stream if stream is not None else _stream()))
+
+
+def fill_carry(A, carry, delta_sum, result, start=None, reverse=False) -> CarryArgs:
+    a = CarryArgs()
+    a.nslices, a.batch, a.dim, a.dstate = carry.shape
+    a.reverse = int(reverse)
+    a.A, a.A_dim_stride = _t(A), A.stride(0)
+    a.carry, a.carry_slice_stride = _t(carry), carry.stride(0)
+    a.delta_sum, a.delta_sum_slice_stride = _t(delta_sum), delta_sum.stride(0)
+    if start is not None:
+        a.start, a.start_stride, a.nstart = _t(start), start.stride(0), start.shape[0]
+    a.result = _t(result)
+    return a
+
+
+def call_carry_compose(args: CarryArgs, stream=None):
+    _check(lib().ssm_scan_carry_compose(ctypes.byref(args), stream if stream is not None else _stream()))
+
+
 def check_device_error(stream=None) -> int:
     code = ctypes.c_int(0)
     lib().ssm_check_device_error(ctypes.byref(code), stream if stream is not None else _stream())
@@ -285,4 +338,4 @@ def check_device_error(stream=None) -> int:
 
 def struct_sizes() -> Dict[str, int]:
     return {"fwd": ctypes.sizeof(ScanFwdArgs), "bwd": ctypes.sizeof(ScanBwdArgs),
-            "update": ctypes.sizeof(StateUpdateArgs)}
+            "update": ctypes.sizeof(StateUpdateArgs), "carry": ctypes.sizeof(CarryArgs)}

@@ -25,6 +25,10 @@ cudaError_t launch_scan_bwd(const BwdParams& p, int is_bf16, int lpc, int spt, c
                             cudaStream_t stream);
 cudaError_t launch_scan_reduce(const ReduceParams& p, cudaStream_t stream);
 cudaError_t launch_state_update(const UpdParams& p, int is_bf16, int lpc, cudaStream_t stream);
+cudaError_t launch_scan_chunk(const ChunkParams& p, int is_bf16, int lpc, int spt, int reverse,
+                              const CUtensorMap* maps, cudaStream_t stream);
+int chunk_occupancy(int is_bf16, int lpc, int spt, int reverse, int dt, int has_z);
+cudaError_t launch_carry_compose(const CarryParams& p, cudaStream_t stream);
 size_t bwd_smem_bytes(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
 int fwd_occupancy(int is_bf16, int lpc, int spt, int dt, int has_z, int has_y);
 int bwd_occupancy(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
@@ -206,7 +210,7 @@ int cached_dt(DtKey key, int sms, OccFn occ) {
         for (int i = 0; i < g_dt_n; i++)
             if (g_dt_keys[i] == key) return g_dt_vals[i];
     }
-    const int dt = choose_dt(key.batch, key.dim, key.lpc, sms, key.kind == 0 ? 4.0 : 8.0, occ);
+    const int dt = choose_dt(key.batch, key.dim, key.lpc, sms, key.kind == 1 ? 8.0 : 4.0, occ);
     std::lock_guard<std::mutex> lk(g_dt_mu);
     const int slot = g_dt_n < 64 ? g_dt_n++ : (int)(key.dim % 64);
     g_dt_keys[slot] = key;
@@ -488,6 +492,12 @@ int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, i
     r.bc_dtype = is_bf16;
     r.ws_bc = p.ws_bc; r.ws_a = p.ws_a; r.ws_dd = p.ws_dd;
     r.dB = a->dB; r.dC = a->dC; r.dA = a->dA; r.dD = a->dD; r.ddelta_bias = a->ddelta_bias;
+    const bool bc_default = a->dB_batch_stride == 0 && a->dB_state_stride == 0;
+    const bool cc_default = a->dC_batch_stride == 0 && a->dC_state_stride == 0;
+    r.dB_sb = bc_default ? a->dstate * a->seqlen : a->dB_batch_stride;
+    r.dB_sn = bc_default ? a->seqlen : a->dB_state_stride;
+    r.dC_sb = cc_default ? a->dstate * a->seqlen : a->dC_batch_stride;
+    r.dC_sn = cc_default ? a->seqlen : a->dC_state_stride;
     e = launch_scan_reduce(r, stream);
     if (e != cudaSuccess) return cuda_fail(e, "scan_reduce launch");
     return SSM_OK;
@@ -535,6 +545,113 @@ int ssm_state_update(const ssm_state_update_args* a, void* stream_) {
     p.out = a->out; p.out_sb = a->out_batch_stride;
     cudaError_t e = launch_state_update(p, a->dtype == SSM_BF16, sp.lpc, stream);
     if (e != cudaSuccess) return cuda_fail(e, "state_update launch");
+    return SSM_OK;
+}
+
+// ---- sequence slices ------------------------------------------------------------------------
+// Shared launch path of the two chunk-state kernels.  x0 = u (forward) or dout (reverse);
+// bc = B (forward) or C (reverse); z only in reverse.
+static int chunk_impl(const char* name, int reverse, int64_t batch, int64_t dim, int64_t seqlen, int64_t dstate,
+                      int32_t dtype, int32_t softplus, const void* x0, int64_t x0_sb, int64_t x0_sd,
+                      const void* delta, int64_t delta_sb, int64_t delta_sd, const void* z, int64_t z_sb,
+                      int64_t z_sd, const void* bc, int64_t bc_sb, int64_t bc_sn, const float* A, int64_t A_sd,
+                      const float* delta_bias, float* carry, float* delta_sum, cudaStream_t stream) {
+    if (batch < 1 || dim < 1 || seqlen < 1 || dstate < 1)
+        return fail(SSM_ERR_INVALID, "%s: sizes must be positive", name);
+    if (dstate > 256) return fail(SSM_ERR_INVALID, "selective_scan only supports state_dim <= 256");
+    if (seqlen > (1 << 30) || dim > (1 << 30) || batch > (1 << 30))
+        return fail(SSM_ERR_INVALID, "%s: sizes too large", name);
+    if (!valid_dtype(dtype)) return fail(SSM_ERR_INVALID, "%s: dtype must be SSM_F32 or SSM_BF16", name);
+    if (!x0 || !delta || !bc || !A || !carry)
+        return fail(SSM_ERR_INVALID, "%s: a required pointer is NULL", name);
+    const int is_bf16 = dtype == SSM_BF16;
+    const int64_t es = is_bf16 ? 2 : 4;
+    DevInfo* di = nullptr;
+    int rc = device_info(&di);
+    if (rc) return rc;
+    const StateSplit sp = scan_split(dstate, batch * dim, di->sms, "SSM_FWD_SPT");
+    const int has_z = z != nullptr;
+    ChunkParams p;
+    memset(&p, 0, sizeof(p));
+    p.batch = (int)batch; p.dim = (int)dim; p.seqlen = (int)seqlen; p.dstate = (int)dstate;
+    p.delta_softplus = softplus;
+    p.x0 = x0; p.x0_sb = x0_sb; p.x0_sd = x0_sd;
+    p.delta = delta; p.delta_sb = delta_sb; p.delta_sd = delta_sd;
+    p.z = z; p.z_sb = z_sb; p.z_sd = z_sd;
+    p.bc = bc; p.bc_sb = bc_sb; p.bc_sn = bc_sn;
+    p.A = A; p.A_sd = A_sd; p.delta_bias = delta_bias;
+    p.carry = carry; p.delta_sum = delta_sum; p.err = di->err;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    DtKey key;
+    memset(&key, 0, sizeof(key));
+    key.dev = dev; key.kind = 2 + reverse; key.is_bf16 = is_bf16; key.lpc = sp.lpc; key.spt = sp.spt;
+    key.has_z = has_z; key.batch = batch; key.dim = dim;
+    p.dt = cached_dt(key, di->sms, [&](int dt) { return chunk_occupancy(is_bf16, sp.lpc, sp.spt, reverse, dt, has_z); });
+    if (p.dt < 1) return fail(SSM_ERR_INVALID, "%s: no CTA shape fits shared memory", name);
+    p.ntile_d = (int)((dim + p.dt - 1) / p.dt);
+    p.use_tma = tma_ok(x0, x0_sd, x0_sb, es) && tma_ok(delta, delta_sd, delta_sb, es) &&
+                tma_ok(z, z_sd, z_sb, es) && tma_ok(bc, bc_sn, bc_sb, es);
+    CUtensorMap maps[4];
+    memset(maps, 0, sizeof(maps));
+    if (p.use_tma) {
+        if ((rc = get_encoder())) return rc;
+        const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+        const int T = (int)(128 / es);
+        if ((rc = encode3d(&maps[0], x0, is_bf16, seqlen, dim, batch, x0_sd, x0_sb, T, p.dt, sw)) ||
+            (rc = encode3d(&maps[1], delta, is_bf16, seqlen, dim, batch, delta_sd, delta_sb, T, p.dt, sw)) ||
+            (rc = encode3d(&maps[2], z, is_bf16, seqlen, dim, batch, z_sd, z_sb, T, p.dt, sw)) ||
+            (rc = encode3d(&maps[3], bc, is_bf16, seqlen, dstate, batch, bc_sn, bc_sb, T, (int)dstate, sw)))
+            return rc;
+    }
+    cudaError_t e = launch_scan_chunk(p, is_bf16, sp.lpc, sp.spt, reverse, maps, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "scan_chunk launch");
+    return SSM_OK;
+}
+
+int ssm_scan_chunk_state_fwd(const ssm_scan_fwd_args* a, float* h_end, float* delta_sum, void* stream) {
+    if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_chunk_state_fwd: args is NULL");
+    if (a->out || a->y || a->ckpt || a->h_init || a->h_last || a->length)
+        return fail(SSM_ERR_INVALID, "ssm_scan_chunk_state_fwd: out, y, ckpt, h_init, h_last and length must be NULL");
+    if (!h_end || !delta_sum) return fail(SSM_ERR_INVALID, "ssm_scan_chunk_state_fwd: h_end and delta_sum are required");
+    return chunk_impl("ssm_scan_chunk_state_fwd", 0, a->batch, a->dim, a->seqlen, a->dstate, a->dtype,
+                      a->delta_softplus, a->u, a->u_batch_stride, a->u_dim_stride, a->delta,
+                      a->delta_batch_stride, a->delta_dim_stride, nullptr, 0, 0, a->B, a->B_batch_stride,
+                      a->B_state_stride, a->A, a->A_dim_stride, a->delta_bias, h_end, delta_sum,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int ssm_scan_chunk_state_bwd(const ssm_scan_bwd_args* a, float* g_start, void* stream) {
+    if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_chunk_state_bwd: args is NULL");
+    if (a->length) return fail(SSM_ERR_INVALID, "ssm_scan_chunk_state_bwd: length must be NULL");
+    if (!g_start) return fail(SSM_ERR_INVALID, "ssm_scan_chunk_state_bwd: g_start is required");
+    return chunk_impl("ssm_scan_chunk_state_bwd", 1, a->batch, a->dim, a->seqlen, a->dstate, a->dtype,
+                      a->delta_softplus, a->dout, a->dout_batch_stride, a->dout_dim_stride, a->delta,
+                      a->delta_batch_stride, a->delta_dim_stride, a->z, a->z_batch_stride, a->z_dim_stride, a->C,
+                      a->C_batch_stride, a->C_state_stride, a->A, a->A_dim_stride, a->delta_bias, g_start, nullptr,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int ssm_scan_carry_compose(const ssm_carry_args* a, void* stream) {
+    if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_carry_compose: args is NULL");
+    if (a->batch < 1 || a->dim < 1 || a->dstate < 1 || a->nslices < 1 || a->nslices > (1 << 20))
+        return fail(SSM_ERR_INVALID, "ssm_scan_carry_compose: sizes must be positive");
+    if (a->batch * a->dim * a->dstate >= (int64_t(1) << 40))
+        return fail(SSM_ERR_INVALID, "ssm_scan_carry_compose: sizes too large");
+    if (!a->A || !a->carry || !a->delta_sum || !a->result)
+        return fail(SSM_ERR_INVALID, "ssm_scan_carry_compose: A, carry, delta_sum and result are required");
+    if (a->start && a->nstart < 1) return fail(SSM_ERR_INVALID, "ssm_scan_carry_compose: nstart must be >= 1 with start");
+    CarryParams p;
+    memset(&p, 0, sizeof(p));
+    p.batch = (int)a->batch; p.dim = (int)a->dim; p.dstate = (int)a->dstate; p.nslices = (int)a->nslices;
+    p.reverse = a->reverse != 0;
+    p.A = a->A; p.A_sd = a->A_dim_stride;
+    p.carry = a->carry; p.carry_ss = a->carry_slice_stride;
+    p.delta_sum = a->delta_sum; p.dsum_ss = a->delta_sum_slice_stride;
+    p.start = a->start; p.start_ss = a->start_stride; p.nstart = a->start ? a->nstart : 0;
+    p.result = a->result;
+    cudaError_t e = launch_carry_compose(p, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "carry_compose launch");
     return SSM_OK;
 }
 

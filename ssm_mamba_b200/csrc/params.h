@@ -73,7 +73,35 @@ struct ReduceParams {
     int bc_dtype;        // 0 f32, 1 bf16
     const float* ws_bc; const float* ws_a; const float* ws_dd;
     void* dB; void* dC;
+    int64_t dB_sb, dB_sn, dC_sb, dC_sn;   // element strides of dB, dC
     float* dA; float* dD; float* ddelta_bias;
+};
+
+// Sequence-slice carries: the state a slice reaches from a zero start (forward) or the
+// gradient it sends back to the state before it (reverse).
+struct ChunkParams {
+    int batch, dim, seqlen, dstate;
+    int dt, ntile_d;
+    int use_tma;
+    int delta_softplus;
+    const void* x0; int64_t x0_sb, x0_sd;   // forward: u; reverse: dout
+    const void* delta; int64_t delta_sb, delta_sd;
+    const void* z; int64_t z_sb, z_sd;      // reverse only, may be null
+    const void* bc; int64_t bc_sb, bc_sn;   // forward: B; reverse: C
+    const float* A; int64_t A_sd;
+    const float* delta_bias;
+    float* carry;        // (batch, dim, dstate): h_end (forward) or g_start (reverse)
+    float* delta_sum;    // (batch, dim): sum of the effective delta (forward only, may be null)
+    int* err;
+};
+
+struct CarryParams {
+    int batch, dim, dstate, nslices, reverse;
+    const float* A; int64_t A_sd;
+    const float* carry; int64_t carry_ss;
+    const float* delta_sum; int64_t dsum_ss;
+    const float* start; int64_t start_ss; int nstart;
+    float* result;       // forward: (nslices + 1, batch, dim, dstate); reverse: (nslices, ...)
 };
 
 struct UpdParams {

@@ -612,10 +612,13 @@ __global__ void scan_reduce_kernel(const __grid_constant__ ReduceParams p) {
             for (int tile = 0; tile < p.ntile_d; tile++)
                 acc += p.ws_bc[(((int64_t)tile * p.batch + b) * 2 + q) * p.dstate * p.seqlen + nt];
             void* dst = q == 0 ? p.dB : p.dC;
+            const int64_t sb = q == 0 ? p.dB_sb : p.dC_sb, sn = q == 0 ? p.dB_sn : p.dC_sn;
+            const int64_t n = nt / p.seqlen, t = nt - n * p.seqlen;
+            const int64_t o = b * sb + n * sn + t;
             if (p.bc_dtype == 1)
-                static_cast<__nv_bfloat16*>(dst)[r] = __float2bfloat16_rn(acc);
+                static_cast<__nv_bfloat16*>(dst)[o] = __float2bfloat16_rn(acc);
             else
-                static_cast<float*>(dst)[r] = acc;
+                static_cast<float*>(dst)[o] = acc;
         } else if (i < 2 * nbc + na) {
             const int64_t r = i - 2 * nbc;             // (d, n)
             float acc = 0.f;

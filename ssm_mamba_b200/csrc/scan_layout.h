@@ -40,6 +40,36 @@ __host__ __device__ inline FwdSmem fwd_smem_layout(int dt, int ns, int es, int h
     return L;
 }
 
+// ---- sequence-slice carries (scan_chunk.cu): 2 raw stages, f32 work rows ---------------
+// forward: raw tiles x0 = u, x1 = delta, x3 = B (state rows);
+// reverse: raw tiles x0 = dout, x1 = delta, x2 = z (optional), x3 = C (state rows).
+struct ChunkSmem {
+    uint32_t x0[2], x1[2], x2[2], x3[2];
+    uint32_t sD, sX, sM, bias, bar, total;
+};
+
+__host__ __device__ inline ChunkSmem chunk_smem_layout(int dt, int ns, int es, int has_z) {
+    ChunkSmem L;
+    const int T = 128 / es;
+    const uint32_t tile = align_up((uint32_t)dt * 128u, 1024u);
+    const uint32_t bc = align_up((uint32_t)ns * 128u, 1024u);
+    uint32_t o = 0;
+    for (int s = 0; s < 2; s++) {
+        L.x0[s] = o; o += tile;
+        L.x1[s] = o; o += tile;
+        L.x2[s] = o; o += has_z ? tile : 0u;
+        L.x3[s] = o; o += bc;
+    }
+    const uint32_t rows = align_up((uint32_t)dt * (T + 4) * 4u, 128u);
+    L.sD = o; o += rows;
+    L.sX = o; o += rows;
+    L.sM = o; o += (uint32_t)T * ns * 4u;
+    L.bias = o; o += align_up((uint32_t)dt * 4u, 16u);
+    L.bar = align_up(o, 8u); o = L.bar + 16u;
+    L.total = o;
+    return L;
+}
+
 // ---- backward: one raw stage of 32-token tiles, f32 work rows, rotated B/C copies ------
 constexpr int kBwdTile = 16;   // tokens per backward tile
 

@@ -118,24 +118,25 @@ ssm_scan_fwd_args fwd_args(const Common& c, const at::Tensor& u, const at::Tenso
     return a;
 }
 
-// Forward.  ckpt_mode: 0 none, 1 compact (for ssm_scan_bwd), 2 reference layout.
+// Forward into given out (and y) tensors, which may be strided views (unit innermost
+// stride).  ckpt_mode: 0 none, 1 compact (for ssm_scan_bwd), 2 reference layout.
 // Returns [out, y or undefined, ckpt or undefined, h_last or undefined].
-std::vector<at::Tensor> scan_fwd(const at::Tensor& u, const at::Tensor& delta, const at::Tensor& A,
-                                 const at::Tensor& Bm, const at::Tensor& Cm, const std::optional<at::Tensor>& D,
-                                 const std::optional<at::Tensor>& z, const std::optional<at::Tensor>& delta_bias,
-                                 const std::optional<at::Tensor>& h_init, const std::optional<at::Tensor>& length,
-                                 bool padding_right, bool delta_softplus, bool want_y, int64_t ckpt_mode,
-                                 bool want_h_last) {
+std::vector<at::Tensor> scan_fwd_out(const at::Tensor& u, const at::Tensor& delta, const at::Tensor& A,
+                                     const at::Tensor& Bm, const at::Tensor& Cm, const std::optional<at::Tensor>& D,
+                                     const std::optional<at::Tensor>& z, const std::optional<at::Tensor>& delta_bias,
+                                     const std::optional<at::Tensor>& h_init, const std::optional<at::Tensor>& length,
+                                     bool padding_right, bool delta_softplus, const at::Tensor& out,
+                                     const std::optional<at::Tensor>& y, int64_t ckpt_mode, bool want_h_last) {
     Common c = check_inputs(u, delta, A, Bm, Cm, D, z, delta_bias, h_init, length);
     c10::cuda::CUDAGuard guard(u.device());
     ssm_scan_fwd_args a = fwd_args(c, u, delta, A, Bm, Cm, D, z, delta_bias, h_init, length, padding_right,
                                    delta_softplus);
-    at::Tensor out = at::empty({c.B, c.D, c.L}, u.options());
-    at::Tensor y, ck, hl;
+    check_bdl(out, "out", c.B, c.D, c.L, u.scalar_type());
+    at::Tensor ck, hl;
     a.out = out.data_ptr(); a.out_batch_stride = out.stride(0); a.out_dim_stride = out.stride(1);
-    if (want_y) {
-        y = at::empty({c.B, c.D, c.L}, u.options());
-        a.y = y.data_ptr(); a.y_batch_stride = y.stride(0); a.y_dim_stride = y.stride(1);
+    if (y) {
+        check_bdl(*y, "y", c.B, c.D, c.L, u.scalar_type());
+        a.y = y->data_ptr(); a.y_batch_stride = y->stride(0); a.y_dim_stride = y->stride(1);
     }
     const auto f32 = u.options().dtype(at::kFloat);
     if (ckpt_mode == 1) {
@@ -151,7 +152,22 @@ std::vector<at::Tensor> scan_fwd(const at::Tensor& u, const at::Tensor& delta, c
         a.h_last = hl.data_ptr<float>();
     }
     ok(ssm_scan_fwd(&a, at::cuda::getCurrentCUDAStream().stream()));
-    return {out, y, ck, hl};
+    return {out, y ? *y : at::Tensor(), ck, hl};
+}
+
+std::vector<at::Tensor> scan_fwd(const at::Tensor& u, const at::Tensor& delta, const at::Tensor& A,
+                                 const at::Tensor& Bm, const at::Tensor& Cm, const std::optional<at::Tensor>& D,
+                                 const std::optional<at::Tensor>& z, const std::optional<at::Tensor>& delta_bias,
+                                 const std::optional<at::Tensor>& h_init, const std::optional<at::Tensor>& length,
+                                 bool padding_right, bool delta_softplus, bool want_y, int64_t ckpt_mode,
+                                 bool want_h_last) {
+    check_cuda(u, "u");
+    TORCH_CHECK(u.dim() == 3, "u must be a 3D tensor");
+    at::Tensor out = at::empty(u.sizes(), u.options());
+    std::optional<at::Tensor> y;
+    if (want_y) y = at::empty(u.sizes(), u.options());
+    return scan_fwd_out(u, delta, A, Bm, Cm, D, z, delta_bias, h_init, length, padding_right, delta_softplus, out,
+                        y, ckpt_mode, want_h_last);
 }
 
 // Compact checkpoints rebuilt from the reference-layout chunk states.
@@ -173,14 +189,17 @@ at::Tensor ckpt_from_reference(const at::Tensor& u, const at::Tensor& delta, con
     return ck;
 }
 
-// Backward.  Returns [du, ddelta, dA, dB, dC, dD?, ddelta_bias?, dz?, dh_init?].
-std::vector<at::Tensor> scan_bwd(const at::Tensor& u, const at::Tensor& delta, const at::Tensor& A,
-                                 const at::Tensor& Bm, const at::Tensor& Cm, const std::optional<at::Tensor>& D,
-                                 const std::optional<at::Tensor>& z, const std::optional<at::Tensor>& delta_bias,
-                                 const std::optional<at::Tensor>& h_init, const std::optional<at::Tensor>& length,
-                                 bool padding_right, bool delta_softplus, const std::optional<at::Tensor>& y,
-                                 const at::Tensor& ckpt, const at::Tensor& dout,
-                                 const std::optional<at::Tensor>& dh_last) {
+// Backward into given du, ddelta, dB, dC (and dz) tensors, which may be strided views
+// (unit innermost stride).  Returns [du, ddelta, dA, dB, dC, dD?, ddelta_bias?, dz?, dh_init?].
+std::vector<at::Tensor> scan_bwd_out(const at::Tensor& u, const at::Tensor& delta, const at::Tensor& A,
+                                     const at::Tensor& Bm, const at::Tensor& Cm, const std::optional<at::Tensor>& D,
+                                     const std::optional<at::Tensor>& z, const std::optional<at::Tensor>& delta_bias,
+                                     const std::optional<at::Tensor>& h_init, const std::optional<at::Tensor>& length,
+                                     bool padding_right, bool delta_softplus, const std::optional<at::Tensor>& y,
+                                     const at::Tensor& ckpt, const at::Tensor& dout,
+                                     const std::optional<at::Tensor>& dh_last, const at::Tensor& du,
+                                     const at::Tensor& ddelta, const at::Tensor& dB, const at::Tensor& dC,
+                                     const std::optional<at::Tensor>& dz_out) {
     Common c = check_inputs(u, delta, A, Bm, Cm, D, z, delta_bias, h_init, length);
     c10::cuda::CUDAGuard guard(u.device());
     check_bdl(dout, "dout", c.B, c.D, c.L, u.scalar_type());
@@ -214,21 +233,32 @@ std::vector<at::Tensor> scan_bwd(const at::Tensor& u, const at::Tensor& delta, c
     a.ckpt = ckpt.data_ptr<float>(); a.ckpt_format = SSM_CKPT_COMPACT; a.ckpt_len = k;
     a.dout = dout.data_ptr(); a.dout_batch_stride = dout.stride(0); a.dout_dim_stride = dout.stride(1);
     a.dh_last = ptr<const float>(dh_last);
-    at::Tensor du = at::empty({c.B, c.D, c.L}, u.options());
-    at::Tensor ddelta = at::empty({c.B, c.D, c.L}, u.options());
+    check_bdl(du, "du", c.B, c.D, c.L, u.scalar_type());
+    check_bdl(ddelta, "ddelta", c.B, c.D, c.L, u.scalar_type());
+    for (auto* t : {&dB, &dC}) {
+        check_cuda(*t, "dB/dC");
+        TORCH_CHECK(t->dim() == 3 && t->size(0) == c.B && t->size(1) == c.N && t->size(2) == c.L &&
+                        t->stride(2) == 1 && t->scalar_type() == u.scalar_type(),
+                    "dB and dC must have shape (batch, state_dim, seq_len), unit sequence stride");
+    }
     at::Tensor dA = at::empty({c.D, c.N}, A.options());
-    at::Tensor dB = at::empty({c.B, c.N, c.L}, u.options());
-    at::Tensor dC = at::empty({c.B, c.N, c.L}, u.options());
     const auto f32 = u.options().dtype(at::kFloat);
     at::Tensor dD = D ? at::empty({c.D}, f32) : at::Tensor();
     at::Tensor dbias = delta_bias ? at::empty({c.D}, f32) : at::Tensor();
-    at::Tensor dz = z ? at::empty({c.B, c.D, c.L}, u.options()) : at::Tensor();
+    at::Tensor dz;
+    if (z) {
+        TORCH_CHECK(dz_out.has_value(), "dz is needed when z is given");
+        dz = *dz_out;
+        check_bdl(dz, "dz", c.B, c.D, c.L, u.scalar_type());
+    }
     at::Tensor dh_init = h_init ? at::empty({c.B, c.D, c.N}, f32) : at::Tensor();
     a.du = du.data_ptr(); a.du_batch_stride = du.stride(0); a.du_dim_stride = du.stride(1);
     a.ddelta = ddelta.data_ptr(); a.ddelta_batch_stride = ddelta.stride(0); a.ddelta_dim_stride = ddelta.stride(1);
     if (z) { a.dz = dz.data_ptr(); a.dz_batch_stride = dz.stride(0); a.dz_dim_stride = dz.stride(1); }
     a.dA = dA.data_ptr<float>();
     a.dB = dB.data_ptr(); a.dC = dC.data_ptr();
+    a.dB_batch_stride = dB.stride(0); a.dB_state_stride = dB.stride(1);
+    a.dC_batch_stride = dC.stride(0); a.dC_state_stride = dC.stride(1);
     a.dD = D ? dD.data_ptr<float>() : nullptr;
     a.ddelta_bias = delta_bias ? dbias.data_ptr<float>() : nullptr;
     a.dh_init = h_init ? dh_init.data_ptr<float>() : nullptr;
@@ -237,6 +267,99 @@ std::vector<at::Tensor> scan_bwd(const at::Tensor& u, const at::Tensor& delta, c
     at::Tensor ws = at::empty({(int64_t)ws_bytes}, u.options().dtype(at::kByte));
     ok(ssm_scan_bwd(&a, ws.data_ptr(), ws_bytes, at::cuda::getCurrentCUDAStream().stream()));
     return {du, ddelta, dA, dB, dC, dD, dbias, dz, dh_init};
+}
+
+std::vector<at::Tensor> scan_bwd(const at::Tensor& u, const at::Tensor& delta, const at::Tensor& A,
+                                 const at::Tensor& Bm, const at::Tensor& Cm, const std::optional<at::Tensor>& D,
+                                 const std::optional<at::Tensor>& z, const std::optional<at::Tensor>& delta_bias,
+                                 const std::optional<at::Tensor>& h_init, const std::optional<at::Tensor>& length,
+                                 bool padding_right, bool delta_softplus, const std::optional<at::Tensor>& y,
+                                 const at::Tensor& ckpt, const at::Tensor& dout,
+                                 const std::optional<at::Tensor>& dh_last) {
+    check_cuda(u, "u");
+    TORCH_CHECK(u.dim() == 3, "u must be a 3D tensor");
+    at::Tensor du = at::empty(u.sizes(), u.options());
+    at::Tensor ddelta = at::empty(u.sizes(), u.options());
+    at::Tensor dB = at::empty(Bm.sizes(), u.options());
+    at::Tensor dC = at::empty(Cm.sizes(), u.options());
+    std::optional<at::Tensor> dz;
+    if (z) dz = at::empty(u.sizes(), u.options());
+    return scan_bwd_out(u, delta, A, Bm, Cm, D, z, delta_bias, h_init, length, padding_right, delta_softplus, y,
+                        ckpt, dout, dh_last, du, ddelta, dB, dC, dz);
+}
+
+// Sequence slices: end state from a zero start and sum of delta of every row.
+std::vector<at::Tensor> chunk_state_fwd(const at::Tensor& u, const at::Tensor& delta, const at::Tensor& A,
+                                        const at::Tensor& Bm, const std::optional<at::Tensor>& delta_bias,
+                                        bool delta_softplus) {
+    Common c = check_inputs(u, delta, A, Bm, Bm, std::nullopt, std::nullopt, delta_bias, std::nullopt,
+                            std::nullopt);
+    c10::cuda::CUDAGuard guard(u.device());
+    ssm_scan_fwd_args a = fwd_args(c, u, delta, A, Bm, Bm, std::nullopt, std::nullopt, delta_bias, std::nullopt,
+                                   std::nullopt, true, delta_softplus);
+    const auto f32 = u.options().dtype(at::kFloat);
+    at::Tensor h_end = at::empty({c.B, c.D, c.N}, f32);
+    at::Tensor dsum = at::empty({c.B, c.D}, f32);
+    ok(ssm_scan_chunk_state_fwd(&a, h_end.data_ptr<float>(), dsum.data_ptr<float>(),
+                                at::cuda::getCurrentCUDAStream().stream()));
+    return {h_end, dsum};
+}
+
+// Sequence slices: gradient into the state before every row, from a zero incoming gradient.
+at::Tensor chunk_state_bwd(const at::Tensor& delta, const at::Tensor& A, const at::Tensor& Cm,
+                           const std::optional<at::Tensor>& z, const std::optional<at::Tensor>& delta_bias,
+                           bool delta_softplus, const at::Tensor& dout) {
+    Common c = check_inputs(delta, delta, A, Cm, Cm, std::nullopt, z, delta_bias, std::nullopt, std::nullopt);
+    c10::cuda::CUDAGuard guard(delta.device());
+    check_bdl(dout, "dout", c.B, c.D, c.L, delta.scalar_type());
+    ssm_scan_bwd_args a;
+    memset(&a, 0, sizeof(a));
+    a.batch = c.B; a.dim = c.D; a.seqlen = c.L; a.dstate = c.N; a.dtype = c.dt;
+    a.delta_softplus = delta_softplus;
+    a.delta = delta.data_ptr(); a.delta_batch_stride = delta.stride(0); a.delta_dim_stride = delta.stride(1);
+    a.A = A.data_ptr<float>(); a.A_dim_stride = A.stride(0);
+    a.C = Cm.data_ptr(); a.C_batch_stride = Cm.stride(0); a.C_state_stride = Cm.stride(1);
+    if (z) { a.z = z->data_ptr(); a.z_batch_stride = z->stride(0); a.z_dim_stride = z->stride(1); }
+    a.delta_bias = ptr<const float>(delta_bias);
+    a.dout = dout.data_ptr(); a.dout_batch_stride = dout.stride(0); a.dout_dim_stride = dout.stride(1);
+    at::Tensor g = at::empty({c.B, c.D, c.N}, delta.options().dtype(at::kFloat));
+    ok(ssm_scan_chunk_state_bwd(&a, g.data_ptr<float>(), at::cuda::getCurrentCUDAStream().stream()));
+    return g;
+}
+
+// Sequence slices: fold per-slice carries.  carry (S, batch, dim, N) with any slice stride,
+// delta_sum (S, batch, dim); start: (R, batch, dim, N) summed over R, or None.
+at::Tensor carry_compose(const at::Tensor& A, const at::Tensor& carry, const at::Tensor& delta_sum,
+                         const std::optional<at::Tensor>& start, bool reverse) {
+    check_cuda(carry, "carry");
+    TORCH_CHECK(carry.dim() == 4 && carry.scalar_type() == at::kFloat, "carry must be float32 (S, batch, dim, N)");
+    const int64_t S = carry.size(0), Bs = carry.size(1), Dm = carry.size(2), N = carry.size(3);
+    TORCH_CHECK(carry[0].is_contiguous(), "each carry slice must be contiguous");
+    TORCH_CHECK(delta_sum.is_cuda() && delta_sum.scalar_type() == at::kFloat && delta_sum.dim() == 3 &&
+                    delta_sum.size(0) == S && delta_sum.size(1) == Bs && delta_sum.size(2) == Dm &&
+                    delta_sum[0].is_contiguous(),
+                "delta_sum must be float32 (S, batch, dim)");
+    TORCH_CHECK(A.is_cuda() && A.scalar_type() == at::kFloat && A.dim() == 2 && A.size(0) == Dm && A.size(1) == N &&
+                    A.stride(1) == 1,
+                "A must be float32 (dim, N)");
+    c10::cuda::CUDAGuard guard(carry.device());
+    ssm_carry_args a;
+    memset(&a, 0, sizeof(a));
+    a.batch = Bs; a.dim = Dm; a.dstate = N; a.nslices = S; a.reverse = reverse;
+    a.A = A.data_ptr<float>(); a.A_dim_stride = A.stride(0);
+    a.carry = carry.data_ptr<float>(); a.carry_slice_stride = carry.stride(0);
+    a.delta_sum = delta_sum.data_ptr<float>(); a.delta_sum_slice_stride = delta_sum.stride(0);
+    if (start) {
+        TORCH_CHECK(start->is_cuda() && start->scalar_type() == at::kFloat && start->dim() == 4 &&
+                        start->size(1) == Bs && start->size(2) == Dm && start->size(3) == N &&
+                        (*start)[0].is_contiguous(),
+                    "start must be float32 (R, batch, dim, N)");
+        a.start = start->data_ptr<float>(); a.start_stride = start->stride(0); a.nstart = (int32_t)start->size(0);
+    }
+    at::Tensor result = at::empty({reverse ? S : S + 1, Bs, Dm, N}, carry.options());
+    a.result = result.data_ptr<float>();
+    ok(ssm_scan_carry_compose(&a, at::cuda::getCurrentCUDAStream().stream()));
+    return result;
 }
 
 // One decode step; writes state_out (may be the same tensor as state) and returns out.
@@ -305,6 +428,11 @@ PYBIND11_MODULE(_C, m) {
     m.doc() = "torch binding of the ssm_b200 C ABI";
     m.def("scan_fwd", &scan_fwd, "selective scan forward");
     m.def("scan_bwd", &scan_bwd, "selective scan backward");
+    m.def("scan_fwd_out", &scan_fwd_out, "selective scan forward into given outputs");
+    m.def("scan_bwd_out", &scan_bwd_out, "selective scan backward into given outputs");
+    m.def("chunk_state_fwd", &chunk_state_fwd, "per-row end state from a zero start, and sum of delta");
+    m.def("chunk_state_bwd", &chunk_state_bwd, "per-row gradient into the preceding state");
+    m.def("carry_compose", &carry_compose, "fold per-slice carries");
     m.def("ckpt_from_reference", &ckpt_from_reference, "compact checkpoints from reference chunk states");
     m.def("state_update", &state_update, "one decode step");
     m.def("ckpt_len", [](int64_t n) { return ssm_scan_ckpt_len(n); });

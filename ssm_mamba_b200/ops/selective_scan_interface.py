@@ -20,6 +20,7 @@ from typing import Optional, Tuple
 import torch
 
 from .._ext import _C
+from ..slices import plan_segments, sliced_scan
 
 
 def ensure_contiguous(x: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
@@ -35,7 +36,36 @@ def _padding_right(padding_size: Optional[str]) -> bool:
     return padding_size is None or padding_size == "right"
 
 
-class SelectiveScanFn(torch.autograd.Function):
+def _segments_for(u: torch.Tensor, N: int) -> int:
+    """Segments for a scan of u on its GPU (see slices.plan_segments)."""
+    if not u.is_cuda:
+        return 1
+    sms = torch.cuda.get_device_properties(u.device).multi_processor_count
+    return plan_segments(u.shape[0], u.shape[1], u.shape[2], N, sms=sms)
+
+
+class SelectiveScanFn:
+    """Reference-compatible selective scan (ops/selective_scan_interface.py:7-80).
+
+    SelectiveScanFn.apply(u, A, B, C, D, delta, delta_bias, h_init=None, length=None,
+                          padding_size="left") -> (out, h_last)
+
+    Dispatches to one autograd function: a batch-1 sequence too narrow to fill the GPU and
+    without `length` is scanned as segments (slices.SlicedScanFn, same results); every
+    other call runs _SelectiveScanRefFn below."""
+
+    @staticmethod
+    def apply(u, A, B, C, D, delta, delta_bias, h_init=None, length=None, padding_size: Optional[str] = "left"):
+        if length is None:
+            S = _segments_for(u, A.shape[1])
+            if S > 1:
+                u, A, B, C, D, delta, delta_bias, h_init = map(
+                    ensure_contiguous, (u, A, B, C, D, delta, delta_bias, h_init))
+                return sliced_scan(u, delta, A, B, C, D, None, delta_bias, h_init, True, segments=S)
+        return _SelectiveScanRefFn.apply(u, A, B, C, D, delta, delta_bias, h_init, length, padding_size)
+
+
+class _SelectiveScanRefFn(torch.autograd.Function):
     """Reference-compatible selective scan (ops/selective_scan_interface.py:7-80).
 
     Args:
@@ -154,6 +184,10 @@ def selective_scan_fn(u: torch.Tensor, delta: torch.Tensor, A: torch.Tensor, B: 
     delta_bias = delta_bias.float() if delta_bias is not None else None
     u, delta, A, B, C, D, z, delta_bias = map(
         ensure_contiguous, (u, delta, A, B, C, D, z, delta_bias))
+    S = _segments_for(u, A.shape[1])
+    if S > 1:
+        out, h_last = sliced_scan(u, delta, A, B, C, D, z, delta_bias, None, bool(delta_softplus), segments=S)
+        return (out, h_last) if return_last_state else out
     return _SelectiveScanExt.apply(u, delta, A, B, C, D, z, delta_bias, delta_softplus,
                                    return_last_state)
 

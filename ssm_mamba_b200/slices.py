@@ -1,0 +1,229 @@
+"""Selective scan of long sequences as independent slices.
+
+A sequence can be cut into slices that are scanned at the same time, because the
+recurrence h_t = exp(delta_t A) h_{t-1} + delta_t u_t B_t is linear in the state: a slice
+q started from the state h_in(q) ends in P_q h_in(q) + h0_end(q), where h0_end(q) is its end
+state from a zero start and P_q = exp(A * sum(delta over the slice)).  Two uses:
+
+* segments on one GPU -- a batch-1 sequence with few channels (the long-sequence config:
+  batch 1, d_inner 5120) gives the scan kernels one CTA per 32 channels, too few to fill
+  148 SMs; viewed as S segments of length L/S (a (S, dim, L/S) view with batch stride
+  L/S, no copy) it gives S times more CTAs;
+* sequence parallelism -- the ranks of a process group each hold a contiguous slice of the
+  sequence (and may segment it further); the per-slice carries cross GPUs with one NCCL
+  all_gather per direction.
+
+Forward: chunk_state_fwd (end states and delta sums of every local slice) -> all_gather ->
+carry_compose (the state entering every slice, and the final state) -> the ordinary forward
+of every slice with that h_init.  Backward: chunk_state_bwd (every slice's gradient into
+the state before it) -> all_gather -> carry_compose in reverse (the gradient leaving every
+slice) -> the ordinary backward of every slice with that dh_last -> all_reduce of the
+parameter gradients dA, dD, ddelta_bias across ranks.
+
+No reference counterpart: the reference scans every sequence serially in 128-token
+chunks inside one CTA (csrc/selective_scan/forward_kernel.cu:208-228,
+backward_kernel.cu:341-366); the math of each slice is unchanged.
+"""
+from __future__ import annotations
+
+import os
+from typing import Optional
+
+import torch
+
+from ._ext import _C
+
+# The scan kernels run 3 CTAs of 128 threads per SM; segmenting stops once the rows give
+# this many full waves of them.  Measured on B200, long-sequence config (batch 1, d_inner
+# 5120, seqlen 131072, bf16, fwd+bwd): 1 segment 54.0 ms, 2: 43.3, 4: 39.1, 8: 33.7,
+# 16: 32.4 -- the gain continues to ~5-6 waves.
+_CTAS_PER_SM = 3
+_TARGET_WAVES = 4
+
+
+def plan_segments(batch: int, dim: int, seqlen: int, dstate: int, sms: int = 148,
+                  min_segment: int = 1024) -> int:
+    """Number of segments (a power of two) to split a sequence into on one GPU: 1 unless
+    batch == 1 and batch * dim rows leave the SMs short of warps.  Every segment is a
+    multiple of 128 tokens and at least `min_segment` long.  SSM_SEGMENTS overrides."""
+    env = os.environ.get("SSM_SEGMENTS")
+    if env:
+        s = int(env)
+        return s if s >= 1 and seqlen % (s * 128) == 0 else 1
+    if batch != 1:
+        return 1
+    ns = 4
+    while ns < dstate:
+        ns *= 2
+    lanes = max(ns // 4, 1)  # lanes per channel at 4 states per thread
+    rows_needed = sms * _CTAS_PER_SM * (128 // lanes) * _TARGET_WAVES
+    s = 1
+    while s * dim < rows_needed and seqlen % (2 * s * 128) == 0 and seqlen // (2 * s) >= min_segment:
+        s *= 2
+    return s
+
+
+def segment_view(t: Optional[torch.Tensor], s: int) -> Optional[torch.Tensor]:
+    """(1, X, L) contiguous -> (s, X, L // s) view with batch stride L // s; s == 1: t."""
+    if t is None or s == 1:
+        return t
+    _, x, L = t.shape
+    return t.as_strided((s, x, L // s), (L // s, L, 1), t.storage_offset())
+
+
+class SliceGroup:
+    """The ranks that share one sequence (rank r holds the r-th contiguous slice), or a
+    single process (world 1, no communication)."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.group = group
+        if group is None:
+            self.world, self.rank = 1, 0
+        else:
+            self.world = dist.get_world_size(group)
+            self.rank = dist.get_rank(group)
+
+    def all_gather(self, t: torch.Tensor) -> torch.Tensor:
+        """(world, *t.shape): every rank's t, in rank order."""
+        if self.world == 1:
+            return t.unsqueeze(0)
+        import torch.distributed as dist
+        t = t.contiguous()
+        out = t.new_empty((self.world,) + tuple(t.shape))
+        if dist.get_backend(self.group) == "nccl":
+            dist.all_gather_into_tensor(out, t, group=self.group)
+        else:
+            dist.all_gather(list(out.unbind(0)), t, group=self.group)
+        return out
+
+    def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(t, group=self.group)
+        return t
+
+
+class _Kernels:
+    """The native entry points the slice orchestration calls (the torch binding of the C
+    ABI: ssm_scan_chunk_state_fwd / _bwd, ssm_scan_carry_compose, ssm_scan_fwd,
+    ssm_scan_bwd)."""
+
+    chunk_state_fwd = staticmethod(_C.chunk_state_fwd)
+    chunk_state_bwd = staticmethod(_C.chunk_state_bwd)
+    carry_compose = staticmethod(_C.carry_compose)
+    scan_fwd_out = staticmethod(_C.scan_fwd_out)
+    scan_bwd_out = staticmethod(_C.scan_bwd_out)
+    ckpt_len = staticmethod(_C.ckpt_len)
+
+
+KERNELS = _Kernels()
+
+
+class SlicedScanFn(torch.autograd.Function):
+    """Selective scan of this rank's slice of a sequence, cut into `segments` local
+    segments (batch must be 1 when segments > 1).  Returns (out, h_final) where h_final is
+    the state after the LAST token of the whole sequence (the same on every rank).
+
+    Gradients are those of the sum of every rank's objective: dA, dD and ddelta_bias are
+    summed over ranks (every rank gets the total), dh_final is summed over ranks, and the
+    gradient of h_init (the state before the first token of rank 0's slice) is returned on
+    rank 0 and zero on the other ranks."""
+
+    @staticmethod
+    def forward(ctx, u, delta, A, B, C, D, z, delta_bias, h_init, delta_softplus, segments, group, kernels):
+        k = kernels
+        S = int(segments)
+        Bt, Dm, L = u.shape
+        N = A.shape[1]
+        if S > 1 and (Bt != 1 or L % S != 0):
+            raise ValueError("segmented scan needs batch 1 and seqlen divisible by the segment count")
+        Bc = Bt if S == 1 else 1            # batch of one slice
+        rows = Bt if S == 1 else S          # rows of the segmented views
+        sv = lambda t: segment_view(t, S)  # noqa: E731
+        u_s, d_s, B_s, C_s, z_s = sv(u), sv(delta), sv(B), sv(C), sv(z)
+
+        # 1. every local slice from a zero start: end state and delta sum
+        h0, dsum = k.chunk_state_fwd(u_s, d_s, A, B_s, delta_bias, bool(delta_softplus))
+        per = Bc * Dm * N
+        pack = torch.cat([h0.reshape(S, per), dsum.reshape(S, Bc * Dm)], dim=1)   # (S, per + Bc*Dm)
+        # 2. carries of every slice of the sequence, in order
+        allp = group.all_gather(pack).reshape(group.world * S, per + Bc * Dm)
+        M = group.world * S
+        carry = allp[:, :per].unflatten(1, (Bc, Dm, N))     # slice stride per + Bc*Dm
+        dsum_all = allp[:, per:].unflatten(1, (Bc, Dm))
+        start = h_init.reshape(1, Bc, Dm, N) if h_init is not None else None
+        carries = k.carry_compose(A, carry, dsum_all, start, False)                # (M + 1, Bc, Dm, N)
+        r = group.rank
+        h_in = carries[r * S:(r + 1) * S].reshape(rows, Dm, N)
+        h_final = carries[M].reshape(Bc, Dm, N)
+        # 3. the ordinary forward of every slice from its own initial state
+        need_grad = any(ctx.needs_input_grad[:9])
+        out = torch.empty_like(u)
+        y = torch.empty_like(u) if (need_grad and z is not None) else None
+        _, _, ckpt, _ = k.scan_fwd_out(u_s, d_s, A, B_s, C_s, D, z_s, delta_bias, h_in, None, True,
+                                       bool(delta_softplus), sv(out), sv(y), 1 if need_grad else 0, False)
+        if need_grad:
+            ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, y, ckpt, h_in, dsum_all, h_init)
+            ctx.cfg = (bool(delta_softplus), S, group, k, Bc, rows)
+        return out, h_final
+
+    @staticmethod
+    def backward(ctx, dout, dh_final):
+        u, delta, A, B, C, D, z, delta_bias, y, ckpt, h_in, dsum_all, h_init = ctx.saved_tensors
+        softplus, S, group, k, Bc, rows = ctx.cfg
+        Bt, Dm, L = u.shape
+        N = A.shape[1]
+        M = group.world * S
+        sv = lambda t: segment_view(t, S)  # noqa: E731
+        dout = dout.contiguous()
+        u_s, d_s, B_s, C_s, z_s, dout_s = sv(u), sv(delta), sv(B), sv(C), sv(z), sv(dout)
+        # 1. every local slice's gradient into the state before it, from a zero start
+        g0 = k.chunk_state_bwd(d_s, A, C_s, z_s, delta_bias, softplus, dout_s)     # (rows, Dm, N)
+        per = Bc * Dm * N
+        if dh_final is None:
+            dh_final = torch.zeros(Bc, Dm, N, device=u.device, dtype=g0.dtype)
+        pack = torch.cat([g0.reshape(S * per), dh_final.reshape(per).to(g0.dtype)])
+        allp = group.all_gather(pack)                                                # (world, (S + 1) * per)
+        g_all = allp[:, :S * per].reshape(M, Bc, Dm, N)
+        dhf_all = allp[:, S * per:].reshape(group.world, Bc, Dm, N)
+        # 2. the gradient leaving every slice's end
+        gout = k.carry_compose(A, g_all, dsum_all, dhf_all, True)                   # (M, Bc, Dm, N)
+        r = group.rank
+        dh_last = gout[r * S:(r + 1) * S].reshape(rows, Dm, N)
+        # 3. the ordinary backward of every slice
+        du, ddelta = torch.empty_like(u), torch.empty_like(u)
+        dB, dC = torch.empty_like(B), torch.empty_like(C)
+        dz = torch.empty_like(u) if z is not None else None
+        res = k.scan_bwd_out(u_s, d_s, A, B_s, C_s, D, z_s, delta_bias, h_in, None, True, softplus, sv(y),
+                             ckpt, dout_s, dh_last, sv(du), sv(ddelta), sv(dB), sv(dC), sv(dz))
+        dA, dD, ddb, dh_rows = res[2], res[5], res[6], res[8]
+        # 4. parameter gradients are sums over the whole sequence
+        if group.world > 1:
+            parts = [dA.reshape(-1)] + [t for t in (dD, ddb) if t is not None and t.numel()]
+            flat = group.all_reduce_(torch.cat(parts))
+            dA = flat[:dA.numel()].view_as(dA)
+            o = dA.numel()
+            if dD is not None and dD.numel():
+                dD = flat[o:o + Dm]
+                o += Dm
+            if ddb is not None and ddb.numel():
+                ddb = flat[o:o + Dm]
+        dh_init = None
+        if h_init is not None:
+            dh_init = dh_rows[:Bc].reshape_as(h_init) if r == 0 else torch.zeros_like(h_init)
+        return (du, ddelta, dA, dB, dC, dD if D is not None else None, dz,
+                ddb if delta_bias is not None else None, dh_init, None, None, None, None)
+
+
+def sliced_scan(u, delta, A, B, C, D=None, z=None, delta_bias=None, h_init=None, delta_softplus=False,
+                segments: int = 1, group=None, kernels=None):
+    """Selective scan of this rank's contiguous slice of a sequence (the whole sequence
+    when `group` is None), cut into `segments` segments; returns (out, h_final).
+    Tensors as for selective_scan_fn with B, C of shape (batch, dstate, seqlen)."""
+    g = group if isinstance(group, SliceGroup) else SliceGroup(group)
+    return SlicedScanFn.apply(u, delta, A, B, C, D, z, delta_bias, h_init, delta_softplus, segments, g,
+                              kernels if kernels is not None else KERNELS)
+
+
+__all__ = ["plan_segments", "segment_view", "SliceGroup", "SlicedScanFn", "sliced_scan", "KERNELS"]

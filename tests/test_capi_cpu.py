@@ -31,8 +31,11 @@ def test_struct_layout_matches_header(tmp_path):
     """Compile a probe against the header and compare sizeof/offsetof with ctypes."""
     src = tmp_path / "probe.c"
     fields = {"ssm_scan_fwd_args": ("ScanFwdArgs", ["u", "B", "ckpt", "ckpt_len", "h_last"]),
-              "ssm_scan_bwd_args": ("ScanBwdArgs", ["y", "ckpt_len", "dout", "dz", "dh_init"]),
-              "ssm_state_update_args": ("StateUpdateArgs", ["state", "x", "z", "out"])}
+              "ssm_scan_bwd_args": ("ScanBwdArgs", ["y", "ckpt_len", "dout", "dz", "dh_init",
+                                                    "dB_batch_stride", "dC_state_stride"]),
+              "ssm_state_update_args": ("StateUpdateArgs", ["state", "x", "z", "out"]),
+              "ssm_carry_args": ("CarryArgs", ["reverse", "nstart", "A", "carry", "delta_sum", "start",
+                                               "start_stride", "result"])}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "ssm_b200.h"', "int main(void){"]
     for cs, (_, fl) in fields.items():
         lines.append(f'printf("{cs} %zu\\n", sizeof({cs}));')
@@ -72,6 +75,19 @@ def test_validation_errors_without_gpu():
     u.batch, u.dim, u.dstate, u.dtype = 1, 1, 16, 7
     assert lib.ssm_state_update(ctypes.byref(u), None) == capi.SSM_ERR_INVALID
     assert b"dtype" in lib.ssm_last_error()
+    # sequence-slice entry points validate before touching a device
+    f = capi.ScanFwdArgs()
+    f.batch, f.dim, f.seqlen, f.dstate = 1, 1, 1, 16
+    f.out = 1  # any non-NULL output is refused
+    assert lib.ssm_scan_chunk_state_fwd(ctypes.byref(f), None, None, None) == capi.SSM_ERR_INVALID
+    assert b"must be NULL" in lib.ssm_last_error()
+    b = capi.ScanBwdArgs()
+    b.batch, b.dim, b.seqlen, b.dstate = 1, 1, 1, 16
+    assert lib.ssm_scan_chunk_state_bwd(ctypes.byref(b), None, None) == capi.SSM_ERR_INVALID
+    c = capi.CarryArgs()
+    c.batch, c.dim, c.dstate, c.nslices = 1, 1, 16, 0
+    assert lib.ssm_scan_carry_compose(ctypes.byref(c), None) == capi.SSM_ERR_INVALID
+    assert b"positive" in lib.ssm_last_error()
 
 
 def test_torch_binding_imports():
