@@ -38,6 +38,7 @@ sys.path.insert(0, ROOT)
 
 CFG2 = dict(batch=8, dim=1536, seqlen=2048, dstate=16)
 CFG3 = dict(batch=64, dim=5120, dstate=16, steps=1024, layers=8)
+CFG5 = dict(dim=5120, seqlen=131072, dstate=16)
 
 
 def scan_bytes(batch, dim, seqlen, dstate, es=2):
@@ -247,6 +248,53 @@ def run_decode(args, world, rank, local, pg, peak):
                       "one CUDA graph, state rotated over 8 layer buffers"}
 
 
+def run_long_seq(args, world, rank, local, pg, peak):
+    """Config 5: one sequence of 131072 tokens (batch 1, d_inner 5120, d_state 16, bf16, z
+    gate), forward + backward through the public API.  One GPU scans it as segments; N GPUs
+    hold N contiguous slices (each segmented further) and exchange the slice carries with one
+    NCCL all_gather per direction plus an all_reduce of dA/dD/ddelta_bias (strong scaling:
+    the total work is fixed)."""
+    import torch
+    from ssm_mamba_b200.slices import SliceGroup, plan_segments, sliced_scan
+    from ssm_mamba_b200.workloads import scan_inputs
+    dev = torch.device("cuda", local)
+    Ltot, Dm, N = CFG5["seqlen"], CFG5["dim"], CFG5["dstate"]
+    Lr = Ltot // world
+    inp = scan_inputs(1, Dm, Lr, N, torch.bfloat16, seed=4 + rank, device=dev, with_z=True)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    S = plan_segments(1, Dm, Lr, N, sms=sms)
+    group = SliceGroup(pg.group.WORLD if pg is not None else None)
+    leaves = [t.clone().requires_grad_() for t in (inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, inp.z,
+                                                   inp.delta_bias)]
+
+    def step():
+        out, _ = sliced_scan(*leaves, None, True, segments=S, group=group)
+        out.backward(inp.dout)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    barrier(pg)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = 3
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(pg)
+    ms = max_over_ranks(e0.elapsed_time(e1), pg) / steps
+    fb, bb = scan_bytes(1, Dm, Ltot, N)
+    tbs = (fb + bb) / (ms / 1e3) / 1e12
+    return {"metric": "long-sequence scan fwd+bwd achieved HBM TB/s", "value": tbs, "unit": "TB/s",
+            "ms_per_step": ms, "steps": steps, "scaling": "strong", "segments_per_rank": S,
+            "elem_state_per_s": 1 * Dm * Ltot * N / (ms / 1e3),
+            "frac_of_hbm_peak": tbs * 1e3 / world / peak,
+            "gpu_launches_per_step": 8,
+            "config": f"config 5: batch 1, d_inner {Dm}, seqlen {Ltot} ({world} slice(s) of {Lr}), d_state {N}, "
+                      "bf16, z gate, softplus; sequence-parallel carries over NCCL when n_gpus > 1"}
+
+
 def run_ours(args, world, rank, local, pg):
     import torch
     from ssm_mamba_b200._ext import _C
@@ -343,6 +391,7 @@ def run_ours(args, world, rank, local, pg):
                "api": "ssm_mamba_b200.selective_scan_fn forward + autograd backward"}
 
     decode = None if args.no_decode else run_decode(args, world, rank, local, pg, peak)
+    long_seq = None if args.no_long else run_long_seq(args, world, rank, local, pg, peak)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -369,7 +418,8 @@ def run_ours(args, world, rank, local, pg):
         "roofline_fwd": {"bound": "hbm", "kernel": "scan_fwd_kernel", "achieved": fwd_gbs, "peak": peak,
                          "unit": "GB/s", "frac": fwd_gbs / peak, "traffic": traffic_from_profiles("scan_fwd_kernel"),
                          "algorithmic_bytes_per_launch": fwd_bytes},
-        "e2e": e2e, "gpu_launches": 3 * args.steps, "clocks": clk, "decode": decode, "cpu_baseline": cpu,
+        "e2e": e2e, "gpu_launches": 3 * args.steps, "clocks": clk, "decode": decode, "long_seq": long_seq,
+        "cpu_baseline": cpu,
     }
     return line
 
@@ -460,6 +510,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ref-cuda", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-long", action="store_true", help="skip the long-sequence (config 5) measurement")
     ap.add_argument("--decode-only", action="store_true", help="profiling aid: only the decode loop")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
