@@ -92,13 +92,22 @@ class ClockSampler:
         self.ident = ident
 
     def start(self):
+        """Starts sampling and returns once the first sample has arrived, so that the
+        sampler's own start-up (NVML initialisation, which was seen to stall a timed step
+        by several ms) is over before any timing begins."""
+        self.first = []
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "--query-gpu=" + self.QUERY, "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", self.ident], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
-        time.sleep(0.3)
+            return
+        import select
+        ready, _, _ = select.select([self.proc.stdout], [], [], 10.0)
+        if ready:
+            self.first.append(self.proc.stdout.readline())
+        time.sleep(0.2)
 
     def mark(self, which):
         """mark("t0") / mark("t1") bracket the timed region; only samples inside it count."""
@@ -124,7 +133,7 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
             out, _ = self.proc.communicate()
-        rows = [r.split(", ") for r in out.strip().splitlines() if r.strip()]
+        rows = [r.split(", ") for r in (self.first + out.strip().splitlines()) if r.strip()]
         rows = [r[1:] for r in rows if len(r) >= 10 and self._inside(r[0])] or [r[1:] for r in rows if len(r) >= 10]
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
@@ -295,6 +304,87 @@ def run_long_seq(args, world, rank, local, pg, peak):
                       "bf16, z gate, softplus; sequence-parallel carries over NCCL when n_gpus > 1"}
 
 
+EQ_SCAN = {"cfg1": (2, 64, 256, 0), "cfg2": (8, 1536, 2048, 1), "cfg5": (1, 5120, 131072, 4)}
+
+
+def _time_steps(step, warmup, steps):
+    import torch
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def _decode_graph_us(apply_fn, dev, seed=2):
+    """us per decode step of an out-of-place update (the reference's semantics:
+    selective_update.cpp:208-209) over 8 rotating layer states (168 MB > L2), 256 steps in
+    one CUDA graph; float32 (config 3 shape)."""
+    import torch
+    from ssm_mamba_b200.workloads import decode_inputs
+    Bd, Dd, Nd, Ly = CFG3["batch"], CFG3["dim"], CFG3["dstate"], CFG3["layers"]
+    S = 256
+    dec = decode_inputs(Bd, Dd, Nd, S, torch.float32, seed=seed, device=dev)
+    states = [dec.state.clone() for _ in range(Ly)]
+
+    def loop():
+        for s in range(S):
+            _, states[s % Ly] = apply_fn(dec.x[s], dec.A, dec.B[s], dec.C[s], dec.D, dec.dt[s], dec.dt_bias,
+                                         states[s % Ly])
+
+    loop()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        loop()
+    ms = _time_steps(g.replay, 2, 3)
+    del g
+    return ms * 1e3 / S
+
+
+def run_equal_precision(dev, forward_backward, update_apply):
+    """The float32 workloads the reference's kernels support (no z gate, softplus on),
+    timed through a reference-shaped API: `forward_backward(inputs)` runs one forward and
+    backward, `update_apply` one out-of-place decode step.  Same shapes and seeds in both
+    arms of bench.py."""
+    import torch
+    from ssm_mamba_b200.workloads import scan_inputs
+    res = {}
+    for name, (Bs, Dm, L, seed) in EQ_SCAN.items():
+        inp = scan_inputs(Bs, Dm, L, 16, torch.float32, seed=seed, device=dev, with_z=False)
+        ms = _time_steps(lambda: forward_backward(inp), 2, 3 if L > 100000 else 10)
+        fb, bb = scan_bytes(Bs, Dm, L, 16, es=4)
+        fb -= Bs * Dm * L * 4       # no z stream
+        bb -= 2 * Bs * Dm * L * 4   # no z read, no dz written
+        res[name] = {"shape": [Bs, Dm, L, 16], "ms_per_fwd_bwd": ms, "fp32_tb_s": (fb + bb) / (ms / 1e3) / 1e12}
+        del inp
+        torch.cuda.empty_cache()
+    try:
+        res["cfg3_decode"] = {"us_per_step": _decode_graph_us(update_apply, dev), "mode": "CUDA graph"}
+    except Exception as e:  # noqa: BLE001 - context only
+        res["cfg3_decode"] = {"error": str(e)[:200]}
+    return res
+
+
+def _ours_fwd_bwd(inp):
+    from ssm_mamba_b200 import SelectiveScanFn
+    leaves = [t.requires_grad_() for t in (inp.u, inp.A, inp.B, inp.C, inp.D, inp.delta, inp.delta_bias)]
+    out, _ = SelectiveScanFn.apply(*leaves)
+    out.backward(inp.dout)
+    for t in leaves:
+        t.grad = None
+
+
+def _ours_update(x, A, B, C, D, dt, bias, h):
+    from ssm_mamba_b200 import SelectiveUpdateFn
+    return SelectiveUpdateFn.apply(x, A, B, C, D, dt, bias, h)
+
+
 def run_ours(args, world, rank, local, pg):
     import torch
     from ssm_mamba_b200._ext import _C
@@ -351,44 +441,75 @@ def run_ours(args, world, rank, local, pg):
     peak, peak_kind = measured_peaks()
 
     # ---- end to end through the public API: pinned host inputs in, gradients out -------
+    # Every step copies its inputs from pinned host memory and its input gradients back.
+    # The copies run on their own streams, double-buffered, so step i's host->device copy
+    # and step i-1's device->host copy overlap step i's compute (a data pipeline would do
+    # the same); the timed region covers all copies of all steps.
     e2e = None
-    e2e_steps = min(args.steps, 10)
-    if args.no_e2e:
-        e2e_steps = 0
+    e2e_steps = 0 if args.no_e2e else min(args.steps, 20)
     f = lambda t: t.detach().to("cpu").pin_memory()  # noqa: E731
     host_in = {k: f(getattr(inp, k)) for k in ("u", "delta", "z", "B", "C", "dout")}
     A = inp.A.clone().requires_grad_()
     Dp = inp.D.clone().requires_grad_()
     bias = inp.delta_bias.clone().requires_grad_()
-    host_out = {k: torch.empty(host_in[k].shape, dtype=host_in[k].dtype).pin_memory()
-                for k in ("u", "delta", "z", "B", "C")}
+    grad_keys = ("u", "delta", "z", "B", "C")
+    NBUF = 2
+    host_out = [{k: torch.empty(host_in[k].shape, dtype=host_in[k].dtype).pin_memory() for k in grad_keys}
+                for _ in range(NBUF)]
+    dev_in = [{k: torch.empty(v.shape, dtype=v.dtype, device=dev) for k, v in host_in.items()}
+              for _ in range(NBUF)]
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    comp = torch.cuda.current_stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(NBUF)]
+    in_free = [torch.cuda.Event() for _ in range(NBUF)]
+    used = [False] * NBUF
 
-    def e2e_step():
-        d = {k: v.to(dev, non_blocking=True) for k, v in host_in.items()}
-        leaves = {k: d[k].requires_grad_() for k in ("u", "delta", "z", "B", "C")}
+    def e2e_step(i):
+        b = i % NBUF
+        with torch.cuda.stream(s_in):
+            if used[b]:
+                s_in.wait_event(in_free[b])          # the compute that read this buffer is done
+            for k, v in host_in.items():
+                dev_in[b][k].copy_(v, non_blocking=True)
+            in_ready[b].record(s_in)
+        comp.wait_event(in_ready[b])
+        d = dev_in[b]
+        leaves = {k: d[k].detach().requires_grad_() for k in grad_keys}
         o = selective_scan_fn(leaves["u"], leaves["delta"], A, leaves["B"].unsqueeze(1),
                               leaves["C"].unsqueeze(1), Dp, leaves["z"], bias, delta_softplus=True)
         o.backward(d["dout"])
-        for k in host_out:
-            host_out[k].copy_(leaves[k].grad, non_blocking=True)
+        in_free[b].record(comp)
+        used[b] = True
+        s_out.wait_stream(comp)
+        with torch.cuda.stream(s_out):
+            for k in grad_keys:
+                g = leaves[k].grad
+                host_out[b][k].copy_(g, non_blocking=True)
+                g.record_stream(s_out)
 
     if e2e_steps:
-        for _ in range(3):
-            e2e_step()
+        for i in range(3):
+            e2e_step(i)
+        torch.cuda.synchronize()
         barrier(pg)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(e2e_steps):
-            e2e_step()
-        e1.record()
+        e0.record(comp)
+        s_in.wait_event(e0)
+        s_out.wait_event(e0)
+        for i in range(e2e_steps):
+            e2e_step(i)
+        comp.wait_stream(s_out)
+        e1.record(comp)
         torch.cuda.synchronize()
         barrier(pg)
         e2e_ms = max_over_ranks(e0.elapsed_time(e1), pg)
         h2d = sum(v.numel() * v.element_size() for v in host_in.values())
-        d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+        d2h = sum(v.numel() * v.element_size() for v in host_out[0].values())
         e2e = {"value": (fwd_bytes + bwd_bytes) * e2e_steps * world / (e2e_ms / 1e3) / 1e12, "unit": "TB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / e2e_steps,
-               "api": "ssm_mamba_b200.selective_scan_fn forward + autograd backward"}
+               "steps": e2e_steps,
+               "api": "ssm_mamba_b200.selective_scan_fn forward + autograd backward; copies double-buffered "
+                      "on separate streams"}
 
     decode = None if args.no_decode else run_decode(args, world, rank, local, pg, peak)
     long_seq = None if args.no_long else run_long_seq(args, world, rank, local, pg, peak)
@@ -396,6 +517,10 @@ def run_ours(args, world, rank, local, pg):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline_sample(target_s=args.cpu_seconds)
+    eq = None
+    if world == 1 and not args.no_fp32:
+        eq = run_equal_precision(dev, _ours_fwd_bwd, _ours_update)
+        eq["api"] = "ssm_mamba_b200.SelectiveScanFn / SelectiveUpdateFn (the reference's signatures)"
 
     bwd_gbs = bwd_bytes / (bwd_ms / 1e3) / 1e9
     fwd_gbs = fwd_bytes / (fwd_ms / 1e3) / 1e9
@@ -411,6 +536,7 @@ def run_ours(args, world, rank, local, pg):
                    "frac_of_hbm_peak": value / world * 1e3 / peak},
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
         "step_ms_min_median_max": [min(step_each), statistics.median(step_each), max(step_each)],
+        "slow_steps": [i for i, v in enumerate(step_each) if v > 1.5 * statistics.median(step_each)][:10],
         "roofline": {"bound": "hbm", "kernel": "ssm_scan_bwd (scan_bwd_kernel + scan_reduce_kernel)",
                      "achieved": bwd_gbs, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": bwd_gbs / peak, "traffic": traffic_from_profiles("scan_bwd_kernel"),
@@ -419,7 +545,7 @@ def run_ours(args, world, rank, local, pg):
                          "unit": "GB/s", "frac": fwd_gbs / peak, "traffic": traffic_from_profiles("scan_fwd_kernel"),
                          "algorithmic_bytes_per_launch": fwd_bytes},
         "e2e": e2e, "gpu_launches": 3 * args.steps, "clocks": clk, "decode": decode, "long_seq": long_seq,
-        "cpu_baseline": cpu,
+        "cpu_baseline": cpu, "fp32_equal_precision": eq,
     }
     return line
 
@@ -466,35 +592,46 @@ def run_reference(args, world, rank, local, pg):
                                    "C restatement of its kernels, float32, OpenMP)"},
         "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    # the reference's own CUDA kernels (float32 only), same config-2 shape, for context
+    # the reference's own CUDA kernels (float32 only) on the GPU, same shapes as the float32
+    # set of the other arm, through its pybind functions (what its SelectiveScanFn calls)
     try:
         import build_ref
         if torch.cuda.is_available() and build_ref.available() and not args.no_ref_cuda:
             ref = build_ref.load("ref_selective_scan")
+            ref_up = build_ref.load("ref_selective_update")
             dev = torch.device("cuda", local)
-            g = scan_inputs(CFG2["batch"], CFG2["dim"], L, N, torch.float32, seed=1, device=dev, with_z=False)
-            dh = torch.zeros(CFG2["batch"], CFG2["dim"], N, device=dev)
 
-            def rstep():
-                out, h = ref.forward(g.u, g.A, g.B, g.C, g.D, g.delta, g.delta_bias, None, None, "right")
-                ref.backward(g.u, g.A, g.B, g.C, g.D, g.delta, g.delta_bias, h, None, g.dout, dh, None, "right")
+            class RefScanFn(torch.autograd.Function):
+                """Autograd over the reference's pybind functions, as the reference's
+                SelectiveScanFn does (ops/selective_scan_interface.py:9-80): the forward
+                returns (out, final state), the backward passes dout and the final state's
+                gradient back.  Written here because the reference's Python files are not on
+                the GPU box; both arms thus pay the same autograd overhead."""
 
-            for _ in range(2):
-                rstep()
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            n = 3
-            e0.record()
-            for _ in range(n):
-                rstep()
-            e1.record()
-            torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / n
-            fb2, bb2 = scan_bytes(CFG2["batch"], CFG2["dim"], L, N, es=2)
-            line["ref_cuda_b200"] = {
-                "what": "reference CUDA kernels (oracle/_ref, built from its sources), float32, full config-2 "
-                        "shape, no z gate (the reference has none)", "ms_per_step": ms,
-                "value_bf16_byte_accounting": (fb2 + bb2) / (ms / 1e3) / 1e12, "unit": "TB/s"}
+                @staticmethod
+                def forward(ctx, u, A, B, C, D, delta, bias):
+                    out, h = ref.forward(u, A, B, C, D, delta, bias, None, None, None)
+                    ctx.save_for_backward(u, A, B, C, D, delta, bias, h)
+                    return out, h[..., -1, 1::2]
+
+                @staticmethod
+                def backward(ctx, dout, dh):
+                    u, A, B, C, D, delta, bias, h = ctx.saved_tensors
+                    g = ref.backward(u, A, B, C, D, delta, bias, h, None, dout.contiguous(), dh.contiguous(),
+                                     None, None)
+                    return g[0], g[1], g[2], g[3], g[4], g[5], g[6]
+
+            def fwd_bwd(inp):
+                leaves = [t.requires_grad_() for t in (inp.u, inp.A, inp.B, inp.C, inp.D, inp.delta,
+                                                       inp.delta_bias)]
+                out, _ = RefScanFn.apply(*leaves)
+                out.backward(inp.dout)
+                for t in leaves:
+                    t.grad = None
+
+            line["ref_cuda_b200"] = run_equal_precision(dev, fwd_bwd, lambda *a: ref_up.apply(*a))
+            line["ref_cuda_b200"]["what"] = ("reference CUDA kernels (oracle/_ref, built from its sources), "
+                                             "float32, no z gate (the reference has none)")
     except Exception as e:  # context only; never fail the reference arm on it
         line["ref_cuda_b200"] = {"error": str(e)[:200]}
     return line
@@ -511,6 +648,8 @@ def main():
     ap.add_argument("--no-ref-cuda", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-long", action="store_true", help="skip the long-sequence (config 5) measurement")
+    ap.add_argument("--no-fp32", action="store_true",
+                    help="skip the float32 workloads timed like the reference's kernels")
     ap.add_argument("--decode-only", action="store_true", help="profiling aid: only the decode loop")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()

@@ -36,11 +36,17 @@ def _padding_right(padding_size: Optional[str]) -> bool:
     return padding_size is None or padding_size == "right"
 
 
+_SMS = {}
+
+
 def _segments_for(u: torch.Tensor, N: int) -> int:
     """Segments for a scan of u on its GPU (see slices.plan_segments)."""
-    if not u.is_cuda:
+    if not u.is_cuda or u.shape[0] != 1:
         return 1
-    sms = torch.cuda.get_device_properties(u.device).multi_processor_count
+    idx = u.device.index if u.device.index is not None else torch.cuda.current_device()
+    sms = _SMS.get(idx)
+    if sms is None:
+        sms = _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
     return plan_segments(u.shape[0], u.shape[1], u.shape[2], N, sms=sms)
 
 
