@@ -98,6 +98,15 @@ __device__ __forceinline__ void load_state_pairs(const float* rows, int t, int g
     }
 }
 
+// two consecutive elements from a float2 (one 4- or 8-byte shared-memory store)
+template <typename T> __device__ __forceinline__ void store_pair(void* p, float2 v);
+template <> __device__ __forceinline__ void store_pair<float>(void* p, float2 v) {
+    *reinterpret_cast<float2*>(p) = v;
+}
+template <> __device__ __forceinline__ void store_pair<__nv_bfloat16>(void* p, float2 v) {
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(v.x, v.y);
+}
+
 // four consecutive elements as float (from 8 or 16 bytes of shared memory)
 template <typename T> struct Vec4;
 template <> struct Vec4<float> {

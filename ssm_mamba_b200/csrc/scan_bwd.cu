@@ -68,6 +68,8 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
     const int c = tid / LPC, g = tid % LPC;
     const int cw = lane / LPC;
     const int rot = ROT ? (cw & (SPT - 1)) : 0;
+    const int rot_n = (tid % LPC) * SPT + rot;   // state whose dB/dC channel sum this lane stores
+    const bool rot_ok = ROT && rot_n < p.dstate;
     const int b = blockIdx.x / p.ntile_d, tile_d = blockIdx.x % p.ntile_d;
     const int d0 = tile_d * DT, d = d0 + c;
     const bool dvalid = d < p.dim;
@@ -144,6 +146,8 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
     };
 
     const int ntiles = (Lq + TB - 1) / TB;
+    // this CTA's dB/dC partial rows in the workspace: (2, dstate, seqlen) floats
+    float* const ws_bc_row = p.ws_bc + (((int64_t)tile_d * p.batch + b) * 2) * N * (int64_t)Lq;
     const uint32_t tile_bytes = (uint32_t)DT * TB * ES;
     const uint32_t bc_bytes = (uint32_t)N * TB * ES;
     const uint32_t stage_bytes = (has_z ? 5u : 3u) * tile_bytes + 2u * bc_bytes;
@@ -297,8 +301,13 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
         unsigned char* odu = smem + S.du;
         unsigned char* odd = smem + S.ddelta;
         float* wslot = slots + warp * S.slot_stride;
+        // dB/dC slot row of the state this lane sums in the rotated order (ROT only)
+        float* const rot_dst = wslot + rot_n * (TB + 1);
         const float* sBr = sB + rot * (int)S.rot_stride;
         const float* sCr = sC + rot * (int)S.rot_stride;
+        // swizzle term of token t = tl0 + k of a sub-tile: sub-tiles start at multiples of K,
+        // so when K is a multiple of the swizzle period it depends on k alone (a constant)
+        auto swz_of = [](int k, int t) { return (K % (QM + 1) == 0) ? (k & QM) : (t & QM); };
 #pragma unroll 1
         for (int sub = NSUB - 1; sub >= 0; sub--) {
             const int tl0 = sub * K;
@@ -313,7 +322,8 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                 // reference: a 128-token chunk that starts at or after len is skipped
                 if constexpr (LPC <= K) {
 #pragma unroll
-                    for (int k = 0; k < K; k++) *reinterpret_cast<float2*>(xmine + 2 * k) = make_float2(0.f, 0.f);
+                    for (int k = 0; k < K; k += 2)
+                        *reinterpret_cast<float4*>(xmine + 2 * k) = make_float4(0.f, 0.f, 0.f, 0.f);
                 } else {
 #pragma unroll
                     for (int j = 0; j < V; j++) v[j] = 0.f;
@@ -321,12 +331,9 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
 #pragma unroll
                 for (int k = 0; k < K; k++) {
                     if (ROT) {
-                        if (cw < SPT) {
-                            const int n = g * SPT + cw;
-                            if (n < N) {
-                                wslot[n * (TB + 1) + tl0 + k] = 0.f;
-                                wslot[(NS + n) * (TB + 1) + tl0 + k] = 0.f;
-                            }
+                        if (rot_ok) {
+                            rot_dst[tl0 + k] = 0.f;
+                            rot_dst[NS * (TB + 1) + tl0 + k] = 0.f;
                         }
                     } else if (cw == 0) {
 #pragma unroll
@@ -362,7 +369,7 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                             const float2 dl2 = make_float2(dls[j], dls[j]);
                             const float2 du2 = make_float2(dus[j], dus[j]);
                             float2 bp[NP];
-                            load_state_pairs<SPT, NS>(sBr, t, g, t & QM, bp);
+                            load_state_pairs<SPT, NS>(sBr, t, g, swz_of(k, t), bp);
 #pragma unroll
                             for (int pi = 0; pi < NP; pi++) {
                                 const float2 prev = k == 0 ? h0[pi] : hv[k - 1][pi];
@@ -379,6 +386,7 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                         }
                     }
                     // reverse recurrence and gradient terms
+                    float2 s_odd = make_float2(0.f, 0.f);
 #pragma unroll
                     for (int k4 = K - 4; k4 >= 0; k4 -= 4) {
                         const float4 dl4 = lds128(sD + c * RS + tl0 + k4);
@@ -404,8 +412,8 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                             float2 s12 = make_float2(0.f, 0.f), s22 = make_float2(0.f, 0.f);
                             float dBv[SPT], dCv[SPT];
                             float2 bp[NP], cp[NP];
-                            load_state_pairs<SPT, NS>(sBr, t, g, t & QM, bp);
-                            load_state_pairs<SPT, NS>(sCr, t, g, t & QM, cp);
+                            load_state_pairs<SPT, NS>(sBr, t, g, swz_of(k, t), bp);
+                            load_state_pairs<SPT, NS>(sCr, t, g, swz_of(k, t), cp);
 #pragma unroll
                             for (int pi = 0; pi < NP; pi++) {
                                 float2 inj = __fmul2_rn(dg2, cp[pi]);
@@ -434,8 +442,13 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                                 const float s1t = s12.x + s12.y;
                                 const float s2t = (GEN && !vld) ? 0.f : s22.x + s22.y;
                                 if constexpr (LPC <= K) {
-                                    // this lane's partial sums of token k, interleaved (S1, S2)
-                                    *reinterpret_cast<float2*>(xmine + 2 * k) = make_float2(s1t, s2t);
+                                    // this lane's partial sums of tokens k, k + 1 (k even), as
+                                    // (S1_k, S2_k, S1_k+1, S2_k+1); the odd token comes first
+                                    if (j & 1) {
+                                        s_odd = make_float2(s1t, s2t);
+                                    } else {
+                                        *reinterpret_cast<float4*>(xmine + 2 * k) = make_float4(s1t, s2t, s_odd.x, s_odd.y);
+                                    }
                                 } else {
                                     v[k] = s1t;
                                     v[K + k] = s2t;
@@ -452,12 +465,10 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                                 for (int m = SPT; m < CPW; m *= 2)
                                     r2 = __fadd2_rn(r2, make_float2(__shfl_xor_sync(0xffffffffu, r2.x, LPC * m),
                                                                     __shfl_xor_sync(0xffffffffu, r2.y, LPC * m)));
-                                if (cw < SPT) {
-                                    const int n = g * SPT + cw;
-                                    if (n < N) {
-                                        wslot[n * (TB + 1) + t] = r2.x;
-                                        wslot[(NS + n) * (TB + 1) + t] = r2.y;
-                                    }
+                                // lanes cw and cw ^ SPT hold the same sums: both store them
+                                if (rot_ok) {
+                                    rot_dst[t] = r2.x;
+                                    rot_dst[NS * (TB + 1) + t] = r2.y;
                                 }
                             } else {
 #pragma unroll
@@ -509,25 +520,57 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                 *reinterpret_cast<IT*>(odu + out_off(c, t)) = from_f<IT>(du);
                 *reinterpret_cast<IT*>(odd + out_off(c, t)) = from_f<IT>(ddl);
             };
+            // tokens k, k + 1 (k even) at once: 8-byte row loads, one store of both outputs
+            auto finish2 = [&](int k, float4 sv) {
+                const int t = tl0 + k, tg = ts + k;
+                float2 du = make_float2(0.f, 0.f), ddl = make_float2(0.f, 0.f);
+                if (!skipped) {
+                    const float2 dl = *reinterpret_cast<const float2*>(sD + c * RS + t);
+                    const float2 dg = *reinterpret_cast<const float2*>(sG + c * RS + t);
+                    const float2 uv = *reinterpret_cast<const float2*>(sU + c * RS + t);
+                    const float2 sp = *reinterpret_cast<const float2*>(sSP + c * RS + t);
+                    du.x = fmaf(Dd, dg.x, dl.x * sv.x);
+                    du.y = fmaf(Dd, dg.y, dl.y * sv.z);
+                    ddl.x = tg < len ? fmaf(uv.x, sv.x, sv.y) * sp.x : 0.f;
+                    ddl.y = tg + 1 < len ? fmaf(uv.y, sv.z, sv.w) * sp.y : 0.f;
+                    dD_acc = fmaf(dg.x, uv.x, fmaf(dg.y, uv.y, dD_acc));
+                    db_acc += ddl.x + ddl.y;
+                }
+                store_pair<IT>(odu + out_off(c, t), du);
+                store_pair<IT>(odd + out_off(c, t), ddl);
+            };
             if constexpr (LPC <= K) {
-                // each lane stored (S1, S2) of token k at xmine[2k]; the lanes of a channel
-                // swap them through this warp's exchange area and lane g sums the LPC
+                // each lane stored its partial (S1, S2) of every token pair at xmine; the lanes of
+                // a channel swap them through this warp's exchange area and lane g sums the LPC
                 // partials of the RK consecutive tokens g*RK ... and finishes them
                 constexpr int RK = K / LPC;
                 __syncwarp();
-                float2 sr[RK];
+                if constexpr (RK >= 2) {
+                    float4 sr[RK / 2];
 #pragma unroll
-                for (int r = 0; r < RK; r++) sr[r] = make_float2(0.f, 0.f);
+                    for (int r = 0; r < RK / 2; r++) sr[r] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                for (int gg = 0; gg < LPC; gg++) {
-                    const float* src = xwarp + ((lane & ~(LPC - 1)) + gg) * (int)S.xch_stride + 2 * g * RK;
+                    for (int gg = 0; gg < LPC; gg++) {
+                        const float* src = xwarp + ((lane & ~(LPC - 1)) + gg) * (int)S.xch_stride + 2 * g * RK;
 #pragma unroll
-                    for (int r = 0; r < RK; r++)
-                        sr[r] = __fadd2_rn(sr[r], *reinterpret_cast<const float2*>(src + 2 * r));
+                        for (int r = 0; r < RK / 2; r++) {
+                            const float4 x = *reinterpret_cast<const float4*>(src + 4 * r);
+                            sr[r].x += x.x; sr[r].y += x.y; sr[r].z += x.z; sr[r].w += x.w;
+                        }
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int r = 0; r < RK / 2; r++) finish2(g * RK + 2 * r, sr[r]);
+                } else {
+                    float2 sr = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int gg = 0; gg < LPC; gg++) {
+                        const float* src = xwarp + ((lane & ~(LPC - 1)) + gg) * (int)S.xch_stride + 2 * g;
+                        sr = __fadd2_rn(sr, *reinterpret_cast<const float2*>(src));
+                    }
+                    __syncwarp();
+                    finish(g, sr.x, sr.y);
                 }
-                __syncwarp();
-#pragma unroll
-                for (int r = 0; r < RK; r++) finish(g * RK + r, sr[r].x, sr[r].y);
             } else {
                 reduce_scatter<LPC, V>(v, g);
                 const float other = __shfl_xor_sync(0xffffffffu, v[0], K);
@@ -541,18 +584,25 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
         __syncthreads();
 
         // ---- CTA sum of the warp dB/dC slots -> workspace; store du, ddelta, dz -------------
-        const int nw = nthr / 32;
         {
-            // rows r = q * N + n of TB tokens; thread (tid % TB) walks token t of rows tid / TB, ...
+            // rows r = q * N + n of TB tokens; thread (tid % TB) sums token t of rows
+            // tid / TB, tid / TB + nthr / TB, ... over the (at most 4) warps
+            const int nw = nthr >> 5;
             const int t = tid % TB;
-            const int tg = t0 + t;
-            float* dst = p.ws_bc + (((int64_t)tile_d * p.batch + b) * 2) * N * (int64_t)Lq + tg;
-            for (int r = tid / TB; r < 2 * N; r += nthr / TB) {
-                const int q = r >= N ? 1 : 0, n = r - q * N;
-                const float* src = slots + (q * NS + n) * (TB + 1) + t;
-                float acc = 0.f;
-                for (int w = 0; w < nw; w++) acc += src[w * S.slot_stride];
-                if (tg < Lq) dst[(int64_t)r * Lq] = acc;
+            const int rstep = nthr / TB;
+            if (t0 + t < Lq) {
+                float* dst = ws_bc_row + (int64_t)(tid / TB) * Lq + t0 + t;
+                const int64_t dstep = (int64_t)rstep * Lq;
+                const int sstride = (int)S.slot_stride;
+                for (int r = tid / TB; r < 2 * N; r += rstep, dst += dstep) {
+                    const int q = r >= N ? 1 : 0, n = r - q * N;
+                    const float* src = slots + (q * NS + n) * (TB + 1) + t;
+                    float acc = src[0];
+#pragma unroll
+                    for (int w = 1; w < 4; w++)
+                        if (w < nw) acc += src[w * sstride];
+                    *dst = acc;
+                }
             }
         }
         if (p.use_tma) {

@@ -117,7 +117,10 @@ __host__ __device__ inline BwdSmem bwd_smem_layout(int dt, int ns, int n, int es
     L.sC = o; o += align_up((uint32_t)nrot * L.rot_stride * 4u, 128u);
     L.slot_stride = 2u * ns * (TB + 1);
     L.slots = o; o += align_up((uint32_t)nwarps * L.slot_stride * 4u, 128u);
-    L.xch_stride = 2u * ksub + 2u;   // 18 floats for ksub = 8: 8-byte stores by 32 lanes hit 2 wavefronts
+    // (S1, S2) of ksub tokens per lane, written as 16-byte token pairs; a stride of 20 floats
+    // (ksub = 8) makes both the 16-byte writes and the 16-byte reads of the 4 lanes of a
+    // channel bank-conflict free
+    L.xch_stride = 2u * ksub + 4u;
     L.xch = o; o += align_up((uint32_t)nwarps * 32u * L.xch_stride * 4u, 128u);
     L.bias = o; o += align_up((uint32_t)dt * 4u, 16u);
     L.bar = align_up(o, 8u); o = L.bar + 8u;
