@@ -152,7 +152,14 @@ typedef struct ssm_state_update_args {
     const void* z;       int64_t z_batch_stride;   /* may be NULL */
     const float* dt_bias;          /* may be NULL */
     void* out;           int64_t out_batch_stride;
+    int32_t launch_flags;          /* bit 0 (SSM_LAUNCH_PDL): programmatic dependent launch --
+                                      the kernel may start while the previous kernel in the
+                                      stream finishes; it prefetches its state into L2, then
+                                      waits for that kernel before reading any input */
+    int32_t _pad1;
 } ssm_state_update_args;
+
+#define SSM_LAUNCH_PDL 1
 
 /* Message of the last failed call on the calling thread ("" if none). */
 SSM_API const char* ssm_last_error(void);

@@ -19,6 +19,7 @@ HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "ssm_b200.h")
 SSM_F32, SSM_BF16 = 0, 1
 SSM_OK, SSM_ERR_INVALID, SSM_ERR_CUDA, SSM_ERR_WORKSPACE, SSM_ERR_DEVICE = 0, 1, 2, 3, 4
 SSM_CKPT_COMPACT, SSM_CKPT_REFERENCE = 0, 1
+SSM_LAUNCH_PDL = 1
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -105,6 +106,7 @@ class StateUpdateArgs(ctypes.Structure):
         ("z", _p), ("z_batch_stride", _i64),
         ("dt_bias", _p),
         ("out", _p), ("out_batch_stride", _i64),
+        ("launch_flags", _i32), ("_pad1", _i32),
     ]
 
 
@@ -276,7 +278,7 @@ def call_bwd_noalloc(args: ScanBwdArgs, stream=None):
 
 
 def fill_update(state, state_out, x, dt, A, B, C, out, D=None, z=None, dt_bias=None,
-                dt_softplus=True) -> StateUpdateArgs:
+                dt_softplus=True, launch_flags=0) -> StateUpdateArgs:
     a = StateUpdateArgs()
     a.batch, a.dim, a.dstate = state.shape
     a.dtype = _dtype_code(x)
@@ -294,6 +296,7 @@ def fill_update(state, state_out, x, dt, A, B, C, out, D=None, z=None, dt_bias=N
         a.z, a.z_batch_stride = _t(z), z.stride(0)
     a.dt_bias = _t(dt_bias)
     a.out, a.out_batch_stride = _t(out), out.stride(0)
+    a.launch_flags = launch_flags
     return a
 
 

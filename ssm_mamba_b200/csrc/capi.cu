@@ -24,7 +24,7 @@ cudaError_t launch_scan_fwd(const FwdParams& p, int is_bf16, int lpc, int spt, c
 cudaError_t launch_scan_bwd(const BwdParams& p, int is_bf16, int lpc, int spt, const CUtensorMap* maps,
                             cudaStream_t stream);
 cudaError_t launch_scan_reduce(const ReduceParams& p, cudaStream_t stream);
-cudaError_t launch_state_update(const UpdParams& p, int is_bf16, int lpc, cudaStream_t stream);
+cudaError_t launch_state_update(const UpdParams& p, int is_bf16, int lpc, int spt, cudaStream_t stream);
 cudaError_t launch_scan_chunk(const ChunkParams& p, int is_bf16, int lpc, int spt, int reverse,
                               const CUtensorMap* maps, cudaStream_t stream);
 int chunk_occupancy(int is_bf16, int lpc, int spt, int reverse, int dt, int has_z);
@@ -57,12 +57,27 @@ int cuda_fail(cudaError_t e, const char* what) {
 // ---- lanes per channel / states per thread / backward sub-tile for a state count ----------
 struct StateSplit { int lpc, spt, k; };
 
-// Decode kernel: 4 states per thread (8 above 128 states).
+// Backward checkpoint interval (and the scan kernels' split above 128 states).
 StateSplit split_states(int64_t n) {
     if (n > 128) return {32, 8, 4};
     int ns = 4;
     while (ns < n) ns *= 2;
     return {ns / 4, 4, 8};
+}
+
+// Decode kernel: SPT states per thread.  8 states per thread for small state counts (half
+// the per-row scalar work per state of 4, and 32 bytes of state per thread in flight);
+// SSM_DEC_SPT (4, 8, 16) overrides for experiments.
+StateSplit decode_split(int64_t n) {
+    if (n > 128) return {32, 8, 4};
+    int ns = 4;
+    while (ns < n) ns *= 2;
+    int spt = ns >= 8 ? 8 : 4;
+    if (const char* e = getenv("SSM_DEC_SPT")) {
+        const int v = atoi(e);
+        if ((v == 4 || v == 8 || v == 16) && v <= ns && ns / v <= 16) spt = v;
+    }
+    return {ns / spt, spt, 8};
 }
 
 // Scan kernels: 4 states per thread; 2 only when 4 would leave fewer than 4 warps per SM
@@ -526,9 +541,9 @@ int ssm_state_update(const ssm_state_update_args* a, void* stream_) {
     if (!valid_dtype(a->dtype)) return fail(SSM_ERR_INVALID, "ssm_state_update: dtype must be SSM_F32 or SSM_BF16");
     if (!a->state || !a->state_out || !a->x || !a->dt || !a->A || !a->B || !a->C || !a->out)
         return fail(SSM_ERR_INVALID, "ssm_state_update: state, state_out, x, dt, A, B, C and out are required");
-    const StateSplit sp = split_states(a->dstate);
-    if (a->batch > 65535 || a->dim > (1 << 30))
-        return fail(SSM_ERR_INVALID, "ssm_state_update: batch must be <= 65535");
+    const StateSplit sp = decode_split(a->dstate);
+    if (a->batch > (1 << 30) || (a->dim + (256 / sp.lpc) - 1) / (256 / sp.lpc) > 65535)
+        return fail(SSM_ERR_INVALID, "ssm_state_update: dim must be <= 65535 * %d", 256 / sp.lpc);
     UpdParams p;
     memset(&p, 0, sizeof(p));
     p.batch = (int)a->batch; p.dim = (int)a->dim; p.dstate = (int)a->dstate;
@@ -543,7 +558,8 @@ int ssm_state_update(const ssm_state_update_args* a, void* stream_) {
     p.D = a->D; p.z = a->z; p.z_sb = a->z_batch_stride;
     p.dt_bias = a->dt_bias;
     p.out = a->out; p.out_sb = a->out_batch_stride;
-    cudaError_t e = launch_state_update(p, a->dtype == SSM_BF16, sp.lpc, stream);
+    p.pdl = (a->launch_flags & SSM_LAUNCH_PDL) != 0;
+    cudaError_t e = launch_state_update(p, a->dtype == SSM_BF16, sp.lpc, sp.spt, stream);
     if (e != cudaSuccess) return cuda_fail(e, "state_update launch");
     return SSM_OK;
 }

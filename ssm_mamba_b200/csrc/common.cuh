@@ -107,6 +107,17 @@ template <> __device__ __forceinline__ void store_pair<__nv_bfloat16>(void* p, f
     *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(v.x, v.y);
 }
 
+// Programmatic dependent launch (sm_90+): wait until the preceding grid in the stream has
+// completed and its writes are visible (a no-op when this grid was launched without the
+// programmatic-serialization attribute), and let the next grid start launching.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// L2 prefetch hint; L2 is the point of coherence, so a prefetched line is never stale
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
 // four consecutive elements as float (from 8 or 16 bytes of shared memory)
 template <typename T> struct Vec4;
 template <> struct Vec4<float> {

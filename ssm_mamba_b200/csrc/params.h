@@ -118,6 +118,7 @@ struct UpdParams {
     const void* z; int64_t z_sb;
     const float* dt_bias;
     void* out; int64_t out_sb;
+    int pdl;             // launch with programmatic dependent launch
 };
 
 }  // namespace ssm

@@ -412,6 +412,7 @@ at::Tensor state_update(const at::Tensor& state, const at::Tensor& state_out, co
     if (z) { a.z = z->data_ptr(); a.z_batch_stride = z->stride(0); }
     a.dt_bias = ptr<const float>(dt_bias);
     a.out = out.data_ptr(); a.out_batch_stride = out.stride(0);
+    a.launch_flags = SSM_LAUNCH_PDL;   // overlap the launch with the previous kernel's tail
     ok(ssm_state_update(&a, at::cuda::getCurrentCUDAStream().stream()));
     return out;
 }

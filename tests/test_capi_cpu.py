@@ -33,7 +33,7 @@ def test_struct_layout_matches_header(tmp_path):
     fields = {"ssm_scan_fwd_args": ("ScanFwdArgs", ["u", "B", "ckpt", "ckpt_len", "h_last"]),
               "ssm_scan_bwd_args": ("ScanBwdArgs", ["y", "ckpt_len", "dout", "dz", "dh_init",
                                                     "dB_batch_stride", "dC_state_stride"]),
-              "ssm_state_update_args": ("StateUpdateArgs", ["state", "x", "z", "out"]),
+              "ssm_state_update_args": ("StateUpdateArgs", ["state", "x", "z", "out", "launch_flags"]),
               "ssm_carry_args": ("CarryArgs", ["reverse", "nstart", "A", "carry", "delta_sum", "start",
                                                "start_stride", "result"])}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "ssm_b200.h"', "int main(void){"]
