@@ -333,6 +333,11 @@ static int fwd_impl(const ssm_scan_fwd_args* a, const float* restart, void* stre
             (rc = encode3d(&maps[6], a->y, is_bf16, a->seqlen, a->dim, a->batch, a->y_dim_stride, a->y_batch_stride, T, p.dt, sw)))
             return rc;
     }
+    // test hook for failure detection: with SSM_TEST_WITHHOLD_TMA set the forward issues no
+    // TMA load, its first bounded mbarrier wait (~1 s) runs out, and every CTA leaves with
+    // device error kDevErrTmaTimeout (read by ssm_check_device_error); nothing is in flight
+    // when the CTAs exit and the context stays usable
+    p.test_withhold = p.use_tma && getenv("SSM_TEST_WITHHOLD_TMA") != nullptr;
     cudaError_t e = launch_scan_fwd(p, is_bf16, sp.lpc, sp.spt, maps, stream);
     if (e != cudaSuccess) return cuda_fail(e, "scan_fwd launch");
     return SSM_OK;

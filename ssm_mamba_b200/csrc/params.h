@@ -34,6 +34,7 @@ struct FwdParams {
     const float* restart;
     int restart_len, restart_nck;
     int* err;            // device error word
+    int test_withhold;   // test hook: never issue the TMA loads, so the first bounded wait runs out
 };
 
 struct BwdParams {

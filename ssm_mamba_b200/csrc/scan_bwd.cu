@@ -129,18 +129,17 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
     for (int i = tid; i < DT; i += nthr)
         sBias[i] = (d0 + i < p.dim && p.delta_bias) ? p.delta_bias[d0 + i] : 0.f;
 
+    // this thread's channel in checkpoint 0 (checkpoints are dim * dstate floats apart) and
+    // in the initial state
+    const float* const ck_thread = p.ckpt + ((int64_t)b * p.nck * p.dim + (dvalid ? d : 0)) * N;
+    const int64_t ck_stride = (int64_t)p.dim * N;
+    const float* const hi_thread = p.h_init ? p.h_init + ((int64_t)b * p.dim + (dvalid ? d : 0)) * N : nullptr;
     auto load_ckpt = [&](int ts, float2 (&hv)[NP]) {
+        const float* row = ts == 0 ? hi_thread : ck_thread + (int64_t)(ts / K - 1) * ck_stride;
 #pragma unroll
         for (int s = 0; s < SPT; s++) {
             const int n = nidx[s];
-            float v = 0.f;
-            if (dvalid && n < N) {
-                if (ts == 0) {
-                    if (p.h_init) v = p.h_init[((int64_t)b * p.dim + d) * N + n];
-                } else {
-                    v = p.ckpt[(((int64_t)b * p.nck + (ts / K - 1)) * p.dim + d) * N + n];
-                }
-            }
+            const float v = (row != nullptr && dvalid && n < N) ? row[n] : 0.f;
             if (s & 1) hv[s / 2].y = v; else hv[s / 2].x = v;
         }
     };

@@ -33,6 +33,19 @@ namespace ssm {
 // an index, so the layout struct stays in registers.
 __device__ __forceinline__ uint32_t stage_off(const uint32_t (&a)[2], int st) { return st ? a[1] : a[0]; }
 
+// This thread's SPT states of one compact checkpoint, at dst (its first state n0).
+template <int SPT>
+__device__ __forceinline__ void store_ckpt_row(float* dst, const float2 (&h)[SPT / 2], bool vec, int n0, int N) {
+    if (vec) {
+#pragma unroll
+        for (int q = 0; q < SPT / 2; q++) *reinterpret_cast<float2*>(dst + 2 * q) = h[q];
+    } else {
+#pragma unroll
+        for (int s = 0; s < SPT; s++)
+            if (n0 + s < N) dst[s] = (s & 1) ? h[s / 2].y : h[s / 2].x;
+    }
+}
+
 // State checkpoint k of channel d: compact (batch, nck, dim, dstate) fp32 states, or the
 // reference's interleaved (prod, state) chunk carries.  A free function rather than a
 // capturing lambda so that h and A2 stay in registers.
@@ -108,6 +121,12 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     const bool want_y = p.y != nullptr;
     const bool want_prod = p.ckpt != nullptr && p.ckpt_format == 1;
     const int ck_mask = p.ckpt_len - 1;     // checkpoint interval is a power of two
+    // compact checkpoints are written in order: checkpoint k of this thread's states sits at
+    // ck_ptr after k steps of ck_step floats (vector stores when the states are whole pairs)
+    const bool ck_compact = p.ckpt != nullptr && p.ckpt_format == 0 && dvalid;
+    const bool ck_vec = (g * SPT + SPT <= p.dstate) && (p.dstate & 3) == 0;
+    float* ck_ptr = ck_compact ? p.ckpt + ((int64_t)b * p.nck * p.dim + d) * p.dstate + g * SPT : nullptr;
+    const int64_t ck_step = (int64_t)p.dim * p.dstate;
 
     int len = Lq;
     if (p.length) {
@@ -194,7 +213,7 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
         prefetch_tensormap(&tm_C);
     }
     __syncthreads();
-    if (p.use_tma && tid == 0) {
+    if (p.use_tma && tid == 0 && !p.test_withhold) {
         issue(0, 0);
         if (ntiles > 1) issue(1, 1);
     }
@@ -308,7 +327,14 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
                         if (s & 1) h[s / 2].y = v; else h[s / 2].x = v;
                     }
                 }
-                if (p.ckpt && tg_end <= Lq && (tg_end & ck_mask) == 0 && dvalid) fwd_write_ckpt<SPT>(p, h, A2, Ssum, b, d, g, (tg_end >> p.ckpt_shift) - 1);
+                if ((tg_end & ck_mask) == 0 && tg_end <= Lq) {
+                    if (ck_compact) {
+                        store_ckpt_row<SPT>(ck_ptr, h, ck_vec, g * SPT, N);
+                        ck_ptr += ck_step;
+                    } else if (p.ckpt && dvalid) {
+                        fwd_write_ckpt<SPT>(p, h, A2, Ssum, b, d, g, (tg_end >> p.ckpt_shift) - 1);
+                    }
+                }
             }
             // lane g now finishes the RL consecutive tokens q0 + g*RL ...
             reduce_scatter_contig<LPC, G>(yv, g);
@@ -378,7 +404,10 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     }
 
     // the last checkpoint of a sequence whose length is not a multiple of ckpt_len
-    if (p.ckpt && (Lq & ck_mask) != 0 && dvalid) fwd_write_ckpt<SPT>(p, h, A2, Ssum, b, d, g, p.nck - 1);
+    if (p.ckpt && (Lq & ck_mask) != 0 && dvalid) {
+        if (ck_compact) store_ckpt_row<SPT>(ck_ptr, h, ck_vec, g * SPT, N);
+        else fwd_write_ckpt<SPT>(p, h, A2, Ssum, b, d, g, p.nck - 1);
+    }
     if (p.h_last && dvalid) {
 #pragma unroll
         for (int s = 0; s < SPT; s++) {
