@@ -246,6 +246,43 @@ SSM_API int ssm_scan_chunk_state_bwd(const ssm_scan_bwd_args* args, float* g_sta
  * exp(A * delta_sum[q]) * result[q] + carry[q] (carry = g_start). */
 SSM_API int ssm_scan_carry_compose(const ssm_carry_args* args, void* stream);
 
+/* ---- causal depthwise conv1d (+ SiLU): the step in front of the scan ------------------------
+ * Replaces, in the reference's Mamba module (modules/mamba.py), the prefill
+ * silu(conv(x)[..., :seqlen]) with conv = nn.Conv1d(groups=dim, padding=width-1) (:137-139),
+ * the gather of the decode context (the last width-1 inputs before `lengths`, :114-133), its
+ * backward (torch autograd in the reference) and the decode step (:203-213):
+ *   out[b, d, t] = act(bias[d] + sum_k weight[d, k] x[b, d, t - (width-1) + k]), x[< 0] = 0
+ * width is 2, 3 or 4; act is SiLU or the identity. */
+typedef struct ssm_conv1d_args {
+    int64_t batch, dim, seqlen, width;
+    int32_t dtype;                 /* SSM_F32 or SSM_BF16, for x, out, state, dout, dx */
+    int32_t silu;                  /* 1: SiLU after the convolution */
+    const void* x;       int64_t x_batch_stride, x_dim_stride;     /* (batch, dim, seqlen);
+                                      ssm_conv1d_update: (batch, dim) */
+    const float* weight; int64_t weight_dim_stride;                 /* (dim, width) */
+    const float* bias;             /* (dim) or NULL */
+    void* out;           int64_t out_batch_stride, out_dim_stride;
+    const int64_t* length;         /* forward: (batch) or NULL; the context ends at length[b] */
+    void* state;         int64_t state_batch_stride, state_dim_stride; /* (batch, dim, width-1),
+                                      unit innermost stride; forward output (may be NULL),
+                                      ssm_conv1d_update input and output (in place) */
+    const void* dout;    int64_t dout_batch_stride, dout_dim_stride;   /* backward */
+    void* dx;            int64_t dx_batch_stride, dx_dim_stride;       /* backward */
+    float* dweight;      int64_t dweight_dim_stride;                   /* backward, (dim, width) */
+    float* dbias;                  /* backward, (dim) or NULL */
+} ssm_conv1d_args;
+
+SSM_API int ssm_conv1d_fwd(const ssm_conv1d_args* args, void* stream);
+/* Bytes of device workspace ssm_conv1d_bwd needs (per-warp dweight/dbias partials). */
+SSM_API size_t ssm_conv1d_bwd_workspace_size(const ssm_conv1d_args* args);
+/* Backward: dx, dweight, dbias from x and dout (the gradient of out).  Overwrites them;
+ * deterministic (fixed-order sums, no floating-point atomics). */
+SSM_API int ssm_conv1d_bwd(const ssm_conv1d_args* args, void* workspace, size_t workspace_bytes,
+                           void* stream);
+/* One decode step: x (batch, dim) joins the context `state`, which shifts by one in place;
+ * out (batch, dim) = act(bias + sum_k weight[k] window[k]). */
+SSM_API int ssm_conv1d_update(const ssm_conv1d_args* args, void* stream);
+
 /* Reads and clears the device-side error word of the current device (synchronizes
  * `stream`).  Returns SSM_OK, or SSM_ERR_DEVICE with *code set to the kernel's code. */
 SSM_API int ssm_check_device_error(int* code, void* stream);

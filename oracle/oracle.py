@@ -44,6 +44,18 @@ def lib():
             f = getattr(_lib, "oracle_state_update_" + suf)
             f.argtypes = [i64] * 3 + [p] * 8 + [i32] + [p] * 3
             f.restype = i32
+            f = getattr(_lib, "oracle_conv1d_fwd_" + suf)
+            f.argtypes = [i64] * 4 + [p] * 3 + [i32, p]
+            f.restype = i32
+            f = getattr(_lib, "oracle_conv1d_bwd_" + suf)
+            f.argtypes = [i64] * 4 + [p] * 3 + [i32] + [p] * 4
+            f.restype = i32
+            f = getattr(_lib, "oracle_conv1d_state_" + suf)
+            f.argtypes = [i64] * 4 + [p] * 3
+            f.restype = i32
+            f = getattr(_lib, "oracle_conv1d_update_" + suf)
+            f.argtypes = [i64] * 3 + [p] * 4 + [i32, p]
+            f.restype = i32
         _lib.oracle_num_threads.restype = i32
     return _lib
 
@@ -139,3 +151,51 @@ def state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None, dt_softplu
     if rc != 0:
         raise RuntimeError(f"oracle_state_update failed with status {rc}")
     return out, new_state
+
+
+def conv1d_fwd(x, w, bias=None, silu=True, dtype=np.float64):
+    """silu(causal depthwise conv1d(x)); x (batch, dim, L), w (dim, width)."""
+    x, w, bias = (_prep(v, dtype) for v in (x, w, bias))
+    Bsz, Dn, L = x.shape
+    out = np.empty_like(x)
+    rc = getattr(lib(), "oracle_conv1d_fwd_" + _suffix(dtype))(
+        Bsz, Dn, L, w.shape[1], _ptr(x), _ptr(w), _ptr(bias), int(bool(silu)), _ptr(out))
+    if rc != 0:
+        raise RuntimeError(f"oracle_conv1d_fwd failed with status {rc}")
+    return out
+
+
+def conv1d_bwd(x, w, dout, bias=None, silu=True, dtype=np.float64):
+    """Gradients (dx, dw, dbias) of conv1d_fwd for the output gradient dout."""
+    x, w, bias, dout = (_prep(v, dtype) for v in (x, w, bias, dout))
+    Bsz, Dn, L = x.shape
+    dx = np.empty_like(x)
+    dw = np.empty_like(w)
+    dbias = np.empty((Dn,), dtype=dtype)
+    rc = getattr(lib(), "oracle_conv1d_bwd_" + _suffix(dtype))(
+        Bsz, Dn, L, w.shape[1], _ptr(x), _ptr(w), _ptr(bias), int(bool(silu)), _ptr(dout), _ptr(dx),
+        _ptr(dw), _ptr(dbias))
+    if rc != 0:
+        raise RuntimeError(f"oracle_conv1d_bwd failed with status {rc}")
+    return dx, dw, dbias
+
+
+def conv1d_state(x, width, length=None, dtype=np.float64):
+    """The decode context after a prefill: (batch, dim, width-1) inputs before length[b]."""
+    x = _prep(x, dtype)
+    length = None if length is None else np.ascontiguousarray(length, dtype=np.int64)
+    Bsz, Dn, L = x.shape
+    state = np.empty((Bsz, Dn, width - 1), dtype=dtype)
+    getattr(lib(), "oracle_conv1d_state_" + _suffix(dtype))(Bsz, Dn, L, width, _ptr(x), _ptr(length), _ptr(state))
+    return state
+
+
+def conv1d_update(x, state, w, bias=None, silu=True, dtype=np.float64):
+    """One decode step; returns (out, new_state); the input state is not modified."""
+    x, w, bias = (_prep(v, dtype) for v in (x, w, bias))
+    st = np.array(state, dtype=dtype, copy=True)
+    Bsz, Dn = x.shape
+    out = np.empty_like(x)
+    getattr(lib(), "oracle_conv1d_update_" + _suffix(dtype))(
+        Bsz, Dn, w.shape[1], _ptr(x), _ptr(st), _ptr(w), _ptr(bias), int(bool(silu)), _ptr(out))
+    return out, st

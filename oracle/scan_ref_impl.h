@@ -14,6 +14,8 @@
  *   backward : csrc/selective_scan/backward_kernel.cu:212-452
  *   update   : csrc/selective_update/kernel.cu:45-77
  *   gate     : modules/mamba.py:182 (out * silu(gate)), fused here when z != NULL
+ *   conv1d   : modules/mamba.py:37-44, 114-139, 203-213 (the causal depthwise conv and SiLU
+ *              in front of the scan)
  *
  * Layouts (all contiguous, row-major):
  *   u, delta, z, dout, out, y, du, ddelta, dz : (batch, dim, seqlen)
@@ -312,6 +314,113 @@ int FN(oracle_state_update_)(
             acc += Cm[b * N + n] * hn;
         }
         out[bd] = z ? acc * z[bd] * FN(sigmoid_)(z[bd]) : acc;
+    }
+    return 0;
+}
+
+/*
+ * Causal depthwise conv1d + optional SiLU, restating the reference's Mamba module:
+ *   prefill  silu(nn.Conv1d(dim, dim, width, groups=dim, padding=width-1)(x)[..., :L])
+ *            (modules/mamba.py:37-44, 137-139): out[t] = bias + sum_k w[k] x[t-(width-1)+k]
+ *   context  the last width-1 inputs before length[b], zero before the row start
+ *            (modules/mamba.py:114-133)
+ *   decode   window = cat(context, x); out = silu(sum_k window[k] w[k] + bias); the context
+ *            shifts by one (modules/mamba.py:203-213)
+ * Layouts: x, out, dout, dx (batch, dim, L); w, dw (dim, width); bias, dbias (dim);
+ * state (batch, dim, width-1).  The backward is the exact gradient of the prefill.
+ */
+int FN(oracle_conv1d_fwd_)(int64_t Bsz, int64_t Dn, int64_t L, int64_t K, const REAL* x, const REAL* w,
+                           const REAL* bias, int silu, REAL* out)
+{
+    #pragma omp parallel for schedule(static)
+    for (int64_t bd = 0; bd < Bsz * Dn; bd++) {
+        const int64_t d = bd % Dn;
+        for (int64_t t = 0; t < L; t++) {
+            REAL acc = bias ? bias[d] : (REAL)0;
+            for (int64_t k = 0; k < K; k++) {
+                const int64_t s = t - (K - 1) + k;
+                if (s >= 0) acc += w[d * K + k] * x[bd * L + s];
+            }
+            out[bd * L + t] = silu ? acc * FN(sigmoid_)(acc) : acc;
+        }
+    }
+    return 0;
+}
+
+int FN(oracle_conv1d_bwd_)(int64_t Bsz, int64_t Dn, int64_t L, int64_t K, const REAL* x, const REAL* w,
+                           const REAL* bias, int silu, const REAL* dout, REAL* dx, REAL* dw, REAL* dbias)
+{
+    REAL* g = (REAL*)malloc(sizeof(REAL) * Bsz * Dn * L);
+    if (!g) return 3;
+    #pragma omp parallel for schedule(static)
+    for (int64_t bd = 0; bd < Bsz * Dn; bd++) {
+        const int64_t d = bd % Dn;
+        for (int64_t t = 0; t < L; t++) {
+            REAL pre = bias ? bias[d] : (REAL)0;
+            for (int64_t k = 0; k < K; k++) {
+                const int64_t s = t - (K - 1) + k;
+                if (s >= 0) pre += w[d * K + k] * x[bd * L + s];
+            }
+            REAL gi = dout[bd * L + t];
+            if (silu) {
+                const REAL sg = FN(sigmoid_)(pre);
+                gi *= sg * ((REAL)1 + pre * ((REAL)1 - sg));
+            }
+            g[bd * L + t] = gi;
+        }
+        for (int64_t t = 0; t < L; t++) {
+            REAL acc = 0;
+            for (int64_t k = 0; k < K; k++) {
+                const int64_t s = t + (K - 1) - k;
+                if (s < L) acc += w[d * K + k] * g[bd * L + s];
+            }
+            dx[bd * L + t] = acc;
+        }
+    }
+    #pragma omp parallel for schedule(static)
+    for (int64_t d = 0; d < Dn; d++) {
+        REAL db = 0;
+        for (int64_t k = 0; k < K; k++) {
+            REAL acc = 0;
+            for (int64_t b = 0; b < Bsz; b++)
+                for (int64_t t = 0; t < L; t++) {
+                    const int64_t s = t - (K - 1) + k;
+                    if (s >= 0) acc += g[(b * Dn + d) * L + t] * x[(b * Dn + d) * L + s];
+                }
+            dw[d * K + k] = acc;
+        }
+        for (int64_t b = 0; b < Bsz; b++)
+            for (int64_t t = 0; t < L; t++) db += g[(b * Dn + d) * L + t];
+        if (dbias) dbias[d] = db;
+    }
+    free(g);
+    return 0;
+}
+
+int FN(oracle_conv1d_state_)(int64_t Bsz, int64_t Dn, int64_t L, int64_t K, const REAL* x,
+                             const int64_t* length, REAL* state)
+{
+    for (int64_t bd = 0; bd < Bsz * Dn; bd++) {
+        const int64_t len = FN(clamp_len_)(length, bd / Dn, L);
+        for (int64_t j = 0; j < K - 1; j++) {
+            const int64_t t = len - (K - 1) + j;
+            state[bd * (K - 1) + j] = t >= 0 ? x[bd * L + t] : (REAL)0;
+        }
+    }
+    return 0;
+}
+
+int FN(oracle_conv1d_update_)(int64_t Bsz, int64_t Dn, int64_t K, const REAL* x, REAL* state, const REAL* w,
+                              const REAL* bias, int silu, REAL* out)
+{
+    for (int64_t bd = 0; bd < Bsz * Dn; bd++) {
+        const int64_t d = bd % Dn;
+        REAL acc = bias ? bias[d] : (REAL)0;
+        for (int64_t k = 0; k < K - 1; k++) acc += w[d * K + k] * state[bd * (K - 1) + k];
+        acc += w[d * K + K - 1] * x[bd];
+        for (int64_t k = 0; k + 1 < K - 1; k++) state[bd * (K - 1) + k] = state[bd * (K - 1) + k + 1];
+        state[bd * (K - 1) + K - 2] = x[bd];
+        out[bd] = silu ? acc * FN(sigmoid_)(acc) : acc;
     }
     return 0;
 }

@@ -5,12 +5,14 @@ Drop-in for the native hot path of nmquan1503/ssm-mamba:
     (ops/selective_scan_interface.py, ops/selective_update_interface.py);
   * ops.selective_scan_fn / ops.selective_state_update add the fused z gate, bf16 and
     optional softplus;
+  * ops.causal_conv1d_fn / ops.causal_conv1d_update are the causal depthwise conv1d + SiLU
+    in front of the scan (prefill with backward, and the decode step);
   * compat/ holds modules named `selective_scan` and `selective_update` with the
     reference extension modules' functions, so the reference's own ops/ run unchanged
     when compat/ is on sys.path.
 The kernels sit behind the C ABI in include/ssm_b200.h (lib/libssm_b200.so).
 """
-from .ops import (SelectiveScanFn, SelectiveUpdateFn, selective_scan_fn,  # noqa: F401
-                  selective_state_update)
+from .ops import (SelectiveScanFn, SelectiveUpdateFn, causal_conv1d_fn,  # noqa: F401
+                  causal_conv1d_update, selective_scan_fn, selective_state_update)
 
 __version__ = "0.1.0"

@@ -91,6 +91,23 @@ class CarryArgs(ctypes.Structure):
     ]
 
 
+class Conv1dArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64), ("dim", _i64), ("seqlen", _i64), ("width", _i64),
+        ("dtype", _i32), ("silu", _i32),
+        ("x", _p), ("x_batch_stride", _i64), ("x_dim_stride", _i64),
+        ("weight", _p), ("weight_dim_stride", _i64),
+        ("bias", _p),
+        ("out", _p), ("out_batch_stride", _i64), ("out_dim_stride", _i64),
+        ("length", _p),
+        ("state", _p), ("state_batch_stride", _i64), ("state_dim_stride", _i64),
+        ("dout", _p), ("dout_batch_stride", _i64), ("dout_dim_stride", _i64),
+        ("dx", _p), ("dx_batch_stride", _i64), ("dx_dim_stride", _i64),
+        ("dweight", _p), ("dweight_dim_stride", _i64),
+        ("dbias", _p),
+    ]
+
+
 class StateUpdateArgs(ctypes.Structure):
     _fields_ = [
         ("batch", _i64), ("dim", _i64), ("dstate", _i64),
@@ -144,6 +161,14 @@ def lib() -> ctypes.CDLL:
         L.ssm_scan_chunk_state_bwd.restype = ctypes.c_int
         L.ssm_scan_carry_compose.argtypes = [ctypes.POINTER(CarryArgs), _p]
         L.ssm_scan_carry_compose.restype = ctypes.c_int
+        L.ssm_conv1d_fwd.argtypes = [ctypes.POINTER(Conv1dArgs), _p]
+        L.ssm_conv1d_fwd.restype = ctypes.c_int
+        L.ssm_conv1d_bwd_workspace_size.argtypes = [ctypes.POINTER(Conv1dArgs)]
+        L.ssm_conv1d_bwd_workspace_size.restype = ctypes.c_size_t
+        L.ssm_conv1d_bwd.argtypes = [ctypes.POINTER(Conv1dArgs), _p, ctypes.c_size_t, _p]
+        L.ssm_conv1d_bwd.restype = ctypes.c_int
+        L.ssm_conv1d_update.argtypes = [ctypes.POINTER(Conv1dArgs), _p]
+        L.ssm_conv1d_update.restype = ctypes.c_int
         L.ssm_check_device_error.argtypes = [ctypes.POINTER(ctypes.c_int), _p]
         L.ssm_check_device_error.restype = ctypes.c_int
         _lib = L
@@ -333,6 +358,53 @@ def call_carry_compose(args: CarryArgs, stream=None):
     _check(lib().ssm_scan_carry_compose(ctypes.byref(args), stream if stream is not None else _stream()))
 
 
+def fill_conv1d(x, weight, out, bias=None, silu=True, length=None, state=None, dout=None, dx=None,
+                dweight=None, dbias=None) -> Conv1dArgs:
+    """x, out, dout, dx: (batch, dim, seqlen) (ssm_conv1d_update: (batch, dim)); weight,
+    dweight: (dim, width); state: (batch, dim, width - 1)."""
+    a = Conv1dArgs()
+    a.batch, a.dim = x.shape[0], x.shape[1]
+    a.seqlen = x.shape[2] if x.dim() == 3 else 0
+    a.width = weight.shape[1]
+    a.dtype = _dtype_code(x)
+    a.silu = int(bool(silu))
+    sd = lambda t: t.stride(1) if t.dim() == 3 else 1  # noqa: E731
+    a.x, a.x_batch_stride, a.x_dim_stride = _t(x), x.stride(0), sd(x)
+    a.weight, a.weight_dim_stride = _t(weight), weight.stride(0)
+    a.bias = _t(bias)
+    a.out, a.out_batch_stride, a.out_dim_stride = _t(out), out.stride(0), sd(out)
+    a.length = _t(length)
+    if state is not None:
+        a.state, a.state_batch_stride, a.state_dim_stride = _t(state), state.stride(0), state.stride(1)
+    if dout is not None:
+        a.dout, a.dout_batch_stride, a.dout_dim_stride = _t(dout), dout.stride(0), dout.stride(1)
+    if dx is not None:
+        a.dx, a.dx_batch_stride, a.dx_dim_stride = _t(dx), dx.stride(0), dx.stride(1)
+    if dweight is not None:
+        a.dweight, a.dweight_dim_stride = _t(dweight), dweight.stride(0)
+    a.dbias = _t(dbias)
+    return a
+
+
+def call_conv1d_fwd(args: Conv1dArgs, stream=None):
+    _check(lib().ssm_conv1d_fwd(ctypes.byref(args), stream if stream is not None else _stream()))
+
+
+def call_conv1d_bwd(args: Conv1dArgs, workspace=None, stream=None):
+    n = lib().ssm_conv1d_bwd_workspace_size(ctypes.byref(args))
+    if n == 0:
+        raise SsmError(SSM_ERR_INVALID, lib().ssm_last_error().decode())
+    if workspace is None:
+        import torch
+        workspace = torch.empty(n, dtype=torch.uint8, device="cuda")
+    _check(lib().ssm_conv1d_bwd(ctypes.byref(args), _t(workspace), workspace.numel(),
+                                stream if stream is not None else _stream()))
+
+
+def call_conv1d_update(args: Conv1dArgs, stream=None):
+    _check(lib().ssm_conv1d_update(ctypes.byref(args), stream if stream is not None else _stream()))
+
+
 def check_device_error(stream=None) -> int:
     code = ctypes.c_int(0)
     lib().ssm_check_device_error(ctypes.byref(code), stream if stream is not None else _stream())
@@ -341,4 +413,5 @@ def check_device_error(stream=None) -> int:
 
 def struct_sizes() -> Dict[str, int]:
     return {"fwd": ctypes.sizeof(ScanFwdArgs), "bwd": ctypes.sizeof(ScanBwdArgs),
-            "update": ctypes.sizeof(StateUpdateArgs), "carry": ctypes.sizeof(CarryArgs)}
+            "update": ctypes.sizeof(StateUpdateArgs), "carry": ctypes.sizeof(CarryArgs),
+            "conv1d": ctypes.sizeof(Conv1dArgs)}

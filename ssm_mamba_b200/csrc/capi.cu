@@ -29,6 +29,11 @@ cudaError_t launch_scan_chunk(const ChunkParams& p, int is_bf16, int lpc, int sp
                               const CUtensorMap* maps, cudaStream_t stream);
 int chunk_occupancy(int is_bf16, int lpc, int spt, int reverse, int dt, int has_z);
 cudaError_t launch_carry_compose(const CarryParams& p, cudaStream_t stream);
+cudaError_t launch_conv1d(const ConvParams& p, int is_bf16, int width, int kind, int vec, int sms,
+                          cudaStream_t stream);
+cudaError_t launch_conv1d_reduce(const float* ws, int nparts, int dim, int width, float* dw, int64_t dw_sd,
+                                 float* dbias, int sms, cudaStream_t stream);
+cudaError_t launch_conv1d_update(const ConvParams& p, int is_bf16, int width, int sms, cudaStream_t stream);
 size_t bwd_smem_bytes(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
 int fwd_occupancy(int is_bf16, int lpc, int spt, int dt, int has_z, int has_y);
 int bwd_occupancy(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
@@ -673,6 +678,113 @@ int ssm_scan_carry_compose(const ssm_carry_args* a, void* stream) {
     p.result = a->result;
     cudaError_t e = launch_carry_compose(p, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "carry_compose launch");
+    return SSM_OK;
+}
+
+// ---- causal depthwise conv1d -------------------------------------------------------------------
+static int conv_common(const char* name, const ssm_conv1d_args* a, bool seq, bool need_out = true) {
+    if (!a) return fail(SSM_ERR_INVALID, "%s: args is NULL", name);
+    if (a->batch < 1 || a->dim < 1 || (seq && a->seqlen < 1))
+        return fail(SSM_ERR_INVALID, "%s: sizes must be positive", name);
+    if (a->batch > (1 << 30) || a->dim > (1 << 30) || a->seqlen > (1 << 30))
+        return fail(SSM_ERR_INVALID, "%s: sizes too large", name);
+    if (a->width < 2 || a->width > 4) return fail(SSM_ERR_INVALID, "%s: width must be 2, 3 or 4", name);
+    if (!valid_dtype(a->dtype)) return fail(SSM_ERR_INVALID, "%s: dtype must be SSM_F32 or SSM_BF16", name);
+    if (!a->x || !a->weight || (need_out && !a->out))
+        return fail(SSM_ERR_INVALID, "%s: x, weight%s are required", name, need_out ? " and out" : "");
+    return SSM_OK;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 16-byte vectors along the sequence: every row start 16-byte aligned and seqlen a multiple
+// of the vector
+static bool conv_vec_ok(const ssm_conv1d_args* a, bool bwd) {
+    const int64_t es = a->dtype == SSM_BF16 ? 2 : 4, vt = 16 / es;
+    auto ok = [&](const void* p, int64_t sb, int64_t sd) {
+        return p == nullptr || (aligned16(p) && ((sb * es) & 15) == 0 && ((sd * es) & 15) == 0);
+    };
+    return (a->seqlen % vt) == 0 && ok(a->x, a->x_batch_stride, a->x_dim_stride) &&
+           ok(a->out, a->out_batch_stride, a->out_dim_stride) &&
+           (!bwd || (ok(a->dout, a->dout_batch_stride, a->dout_dim_stride) &&
+                     ok(a->dx, a->dx_batch_stride, a->dx_dim_stride)));
+}
+
+static ConvParams conv_params(const ssm_conv1d_args* a) {
+    ConvParams p;
+    memset(&p, 0, sizeof(p));
+    p.batch = (int)a->batch; p.dim = (int)a->dim; p.seqlen = (int)a->seqlen; p.silu = a->silu;
+    p.x = a->x; p.x_sb = a->x_batch_stride; p.x_sd = a->x_dim_stride;
+    p.w = a->weight; p.w_sd = a->weight_dim_stride; p.bias = a->bias;
+    p.out = a->out; p.out_sb = a->out_batch_stride; p.out_sd = a->out_dim_stride;
+    p.length = a->length;
+    p.state = a->state; p.st_sb = a->state_batch_stride; p.st_sd = a->state_dim_stride;
+    p.dout = a->dout; p.dout_sb = a->dout_batch_stride; p.dout_sd = a->dout_dim_stride;
+    p.dx = a->dx; p.dx_sb = a->dx_batch_stride; p.dx_sd = a->dx_dim_stride;
+    return p;
+}
+
+static int conv_nchunk(const ssm_conv1d_args* a, bool vec) {
+    const int64_t vt = vec ? (a->dtype == SSM_BF16 ? 8 : 4) : 1;
+    const int64_t nvec = (a->seqlen + vt - 1) / vt;
+    return (int)((nvec + 31) / 32);
+}
+
+int ssm_conv1d_fwd(const ssm_conv1d_args* a, void* stream) {
+    int rc = conv_common("ssm_conv1d_fwd", a, true);
+    if (rc) return rc;
+    DevInfo* di = nullptr;
+    if ((rc = device_info(&di))) return rc;
+    const bool vec = conv_vec_ok(a, false);
+    ConvParams p = conv_params(a);
+    p.dout = nullptr; p.dx = nullptr;
+    p.nchunk = conv_nchunk(a, vec);
+    cudaError_t e = launch_conv1d(p, a->dtype == SSM_BF16, (int)a->width, 0, vec, di->sms,
+                                  static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "conv1d_fwd launch");
+    return SSM_OK;
+}
+
+size_t ssm_conv1d_bwd_workspace_size(const ssm_conv1d_args* a) {
+    if (conv_common("ssm_conv1d_bwd", a, true, false)) return 0;
+    const bool vec = conv_vec_ok(a, true);
+    return (size_t)conv_nchunk(a, vec) * a->batch * a->dim * (a->width + 1) * sizeof(float);
+}
+
+int ssm_conv1d_bwd(const ssm_conv1d_args* a, void* workspace, size_t ws_bytes, void* stream) {
+    int rc = conv_common("ssm_conv1d_bwd", a, true, false);
+    if (rc) return rc;
+    if (!a->dout || !a->dx || !a->dweight)
+        return fail(SSM_ERR_INVALID, "ssm_conv1d_bwd: dout, dx and dweight are required");
+    const bool vec = conv_vec_ok(a, true);
+    const size_t need = (size_t)conv_nchunk(a, vec) * a->batch * a->dim * (a->width + 1) * sizeof(float);
+    if (!workspace || ws_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15u))
+        return fail(SSM_ERR_WORKSPACE, "ssm_conv1d_bwd: workspace needs %zu bytes, 16-byte aligned", need);
+    DevInfo* di = nullptr;
+    if ((rc = device_info(&di))) return rc;
+    ConvParams p = conv_params(a);
+    p.state = nullptr;
+    p.nchunk = conv_nchunk(a, vec);
+    p.ws = static_cast<float*>(workspace);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = launch_conv1d(p, a->dtype == SSM_BF16, (int)a->width, 1, vec, di->sms, s);
+    if (e != cudaSuccess) return cuda_fail(e, "conv1d_bwd launch");
+    e = launch_conv1d_reduce(p.ws, p.nchunk * p.batch, p.dim, (int)a->width, a->dweight, a->dweight_dim_stride,
+                             a->dbias, di->sms, s);
+    if (e != cudaSuccess) return cuda_fail(e, "conv1d_reduce launch");
+    return SSM_OK;
+}
+
+int ssm_conv1d_update(const ssm_conv1d_args* a, void* stream) {
+    int rc = conv_common("ssm_conv1d_update", a, false);
+    if (rc) return rc;
+    if (!a->state) return fail(SSM_ERR_INVALID, "ssm_conv1d_update: state is required");
+    DevInfo* di = nullptr;
+    if ((rc = device_info(&di))) return rc;
+    ConvParams p = conv_params(a);
+    cudaError_t e = launch_conv1d_update(p, a->dtype == SSM_BF16, (int)a->width, di->sms,
+                                         static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "conv1d_update launch");
     return SSM_OK;
 }
 

@@ -105,6 +105,24 @@ struct CarryParams {
     float* result;       // forward: (nslices + 1, batch, dim, dstate); reverse: (nslices, ...)
 };
 
+// Causal depthwise conv1d (conv1d.cu).
+struct ConvParams {
+    int batch, dim, seqlen;
+    int silu;
+    const void* x; int64_t x_sb, x_sd;
+    const float* w; int64_t w_sd;        // (dim, width)
+    const float* bias;                   // (dim) or null
+    void* out; int64_t out_sb, out_sd;
+    // forward only: the last width-1 inputs of every row, before token length[b] (or seqlen)
+    const int64_t* length;
+    void* state; int64_t st_sb, st_sd;
+    // backward only
+    const void* dout; int64_t dout_sb, dout_sd;
+    void* dx; int64_t dx_sb, dx_sd;
+    float* ws;                           // (nchunk * batch, dim, width + 1) partials
+    int nchunk;                          // warps (chunks of 32 vectors) per row
+};
+
 struct UpdParams {
     int batch, dim, dstate;
     int dt_softplus;

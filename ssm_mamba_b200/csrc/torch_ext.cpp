@@ -417,6 +417,98 @@ at::Tensor state_update(const at::Tensor& state, const at::Tensor& state_out, co
     return out;
 }
 
+// ---- causal depthwise conv1d ------------------------------------------------------------------
+void check_conv_weight(const at::Tensor& w, int64_t D) {
+    check_cuda(w, "weight");
+    TORCH_CHECK(w.scalar_type() == at::kFloat && w.dim() == 2 && w.size(0) == D && w.stride(1) == 1,
+                "weight must be float32 of shape (dim, width) with unit width stride");
+    TORCH_CHECK(w.size(1) >= 2 && w.size(1) <= 4, "conv width must be 2, 3 or 4");
+}
+
+ssm_conv1d_args conv_args(const at::Tensor& x, const at::Tensor& w, const std::optional<at::Tensor>& bias,
+                          bool silu) {
+    ssm_conv1d_args a;
+    memset(&a, 0, sizeof(a));
+    a.batch = x.size(0); a.dim = x.size(1); a.seqlen = x.dim() == 3 ? x.size(2) : 0; a.width = w.size(1);
+    a.dtype = dtype_code(x); a.silu = silu;
+    a.x = x.data_ptr(); a.x_batch_stride = x.stride(0); a.x_dim_stride = x.dim() == 3 ? x.stride(1) : x.stride(1);
+    a.weight = w.data_ptr<float>(); a.weight_dim_stride = w.stride(0);
+    if (bias) {
+        check_f32(*bias, "conv bias", {x.size(1)});
+        TORCH_CHECK(bias->is_contiguous(), "conv bias must be contiguous");
+        a.bias = bias->data_ptr<float>();
+    }
+    return a;
+}
+
+// out = act(conv(x)) (+ the decode context at `length` when want_state).  Returns [out, state?].
+std::vector<at::Tensor> conv1d_fwd(const at::Tensor& x, const at::Tensor& w, const std::optional<at::Tensor>& bias,
+                                   bool silu, const std::optional<at::Tensor>& length, bool want_state) {
+    check_cuda(x, "x");
+    TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1, "x must be (batch, dim, seqlen) with unit sequence stride");
+    check_conv_weight(w, x.size(1));
+    c10::cuda::CUDAGuard guard(x.device());
+    ssm_conv1d_args a = conv_args(x, w, bias, silu);
+    at::Tensor out = at::empty(x.sizes(), x.options());
+    a.out = out.data_ptr(); a.out_batch_stride = out.stride(0); a.out_dim_stride = out.stride(1);
+    at::Tensor st;
+    if (want_state) {
+        st = at::empty({x.size(0), x.size(1), w.size(1) - 1}, x.options());
+        a.state = st.data_ptr(); a.state_batch_stride = st.stride(0); a.state_dim_stride = st.stride(1);
+        if (length) {
+            TORCH_CHECK(length->is_cuda() && length->scalar_type() == at::kLong && length->dim() == 1 &&
+                            length->size(0) == x.size(0) && length->is_contiguous(),
+                        "length must be a contiguous CUDA long tensor of shape (batch,)");
+            a.length = length->data_ptr<int64_t>();
+        }
+    }
+    ok(ssm_conv1d_fwd(&a, at::cuda::getCurrentCUDAStream().stream()));
+    return {out, st};
+}
+
+// Returns [dx, dweight, dbias?].
+std::vector<at::Tensor> conv1d_bwd(const at::Tensor& x, const at::Tensor& w, const std::optional<at::Tensor>& bias,
+                                   bool silu, const at::Tensor& dout) {
+    check_cuda(x, "x");
+    TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1, "x must be (batch, dim, seqlen) with unit sequence stride");
+    check_conv_weight(w, x.size(1));
+    check_bdl(dout, "dout", x.size(0), x.size(1), x.size(2), x.scalar_type());
+    c10::cuda::CUDAGuard guard(x.device());
+    ssm_conv1d_args a = conv_args(x, w, bias, silu);
+    at::Tensor dx = at::empty(x.sizes(), x.options());
+    at::Tensor dw = at::empty(w.sizes(), w.options());
+    at::Tensor db = bias ? at::empty({x.size(1)}, w.options()) : at::Tensor();
+    a.dout = dout.data_ptr(); a.dout_batch_stride = dout.stride(0); a.dout_dim_stride = dout.stride(1);
+    a.dx = dx.data_ptr(); a.dx_batch_stride = dx.stride(0); a.dx_dim_stride = dx.stride(1);
+    a.dweight = dw.data_ptr<float>(); a.dweight_dim_stride = dw.stride(0);
+    a.dbias = bias ? db.data_ptr<float>() : nullptr;
+    const size_t n = ssm_conv1d_bwd_workspace_size(&a);
+    TORCH_CHECK(n > 0, ssm_last_error());
+    at::Tensor ws = at::empty({(int64_t)n}, x.options().dtype(at::kByte));
+    ok(ssm_conv1d_bwd(&a, ws.data_ptr(), n, at::cuda::getCurrentCUDAStream().stream()));
+    return {dx, dw, db};
+}
+
+// One decode step; `state` (batch, dim, width-1) is updated in place.  Returns out (batch, dim).
+at::Tensor conv1d_update(const at::Tensor& x, const at::Tensor& state, const at::Tensor& w,
+                         const std::optional<at::Tensor>& bias, bool silu) {
+    check_cuda(x, "x");
+    TORCH_CHECK(x.dim() == 2, "x must be (batch, dim)");
+    check_conv_weight(w, x.size(1));
+    check_cuda(state, "conv_state");
+    TORCH_CHECK(state.dim() == 3 && state.size(0) == x.size(0) && state.size(1) == x.size(1) &&
+                    state.size(2) == w.size(1) - 1 && state.stride(2) == 1 && state.scalar_type() == x.scalar_type(),
+                "conv_state must be (batch, dim, width - 1) of x's dtype with unit innermost stride");
+    c10::cuda::CUDAGuard guard(x.device());
+    ssm_conv1d_args a = conv_args(x, w, bias, silu);
+    a.x_dim_stride = x.stride(1);
+    at::Tensor out = at::empty(x.sizes(), x.options());
+    a.out = out.data_ptr(); a.out_batch_stride = out.stride(0); a.out_dim_stride = out.stride(1);
+    a.state = state.data_ptr(); a.state_batch_stride = state.stride(0); a.state_dim_stride = state.stride(1);
+    ok(ssm_conv1d_update(&a, at::cuda::getCurrentCUDAStream().stream()));
+    return out;
+}
+
 int64_t check_device_error() {
     int code = 0;
     ssm_check_device_error(&code, at::cuda::getCurrentCUDAStream().stream());
@@ -434,6 +526,9 @@ PYBIND11_MODULE(_C, m) {
     m.def("chunk_state_fwd", &chunk_state_fwd, "per-row end state from a zero start, and sum of delta");
     m.def("chunk_state_bwd", &chunk_state_bwd, "per-row gradient into the preceding state");
     m.def("carry_compose", &carry_compose, "fold per-slice carries");
+    m.def("conv1d_fwd", &conv1d_fwd, "causal depthwise conv1d (+ SiLU) forward");
+    m.def("conv1d_bwd", &conv1d_bwd, "causal depthwise conv1d (+ SiLU) backward");
+    m.def("conv1d_update", &conv1d_update, "causal depthwise conv1d (+ SiLU) decode step");
     m.def("ckpt_from_reference", &ckpt_from_reference, "compact checkpoints from reference chunk states");
     m.def("state_update", &state_update, "one decode step");
     m.def("ckpt_len", [](int64_t n) { return ssm_scan_ckpt_len(n); });

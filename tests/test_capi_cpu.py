@@ -35,7 +35,9 @@ def test_struct_layout_matches_header(tmp_path):
                                                     "dB_batch_stride", "dC_state_stride"]),
               "ssm_state_update_args": ("StateUpdateArgs", ["state", "x", "z", "out", "launch_flags"]),
               "ssm_carry_args": ("CarryArgs", ["reverse", "nstart", "A", "carry", "delta_sum", "start",
-                                               "start_stride", "result"])}
+                                               "start_stride", "result"]),
+              "ssm_conv1d_args": ("Conv1dArgs", ["silu", "x", "weight", "bias", "out", "length", "state",
+                                                 "dout", "dx", "dweight", "dbias"])}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "ssm_b200.h"', "int main(void){"]
     for cs, (_, fl) in fields.items():
         lines.append(f'printf("{cs} %zu\\n", sizeof({cs}));')
@@ -84,6 +86,10 @@ def test_validation_errors_without_gpu():
     b = capi.ScanBwdArgs()
     b.batch, b.dim, b.seqlen, b.dstate = 1, 1, 1, 16
     assert lib.ssm_scan_chunk_state_bwd(ctypes.byref(b), None, None) == capi.SSM_ERR_INVALID
+    cv = capi.Conv1dArgs()
+    cv.batch, cv.dim, cv.seqlen, cv.width, cv.dtype = 1, 4, 16, 5, capi.SSM_BF16
+    assert lib.ssm_conv1d_fwd(ctypes.byref(cv), None) == capi.SSM_ERR_INVALID
+    assert b"width" in lib.ssm_last_error()
     c = capi.CarryArgs()
     c.batch, c.dim, c.dstate, c.nslices = 1, 1, 16, 0
     assert lib.ssm_scan_carry_compose(ctypes.byref(c), None) == capi.SSM_ERR_INVALID
