@@ -371,6 +371,48 @@ def run_equal_precision(dev, forward_backward, update_apply):
     return res
 
 
+CONV = dict(batch=8, dim=1536, seqlen=2048, width=4)
+
+
+def run_conv(dev, fwd_bwd, step, label):
+    """Causal depthwise conv1d + SiLU in front of the scan (config-2 shape, bf16, width 4):
+    forward + backward of the prefill, and one decode step of the context (batch 64,
+    d_inner 5120: the config-3 width).  `fwd_bwd(x, w, b, dout)` and `step(x, state, w, b)`
+    are the implementation under test."""
+    import torch
+    Bc, Dc, Lc, K = CONV["batch"], CONV["dim"], CONV["seqlen"], CONV["width"]
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(Bc, Dc, Lc, device=dev, generator=g).to(torch.bfloat16)
+    dout = torch.randn(Bc, Dc, Lc, device=dev, generator=g).to(torch.bfloat16)
+    w = torch.randn(Dc, K, device=dev, generator=g) * 0.5
+    b = torch.randn(Dc, device=dev, generator=g)
+    ms = _time_steps(lambda: fwd_bwd(x, w, b, dout), 3, 20)
+    E = Bc * Dc * Lc
+    byts = 5 * E * 2           # forward: x in, out; backward: x, dout in, dx out
+    Bd, Dd = CFG3["batch"], CFG3["dim"]
+    xs = torch.randn(Bd, Dd, device=dev, generator=g).to(torch.bfloat16)
+    st = torch.randn(Bd, Dd, K - 1, device=dev, generator=g).to(torch.bfloat16)
+    wd = torch.randn(Dd, K, device=dev, generator=g) * 0.5
+    bd = torch.randn(Dd, device=dev, generator=g)
+    us = _time_steps(lambda: step(xs, st, wd, bd), 3, 200) * 1e3
+    return {"what": label, "prefill_fwd_bwd_ms": ms, "prefill_tb_s": byts / (ms / 1e3) / 1e12,
+            "prefill_algorithmic_bytes": byts, "decode_step_us": us,
+            "config": f"x ({Bc}, {Dc}, {Lc}) bf16, width {K}; decode ({Bd}, {Dd}) bf16 (eager launches)"}
+
+
+def _ours_conv_fwd_bwd(x, w, b, dout):
+    from ssm_mamba_b200 import causal_conv1d_fn
+    xl, wl, bl = x.requires_grad_(), w.requires_grad_(), b.requires_grad_()
+    causal_conv1d_fn(xl, wl, bl).backward(dout)
+    for t in (xl, wl, bl):
+        t.grad = None
+
+
+def _ours_conv_step(x, state, w, b):
+    from ssm_mamba_b200 import causal_conv1d_update
+    causal_conv1d_update(x, state, w, b)
+
+
 def _ours_fwd_bwd(inp):
     from ssm_mamba_b200 import SelectiveScanFn
     leaves = [t.requires_grad_() for t in (inp.u, inp.A, inp.B, inp.C, inp.D, inp.delta, inp.delta_bias)]
@@ -518,6 +560,10 @@ def run_ours(args, world, rank, local, pg):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline_sample(target_s=args.cpu_seconds)
+    conv = None
+    if world == 1 and not args.no_conv:
+        conv = run_conv(dev, _ours_conv_fwd_bwd, _ours_conv_step,
+                        "ssm_mamba_b200.causal_conv1d_fn / causal_conv1d_update")
     eq = None
     if world == 1 and not args.no_fp32:
         eq = run_equal_precision(dev, _ours_fwd_bwd, _ours_update)
@@ -546,7 +592,7 @@ def run_ours(args, world, rank, local, pg):
                          "unit": "GB/s", "frac": fwd_gbs / peak, "traffic": traffic_from_profiles("scan_fwd_kernel"),
                          "algorithmic_bytes_per_launch": fwd_bytes},
         "e2e": e2e, "gpu_launches": 3 * args.steps, "clocks": clk, "decode": decode, "long_seq": long_seq,
-        "cpu_baseline": cpu, "fp32_equal_precision": eq,
+        "cpu_baseline": cpu, "fp32_equal_precision": eq, "conv1d": conv,
     }
     return line
 
@@ -631,6 +677,25 @@ def run_reference(args, world, rank, local, pg):
                     t.grad = None
 
             line["ref_cuda_b200"] = run_equal_precision(dev, fwd_bwd, lambda *a: ref_up.apply(*a))
+
+            # the reference module's conv1d + SiLU (modules/mamba.py:137-139, 203-213): torch ops
+            import torch.nn.functional as F
+
+            def conv_fwd_bwd(x, w, b, dout):
+                xl, wl, bl = x.requires_grad_(), w.requires_grad_(), b.requires_grad_()
+                y = F.silu(F.conv1d(xl, wl.to(x.dtype)[:, None, :], bl.to(x.dtype), padding=w.shape[1] - 1,
+                                    groups=w.shape[0])[..., :x.shape[-1]])
+                y.backward(dout)
+                for t in (xl, wl, bl):
+                    t.grad = None
+
+            def conv_step(x, state, w, b):
+                window = torch.cat([state, x.unsqueeze(-1)], dim=-1)
+                state.copy_(window[:, :, 1:])
+                F.silu((window * w.to(x.dtype).unsqueeze(0)).sum(dim=-1) + b.to(x.dtype))
+
+            line["ref_conv1d_b200"] = run_conv(dev, conv_fwd_bwd, conv_step,
+                                               "reference module's torch ops: nn.Conv1d + F.silu, cat/sum step")
             line["ref_cuda_b200"]["what"] = ("reference CUDA kernels (oracle/_ref, built from its sources), "
                                              "float32, no z gate (the reference has none)")
     except Exception as e:  # context only; never fail the reference arm on it
@@ -649,6 +714,7 @@ def main():
     ap.add_argument("--no-ref-cuda", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-long", action="store_true", help="skip the long-sequence (config 5) measurement")
+    ap.add_argument("--no-conv", action="store_true", help="skip the conv1d + SiLU measurement")
     ap.add_argument("--no-fp32", action="store_true",
                     help="skip the float32 workloads timed like the reference's kernels")
     ap.add_argument("--decode-only", action="store_true", help="profiling aid: only the decode loop")

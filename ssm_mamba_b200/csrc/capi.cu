@@ -688,6 +688,8 @@ static int conv_common(const char* name, const ssm_conv1d_args* a, bool seq, boo
         return fail(SSM_ERR_INVALID, "%s: sizes must be positive", name);
     if (a->batch > (1 << 30) || a->dim > (1 << 30) || a->seqlen > (1 << 30))
         return fail(SSM_ERR_INVALID, "%s: sizes too large", name);
+    if (a->batch * a->dim >= (int64_t(1) << 31) || a->seqlen > (int64_t)65535 * 32)
+        return fail(SSM_ERR_INVALID, "%s: batch * dim must be < 2^31 and seqlen <= 2097120", name);
     if (a->width < 2 || a->width > 4) return fail(SSM_ERR_INVALID, "%s: width must be 2, 3 or 4", name);
     if (!valid_dtype(a->dtype)) return fail(SSM_ERR_INVALID, "%s: dtype must be SSM_F32 or SSM_BF16", name);
     if (!a->x || !a->weight || (need_out && !a->out))

@@ -93,15 +93,14 @@ __device__ __forceinline__ void load_window(const IT* row, int t0, int lo, int s
 template <typename IT, int VT, int K>
 __global__ void __launch_bounds__(256) conv1d_fwd_kernel(const __grid_constant__ ConvParams p) {
     const int lane = threadIdx.x & 31;
-    const int64_t nwarps_total = (int64_t)p.batch * p.dim * p.nchunk;
     const int nvec = (p.seqlen + VT - 1) / VT;
-    for (int64_t wi = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; wi < nwarps_total;
-         wi += ((int64_t)gridDim.x * blockDim.x) >> 5) {
-        const int chunk = (int)(wi % p.nchunk);
-        const int64_t row = wi / p.nchunk;
-        const int b = (int)(row / p.dim), d = (int)(row % p.dim);
+    // grid: x = blocks of 8 rows (one warp per row), y = chunks of 32 vectors
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int chunk = blockIdx.y;
+    if (row < p.batch * p.dim) {
+        const int b = row / p.dim, d = row - b * p.dim;
         const int v = chunk * 32 + lane;
-        if (v >= nvec) continue;
+        if (v < nvec) {
         const int t0 = v * VT;
         float w[K];
 #pragma unroll
@@ -119,13 +118,13 @@ __global__ void __launch_bounds__(256) conv1d_fwd_kernel(const __grid_constant__
             o[i] = p.silu ? silu_f(acc) : acc;
         }
         store_vec<IT, VT>(static_cast<IT*>(p.out) + b * p.out_sb + d * p.out_sd + t0, o);
+        }
     }
-    // the decode context: inputs at [len - (K-1), len), zero before the row start
-    if (p.state) {
-        const int64_t rows = (int64_t)p.batch * p.dim;
-        for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < rows;
-             r += (int64_t)gridDim.x * blockDim.x) {
-            const int b = (int)(r / p.dim), d = (int)(r % p.dim);
+    // the decode context: inputs at [len - (K-1), len), zero before the row start; one
+    // thread per row, in the CTAs of chunk 0
+    if (p.state && blockIdx.y == 0 && (threadIdx.x & 31) == 0 && row < p.batch * p.dim) {
+        {
+            const int b = row / p.dim, d = row - b * p.dim;
             int len = p.seqlen;
             if (p.length) {
                 const long long l = p.length[b];
@@ -148,13 +147,12 @@ __global__ void __launch_bounds__(256) conv1d_fwd_kernel(const __grid_constant__
 template <typename IT, int VT, int K>
 __global__ void __launch_bounds__(256) conv1d_bwd_kernel(const __grid_constant__ ConvParams p) {
     const int lane = threadIdx.x & 31;
-    const int64_t nwarps_total = (int64_t)p.batch * p.dim * p.nchunk;
     const int nvec = (p.seqlen + VT - 1) / VT;
-    for (int64_t wi = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; wi < nwarps_total;
-         wi += ((int64_t)gridDim.x * blockDim.x) >> 5) {
-        const int chunk = (int)(wi % p.nchunk);
-        const int64_t row = wi / p.nchunk;
-        const int b = (int)(row / p.dim), d = (int)(row % p.dim);
+    // grid: x = blocks of 8 rows (one warp per row), y = chunks of 32 vectors
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int chunk = blockIdx.y;
+    if (row < p.batch * p.dim) {
+        const int b = row / p.dim, d = row - b * p.dim;
         const int v = chunk * 32 + lane;
         const bool live = v < nvec;
         const int t0 = v * VT;
@@ -215,9 +213,9 @@ __global__ void __launch_bounds__(256) conv1d_bwd_kernel(const __grid_constant__
 // dweight[d, k] and dbias[d]: sums of the partials over (chunk, batch), in that order.
 __global__ void conv1d_reduce_kernel(const float* __restrict__ ws, int nparts, int dim, int width,
                                      float* __restrict__ dw, int64_t dw_sd, float* __restrict__ dbias) {
-    const int64_t n = (int64_t)dim * (width + 1);
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int d = (int)(i / (width + 1)), k = (int)(i % (width + 1));
+    const int n = dim * (width + 1);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int d = i / (width + 1), k = i - d * (width + 1);
         float acc = 0.f;
         for (int q = 0; q < nparts; q++) acc += ws[((int64_t)q * dim + d) * (width + 1) + k];
         if (k < width) dw[d * dw_sd + k] = acc;
@@ -229,10 +227,9 @@ __global__ void conv1d_reduce_kernel(const float* __restrict__ ws, int nparts, i
 // shifts by one and takes x.  Thread per (batch, channel); state may be updated in place.
 template <typename IT, int K>
 __global__ void __launch_bounds__(256) conv1d_update_kernel(const __grid_constant__ ConvParams p) {
-    const int64_t rows = (int64_t)p.batch * p.dim;
-    for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < rows;
-         r += (int64_t)gridDim.x * blockDim.x) {
-        const int b = (int)(r / p.dim), d = (int)(r % p.dim);
+    // grid: x = batch rows, y = tiles of 256 channels
+    const int b = blockIdx.x, d = blockIdx.y * 256 + threadIdx.x;
+    if (d < p.dim) {
         IT* sr = static_cast<IT*>(p.state) + b * p.st_sb + d * p.st_sd;
         const float x = to_f(static_cast<const IT*>(p.x)[b * p.x_sb + d * p.x_sd]);
         float win[K];
@@ -260,12 +257,12 @@ static int conv_blocks(int64_t items, int sms) {
 
 template <typename IT, int VT>
 static cudaError_t launch_conv_vt(const ConvParams& p, int width, int kind, int sms, cudaStream_t s) {
-    const int64_t warps = (int64_t)p.batch * p.dim * p.nchunk;
-    const int blocks = conv_blocks(warps * 32, sms);
+    (void)sms;
+    const dim3 grid((unsigned)((p.batch * p.dim + 7) / 8), (unsigned)p.nchunk);
 #define SSM_CONV_K(K_)                                                                         \
     if (width == K_) {                                                                         \
-        if (kind == 0) conv1d_fwd_kernel<IT, VT, K_><<<blocks, 256, 0, s>>>(p);                \
-        else conv1d_bwd_kernel<IT, VT, K_><<<blocks, 256, 0, s>>>(p);                          \
+        if (kind == 0) conv1d_fwd_kernel<IT, VT, K_><<<grid, 256, 0, s>>>(p);                  \
+        else conv1d_bwd_kernel<IT, VT, K_><<<grid, 256, 0, s>>>(p);                            \
         return cudaGetLastError();                                                             \
     }
     SSM_CONV_K(2) SSM_CONV_K(3) SSM_CONV_K(4)
@@ -291,11 +288,12 @@ cudaError_t launch_conv1d_reduce(const float* ws, int nparts, int dim, int width
 }
 
 cudaError_t launch_conv1d_update(const ConvParams& p, int is_bf16, int width, int sms, cudaStream_t stream) {
-    const int blocks = conv_blocks((int64_t)p.batch * p.dim, sms);
+    (void)sms;
+    const dim3 grid((unsigned)p.batch, (unsigned)((p.dim + 255) / 256));
 #define SSM_CONVU_K(K_)                                                                          \
     if (width == K_) {                                                                           \
-        if (is_bf16) conv1d_update_kernel<__nv_bfloat16, K_><<<blocks, 256, 0, stream>>>(p);     \
-        else conv1d_update_kernel<float, K_><<<blocks, 256, 0, stream>>>(p);                     \
+        if (is_bf16) conv1d_update_kernel<__nv_bfloat16, K_><<<grid, 256, 0, stream>>>(p);       \
+        else conv1d_update_kernel<float, K_><<<grid, 256, 0, stream>>>(p);                       \
         return cudaGetLastError();                                                               \
     }
     SSM_CONVU_K(2) SSM_CONVU_K(3) SSM_CONVU_K(4)

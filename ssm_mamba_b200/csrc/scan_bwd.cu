@@ -647,42 +647,47 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
 
 // Deterministic final sums: dB/dC over channel tiles, dA/dD/ddelta_bias over the batch.
 __global__ void scan_reduce_kernel(const __grid_constant__ ReduceParams p) {
-    const int64_t nbc = (int64_t)p.batch * p.dstate * p.seqlen;   // per quantity
-    const int64_t na = (int64_t)p.dim * p.dstate;
-    const int64_t total = 2 * nbc + na + p.dim;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        if (i < 2 * nbc) {
-            const int q = (int)(i / nbc);
-            const int64_t r = i % nbc;                 // (b, n, t) flat
-            const int64_t b = r / ((int64_t)p.dstate * p.seqlen);
-            const int64_t nt = r % ((int64_t)p.dstate * p.seqlen);
-            float acc = 0.f;
-            for (int tile = 0; tile < p.ntile_d; tile++)
-                acc += p.ws_bc[(((int64_t)tile * p.batch + b) * 2 + q) * p.dstate * p.seqlen + nt];
-            void* dst = q == 0 ? p.dB : p.dC;
-            const int64_t sb = q == 0 ? p.dB_sb : p.dC_sb, sn = q == 0 ? p.dB_sn : p.dC_sn;
-            const int64_t n = nt / p.seqlen, t = nt - n * p.seqlen;
-            const int64_t o = b * sb + n * sn + t;
-            if (p.bc_dtype == 1)
-                static_cast<__nv_bfloat16*>(dst)[o] = __float2bfloat16_rn(acc);
-            else
-                static_cast<float*>(dst)[o] = acc;
-        } else if (i < 2 * nbc + na) {
-            const int64_t r = i - 2 * nbc;             // (d, n)
-            float acc = 0.f;
-            for (int b = 0; b < p.batch; b++) acc += p.ws_a[(int64_t)b * na + r];
-            p.dA[r] = acc;
-        } else {
-            const int64_t dd = i - 2 * nbc - na;
-            float a0 = 0.f, a1 = 0.f;
-            for (int b = 0; b < p.batch; b++) {
-                a0 += p.ws_dd[((int64_t)b * p.dim + dd) * 2 + 0];
-                a1 += p.ws_dd[((int64_t)b * p.dim + dd) * 2 + 1];
-            }
-            if (p.dD) p.dD[dd] = a0;
-            if (p.ddelta_bias) p.ddelta_bias[dd] = a1;
+    // blocks [0, nbc_blocks): dB / dC, block = (token block, state, quantity * batch + b),
+    // thread = one token; the rest: dA, then dD and ddelta_bias, one value per thread
+    const int tblocks = (p.seqlen + 255) / 256;
+    const int nbc_blocks = tblocks * p.dstate * 2 * p.batch;
+    const int j = blockIdx.x;
+    if (j < nbc_blocks) {
+        const int tb = j % tblocks;
+        const int rest = j / tblocks;
+        const int n = rest % p.dstate, qb = rest / p.dstate;
+        const int q = qb & 1, b = qb >> 1;
+        const int t = tb * 256 + threadIdx.x;
+        if (t >= p.seqlen) return;
+        const int64_t plane = (int64_t)p.dstate * p.seqlen;
+        const float* src = p.ws_bc + ((int64_t)b * 2 + q) * plane + (int64_t)n * p.seqlen + t;
+        const int64_t tile_step = (int64_t)p.batch * 2 * plane;
+        float acc = 0.f;
+        for (int tile = 0; tile < p.ntile_d; tile++, src += tile_step) acc += *src;
+        void* dst = q == 0 ? p.dB : p.dC;
+        const int64_t sb = q == 0 ? p.dB_sb : p.dC_sb, sn = q == 0 ? p.dB_sn : p.dC_sn;
+        const int64_t o = b * sb + n * sn + t;
+        if (p.bc_dtype == 1)
+            static_cast<__nv_bfloat16*>(dst)[o] = __float2bfloat16_rn(acc);
+        else
+            static_cast<float*>(dst)[o] = acc;
+        return;
+    }
+    const int na = p.dim * p.dstate;
+    const int i = (j - nbc_blocks) * 256 + threadIdx.x;
+    if (i < na) {
+        float acc = 0.f;
+        for (int bb = 0; bb < p.batch; bb++) acc += p.ws_a[(int64_t)bb * na + i];
+        p.dA[i] = acc;
+    } else if (i < na + p.dim) {
+        const int dd = i - na;
+        float a0 = 0.f, a1 = 0.f;
+        for (int bb = 0; bb < p.batch; bb++) {
+            a0 += p.ws_dd[((int64_t)bb * p.dim + dd) * 2 + 0];
+            a1 += p.ws_dd[((int64_t)bb * p.dim + dd) * 2 + 1];
         }
+        if (p.dD) p.dD[dd] = a0;
+        if (p.ddelta_bias) p.ddelta_bias[dd] = a1;
     }
 }
 
@@ -756,11 +761,10 @@ cudaError_t launch_scan_bwd(const BwdParams& p, int is_bf16, int lpc, int spt, c
 }
 
 cudaError_t launch_scan_reduce(const ReduceParams& p, cudaStream_t stream) {
-    const int64_t total = 2 * (int64_t)p.batch * p.dstate * p.seqlen + (int64_t)p.dim * p.dstate + p.dim;
-    int64_t blocks = (total + 255) / 256;
-    if (blocks > 148 * 16) blocks = 148 * 16;
-    if (blocks < 1) blocks = 1;
-    scan_reduce_kernel<<<(int)blocks, 256, 0, stream>>>(p);
+    const int64_t nbc_blocks = (int64_t)((p.seqlen + 255) / 256) * p.dstate * 2 * p.batch;
+    const int64_t rest_blocks = ((int64_t)p.dim * p.dstate + p.dim + 255) / 256;
+    if (nbc_blocks + rest_blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+    scan_reduce_kernel<<<(unsigned)(nbc_blocks + rest_blocks), 256, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
