@@ -726,10 +726,11 @@ static ConvParams conv_params(const ssm_conv1d_args* a) {
     return p;
 }
 
+// chunks of 32 lanes x 4 vectors along a row (kConvRows in conv1d.cu)
 static int conv_nchunk(const ssm_conv1d_args* a, bool vec) {
     const int64_t vt = vec ? (a->dtype == SSM_BF16 ? 8 : 4) : 1;
     const int64_t nvec = (a->seqlen + vt - 1) / vt;
-    return (int)((nvec + 31) / 32);
+    return (int)((nvec + 127) / 128);
 }
 
 int ssm_conv1d_fwd(const ssm_conv1d_args* a, void* stream) {

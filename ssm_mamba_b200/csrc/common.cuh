@@ -52,6 +52,22 @@ __device__ __forceinline__ float sigmoidf_fast(float x) {
     return __fdividef(1.f, 1.f + __expf(-x));
 }
 
+// MUFU tanh (PTX tanh.approx.f32: max relative error about 2^-11)
+__device__ __forceinline__ float tanh_approx(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// logistic sigmoid for bfloat16 results: sigma(x) = (1 + tanh(x / 2)) / 2, one MUFU op
+// instead of two (exp and reciprocal); its ~2^-11 relative error is below bf16 rounding.
+// Float results use sigmoidf_fast.
+template <typename IT>
+__device__ __forceinline__ float sigmoid_io(float x) {
+    if constexpr (sizeof(IT) == 2) return fmaf(0.5f, tanh_approx(0.5f * x), 0.5f);
+    else return sigmoidf_fast(x);
+}
+
 // log(1 + e^x) = max(x, 0) + log1p(t), t = e^-|x| in (0, 1], with log1p(t) = 2 atanh(s),
 // s = t / (2 + t) in (0, 1/3], from the series 2 atanh(s) = 2 s (1 + s^2/3 + s^4/5 + ...).
 // Truncated after s^12/13 the series error is below (1/3)^14/15 ~ 1.4e-8 relative; the

@@ -59,7 +59,8 @@ __device__ __forceinline__ void store_vec(IT* p, const float (&v)[VT]) {
     }
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x * sigmoidf_fast(x); }
+template <typename IT>
+__device__ __forceinline__ float silu_f(float x) { return x * sigmoid_io<IT>(x); }
 
 // xw[j] = row[t0 + lo + j] for j in [0, NW), zero outside [0, seqlen).  VT > 1: the window
 // is covered by the 16-byte vectors v-1, v, v+1 (lo >= -VT, lo + NW <= 2 VT; seqlen is a
@@ -88,89 +89,93 @@ __device__ __forceinline__ void load_window(const IT* row, int t0, int lo, int s
     }
 }
 
-// out[t] = act(bias + sum_k w[k] x[t - (K-1) + k]).  Grid-stride over warps; warp j handles
-// chunk (j % nchunk) of row (j / nchunk), row = b * dim + d; lane = one VT-token vector.
+// Vectors per lane: a warp covers kConvRows * 32 consecutive vectors of one row, so the
+// per-row setup (indices, weights) and the backward's weight-gradient partials are shared
+// by kConvRows vectors.
+constexpr int kConvRows = 4;
+
+// out[t] = act(bias + sum_k w[k] x[t - (K-1) + k]).  Grid: x = blocks of 8 rows (one warp
+// per row, row = b * dim + d), y = chunks of 32 * kConvRows vectors; lane = every 32nd vector.
 template <typename IT, int VT, int K>
 __global__ void __launch_bounds__(256) conv1d_fwd_kernel(const __grid_constant__ ConvParams p) {
     const int lane = threadIdx.x & 31;
     const int nvec = (p.seqlen + VT - 1) / VT;
-    // grid: x = blocks of 8 rows (one warp per row), y = chunks of 32 vectors
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int chunk = blockIdx.y;
-    if (row < p.batch * p.dim) {
-        const int b = row / p.dim, d = row - b * p.dim;
-        const int v = chunk * 32 + lane;
+    if (row >= p.batch * p.dim) return;
+    const int b = row / p.dim, d = row - b * p.dim;
+    const IT* xr = static_cast<const IT*>(p.x) + b * p.x_sb + d * p.x_sd;
+    IT* outr = static_cast<IT*>(p.out) + b * p.out_sb + d * p.out_sd;
+    float w[K];
+#pragma unroll
+    for (int k = 0; k < K; k++) w[k] = __ldg(p.w + d * p.w_sd + k);
+    const float bias = p.bias ? __ldg(p.bias + d) : 0.f;
+    const int vbase = blockIdx.y * 32 * kConvRows + lane;
+#pragma unroll
+    for (int r = 0; r < kConvRows; r++) {
+        const int v = vbase + 32 * r;
         if (v < nvec) {
-        const int t0 = v * VT;
-        float w[K];
+            const int t0 = v * VT;
+            float xw[VT + K - 1];   // x[t0 - (K-1) .. t0 + VT - 1]
+            load_window<IT, VT, VT + K - 1>(xr, t0, -(K - 1), p.seqlen, xw);
+            float o[VT];
 #pragma unroll
-        for (int k = 0; k < K; k++) w[k] = __ldg(p.w + d * p.w_sd + k);
-        const float bias = p.bias ? __ldg(p.bias + d) : 0.f;
-        float xw[VT + K - 1];   // x[t0 - (K-1) .. t0 + VT - 1]
-        load_window<IT, VT, VT + K - 1>(static_cast<const IT*>(p.x) + b * p.x_sb + d * p.x_sd, t0, -(K - 1),
-                                        p.seqlen, xw);
-        float o[VT];
+            for (int i = 0; i < VT; i++) {
+                float acc = bias;
 #pragma unroll
-        for (int i = 0; i < VT; i++) {
-            float acc = bias;
-#pragma unroll
-            for (int k = 0; k < K; k++) acc = fmaf(w[k], xw[i + k], acc);
-            o[i] = p.silu ? silu_f(acc) : acc;
-        }
-        store_vec<IT, VT>(static_cast<IT*>(p.out) + b * p.out_sb + d * p.out_sd + t0, o);
+                for (int k = 0; k < K; k++) acc = fmaf(w[k], xw[i + k], acc);
+                o[i] = p.silu ? silu_f<IT>(acc) : acc;
+            }
+            store_vec<IT, VT>(outr + t0, o);
         }
     }
-    // the decode context: inputs at [len - (K-1), len), zero before the row start; one
-    // thread per row, in the CTAs of chunk 0
-    if (p.state && blockIdx.y == 0 && (threadIdx.x & 31) == 0 && row < p.batch * p.dim) {
-        {
-            const int b = row / p.dim, d = row - b * p.dim;
-            int len = p.seqlen;
-            if (p.length) {
-                const long long l = p.length[b];
-                len = l < 0 ? 0 : (l > p.seqlen ? p.seqlen : (int)l);
-            }
-            const IT* xr = static_cast<const IT*>(p.x) + b * p.x_sb + d * p.x_sd;
-            IT* sr = static_cast<IT*>(p.state) + b * p.st_sb + d * p.st_sd;
+    // the decode context: inputs at [len - (K-1), len), zero before the row start; lane 0
+    // of the warps of chunk 0
+    if (p.state && blockIdx.y == 0 && lane == 0) {
+        int len = p.seqlen;
+        if (p.length) {
+            const long long l = p.length[b];
+            len = l < 0 ? 0 : (l > p.seqlen ? p.seqlen : (int)l);
+        }
+        IT* sr = static_cast<IT*>(p.state) + b * p.st_sb + d * p.st_sd;
 #pragma unroll
-            for (int j = 0; j < K - 1; j++) {
-                const int t = len - (K - 1) + j;
-                sr[j] = t >= 0 ? xr[t] : from_f<IT>(0.f);
-            }
+        for (int j = 0; j < K - 1; j++) {
+            const int t = len - (K - 1) + j;
+            sr[j] = t >= 0 ? xr[t] : from_f<IT>(0.f);
         }
     }
 }
 
 // Backward.  g[t] = dout[t] * act'(pre[t]); dx[t] = sum_k w[k] g[t + (K-1) - k];
-// dw[k] = sum g[t] x[t - (K-1) + k]; dbias = sum g[t].  Per-warp partials of dw, dbias go to
-// ws[(chunk * batch + b), d, :].
+// dw[k] = sum g[t] x[t - (K-1) + k]; dbias = sum g[t].  The warp's partials of dw, dbias go
+// to ws[(chunk * batch + b), d, :].
 template <typename IT, int VT, int K>
 __global__ void __launch_bounds__(256) conv1d_bwd_kernel(const __grid_constant__ ConvParams p) {
     const int lane = threadIdx.x & 31;
     const int nvec = (p.seqlen + VT - 1) / VT;
-    // grid: x = blocks of 8 rows (one warp per row), y = chunks of 32 vectors
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int chunk = blockIdx.y;
-    if (row < p.batch * p.dim) {
-        const int b = row / p.dim, d = row - b * p.dim;
-        const int v = chunk * 32 + lane;
-        const bool live = v < nvec;
-        const int t0 = v * VT;
-        float w[K];
+    if (row >= p.batch * p.dim) return;   // whole warps: the shuffles below see full warps
+    const int b = row / p.dim, d = row - b * p.dim;
+    const IT* xr = static_cast<const IT*>(p.x) + b * p.x_sb + d * p.x_sd;
+    const IT* gr = static_cast<const IT*>(p.dout) + b * p.dout_sb + d * p.dout_sd;
+    IT* dxr = static_cast<IT*>(p.dx) + b * p.dx_sb + d * p.dx_sd;
+    float w[K];
 #pragma unroll
-        for (int k = 0; k < K; k++) w[k] = __ldg(p.w + d * p.w_sd + k);
-        const float bias = p.bias ? __ldg(p.bias + d) : 0.f;
-        float part[K + 1];
+    for (int k = 0; k < K; k++) w[k] = __ldg(p.w + d * p.w_sd + k);
+    const float bias = p.bias ? __ldg(p.bias + d) : 0.f;
+    float part[K + 1];
 #pragma unroll
-        for (int k = 0; k <= K; k++) part[k] = 0.f;
-        if (live) {
+    for (int k = 0; k <= K; k++) part[k] = 0.f;
+    const int vbase = blockIdx.y * 32 * kConvRows + lane;
+#pragma unroll
+    for (int r = 0; r < kConvRows; r++) {
+        const int v = vbase + 32 * r;
+        if (v < nvec) {
+            const int t0 = v * VT;
             constexpr int NG = VT + K - 1;          // tokens t0 .. t0 + VT + K - 2
             float xw[NG + K - 1];                   // x[t0 - (K-1) .. t0 + VT + K - 2]
             float gw[NG];                           // dout[t0 .. t0 + VT + K - 2]
-            load_window<IT, VT, NG + K - 1>(static_cast<const IT*>(p.x) + b * p.x_sb + d * p.x_sd, t0, -(K - 1),
-                                            p.seqlen, xw);
-            load_window<IT, VT, NG>(static_cast<const IT*>(p.dout) + b * p.dout_sb + d * p.dout_sd, t0, 0,
-                                    p.seqlen, gw);
+            load_window<IT, VT, NG + K - 1>(xr, t0, -(K - 1), p.seqlen, xw);
+            load_window<IT, VT, NG>(gr, t0, 0, p.seqlen, gw);
             float g[NG];
 #pragma unroll
             for (int i = 0; i < NG; i++) {
@@ -179,7 +184,7 @@ __global__ void __launch_bounds__(256) conv1d_bwd_kernel(const __grid_constant__
                 for (int k = 0; k < K; k++) pre = fmaf(w[k], xw[i + k], pre);
                 float gi = gw[i];
                 if (p.silu) {
-                    const float s = sigmoidf_fast(pre);
+                    const float s = sigmoid_io<IT>(pre);
                     gi *= s * (1.f + pre * (1.f - s));
                 }
                 g[i] = (t0 + i < p.seqlen) ? gi : 0.f;
@@ -195,29 +200,34 @@ __global__ void __launch_bounds__(256) conv1d_bwd_kernel(const __grid_constant__
                 for (int k = 0; k < K; k++) part[k] = fmaf(g[i], xw[i + k], part[k]);
                 part[K] += g[i];
             }
-            store_vec<IT, VT>(static_cast<IT*>(p.dx) + b * p.dx_sb + d * p.dx_sd + t0, dxv);
+            store_vec<IT, VT>(dxr + t0, dxv);
         }
+    }
 #pragma unroll
-        for (int k = 0; k <= K; k++) {
+    for (int k = 0; k <= K; k++) {
 #pragma unroll
-            for (int m = 16; m >= 1; m >>= 1) part[k] += __shfl_xor_sync(0xffffffffu, part[k], m);
-        }
-        if (lane == 0) {
-            float* dst = p.ws + (((int64_t)chunk * p.batch + b) * p.dim + d) * (K + 1);
+        for (int m = 16; m >= 1; m >>= 1) part[k] += __shfl_xor_sync(0xffffffffu, part[k], m);
+    }
+    if (lane == 0) {
+        float* dst = p.ws + (((int64_t)blockIdx.y * p.batch + b) * p.dim + d) * (K + 1);
 #pragma unroll
-            for (int k = 0; k <= K; k++) dst[k] = part[k];
-        }
+        for (int k = 0; k <= K; k++) dst[k] = part[k];
     }
 }
 
-// dweight[d, k] and dbias[d]: sums of the partials over (chunk, batch), in that order.
+// dweight[d, k] and dbias[d]: sums of the nparts partials, one warp per value; lane j sums
+// partials j, j + 32, ... and the warp adds the lanes in a fixed tree (deterministic).
 __global__ void conv1d_reduce_kernel(const float* __restrict__ ws, int nparts, int dim, int width,
                                      float* __restrict__ dw, int64_t dw_sd, float* __restrict__ dbias) {
-    const int n = dim * (width + 1);
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const int d = i / (width + 1), k = i - d * (width + 1);
-        float acc = 0.f;
-        for (int q = 0; q < nparts; q++) acc += ws[((int64_t)q * dim + d) * (width + 1) + k];
+    const int lane = threadIdx.x & 31;
+    const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);   // (d, k) flat
+    if (i >= dim * (width + 1)) return;
+    const int d = i / (width + 1), k = i - d * (width + 1);
+    float acc = 0.f;
+    for (int q = lane; q < nparts; q += 32) acc += ws[((int64_t)q * dim + d) * (width + 1) + k];
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+    if (lane == 0) {
         if (k < width) dw[d * dw_sd + k] = acc;
         else if (dbias) dbias[d] = acc;
     }
@@ -241,20 +251,13 @@ __global__ void __launch_bounds__(256) conv1d_update_kernel(const __grid_constan
         for (int k = 0; k < K; k++) acc = fmaf(__ldg(p.w + d * p.w_sd + k), win[k], acc);
 #pragma unroll
         for (int k = 0; k < K - 1; k++) sr[k] = from_f<IT>(win[k + 1]);
-        static_cast<IT*>(p.out)[b * p.out_sb + d * p.out_sd] = from_f<IT>(p.silu ? silu_f(acc) : acc);
+        static_cast<IT*>(p.out)[b * p.out_sb + d * p.out_sd] = from_f<IT>(p.silu ? silu_f<IT>(acc) : acc);
     }
 }
 
 // ---------------------------------------------------------------------------------------
 // launch
 // ---------------------------------------------------------------------------------------
-static int conv_blocks(int64_t items, int sms) {
-    int64_t blocks = (items + 255) / 256;
-    const int64_t cap = (int64_t)sms * 16;
-    if (blocks > cap) blocks = cap;
-    return blocks < 1 ? 1 : (int)blocks;
-}
-
 template <typename IT, int VT>
 static cudaError_t launch_conv_vt(const ConvParams& p, int width, int kind, int sms, cudaStream_t s) {
     (void)sms;
@@ -282,8 +285,9 @@ cudaError_t launch_conv1d(const ConvParams& p, int is_bf16, int width, int kind,
 
 cudaError_t launch_conv1d_reduce(const float* ws, int nparts, int dim, int width, float* dw, int64_t dw_sd,
                                  float* dbias, int sms, cudaStream_t stream) {
-    const int blocks = conv_blocks((int64_t)dim * (width + 1), sms);
-    conv1d_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, nparts, dim, width, dw, dw_sd, dbias);
+    (void)sms;
+    const int warps = dim * (width + 1);
+    conv1d_reduce_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(ws, nparts, dim, width, dw, dw_sd, dbias);
     return cudaGetLastError();
 }
 

@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
                 Vec4<IT>::load(smem + S.y + off, yv);
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    const float sg = sigmoidf_fast(zv[j]);
+                    const float sg = sigmoid_io<IT>(zv[j]);
                     dz[j] = t0 + t4 + j < Rskip ? dv[j] * yv[j] * sg * (1.f + zv[j] * (1.f - sg)) : 0.f;
                     dv[j] = dv[j] * zv[j] * sg;
                 }

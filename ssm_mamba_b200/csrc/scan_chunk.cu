@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(128, 4) scan_chunk_kernel(const __grid_constan
                 const float x = dr[k] + bias;
                 dl[k] = p.delta_softplus ? softplus_series(x) : x;
                 if (REV)
-                    xo[k] = has_z ? xv[k] * zv[k] * sigmoidf_fast(zv[k]) : xv[k];
+                    xo[k] = has_z ? xv[k] * zv[k] * sigmoid_io<IT>(zv[k]) : xv[k];
                 else
                     xo[k] = dl[k] * xv[k];
                 if (tile_short && t0 + t4 + k >= Lq) { dl[k] = 0.f; xo[k] = 0.f; }

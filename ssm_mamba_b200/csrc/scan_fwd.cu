@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
 #pragma unroll
                         for (int j = 0; j < 4; j++) {
                             yt[j] = fmaf(Dd, uv[j], yv[r4 + j]);
-                            o[j] = has_z ? yt[j] * zv[j] * sigmoidf_fast(zv[j]) : yt[j];
+                            o[j] = has_z ? yt[j] * zv[j] * sigmoid_io<IT>(zv[j]) : yt[j];
                         }
                         Vec4<IT>::store(so + off, o);
                         if (want_y) Vec4<IT>::store(sy + off, yt);
@@ -367,7 +367,7 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
                         float o = yt;
                         if (has_z) {
                             const float zv = to_f(*reinterpret_cast<const IT*>(sz + off));
-                            o = yt * zv * sigmoidf_fast(zv);
+                            o = yt * zv * sigmoid_io<IT>(zv);
                         }
                         *reinterpret_cast<IT*>(so + off) = from_f<IT>(o);
                         if (want_y) *reinterpret_cast<IT*>(sy + off) = from_f<IT>(yt);

@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(256) state_update_kernel(const __grid_constant
     }
     if (live && g == 0) {
         float o = fmaf(Dv, xv, y);
-        if (p.z) o = o * zv * sigmoidf_fast(zv);
+        if (p.z) o = o * zv * sigmoid_io<IT>(zv);
         static_cast<IT*>(p.out)[(int64_t)b * p.out_sb + dd] = from_f<IT>(o);
     }
 }
