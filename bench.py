@@ -414,6 +414,74 @@ def run_conv(dev, fwd_bwd, step, label):
                       "CUDA graph"}
 
 
+LAYER = dict(batch=64, model=2560, inner=5120, state=16, rank=160, width=4)
+
+
+def _layer_weights(dev, dtype, seed=11):
+    """Random weights of a Mamba-2.8B-width layer (ssm_mamba_b200.decode.MambaLayerWeights)."""
+    import torch
+    from ssm_mamba_b200.decode import MambaLayerWeights
+    from ssm_mamba_b200.workloads import dt_bias_init, s4d_real_A
+    c = LAYER
+    g = torch.Generator(device=dev).manual_seed(seed)
+    r = lambda *sh, sc=0.02: (torch.randn(*sh, device=dev, generator=g) * sc)  # noqa: E731
+    return MambaLayerWeights(
+        in_proj_weight=r(2 * c["inner"], c["model"]).to(dtype), conv_weight=r(c["inner"], c["width"], sc=0.3),
+        x_proj_weight=r(c["rank"] + 2 * c["state"], c["inner"]).to(dtype),
+        dt_proj_weight=r(c["inner"], c["rank"], sc=0.08).to(dtype), dt_proj_bias=dt_bias_init(c["inner"], g, dev),
+        A=s4d_real_A(c["inner"], c["state"], dev), D=torch.ones(c["inner"], device=dev),
+        out_proj_weight=r(c["model"], c["inner"]).to(dtype), conv_bias=r(c["inner"]))
+
+
+def run_decode_layer(dev, step_factory, label):
+    """tokens/s of a whole Mamba layer's decoding step (in_proj, conv step, x_proj, dt_proj,
+    state update, gate, out_proj) at the Mamba-2.8B width, batch 64: `step_factory()`
+    returns (step(hidden) -> out, graphable).  Eager and (when graphable) CUDA-graph
+    replays, 128 steps each."""
+    import torch
+    step, graphable = step_factory()
+    Bsz = LAYER["batch"]
+    g = torch.Generator(device=dev).manual_seed(3)
+    hid = [torch.randn(Bsz, LAYER["model"], device=dev, generator=g).to(step.dtype) for _ in range(8)]
+    n = 128
+
+    def eager():
+        for i in range(n):
+            step(hid[i % 8])
+
+    us_eager = _time_steps(eager, 1, 2) * 1e3 / n
+    res = {"what": label, "eager_us_per_step": us_eager, "eager_tokens_per_s": Bsz / (us_eager / 1e6)}
+    if graphable:
+        from ssm_mamba_b200.decode import GraphedStep
+        gs = GraphedStep(step, [hid[0]], preserve=step.caches)
+
+        def graphed():
+            for i in range(n):
+                gs(hid[i % 8])
+
+        us = _time_steps(graphed, 1, 2) * 1e3 / n
+        res.update({"graph_us_per_step": us, "graph_tokens_per_s": Bsz / (us / 1e6)})
+        del gs
+    res["config"] = ("one Mamba layer, model 2560, inner 5120, state 16, rank 160, conv width 4, batch 64, "
+                     f"{'bf16' if step.dtype == torch.bfloat16 else 'fp32'} weights and activations")
+    return res
+
+
+def _ours_layer_factory(dev, dtype):
+    def make():
+        from ssm_mamba_b200.decode import MambaLayerCache, mamba_layer_step
+        w = _layer_weights(dev, dtype)
+        cache = MambaLayerCache.zeros(w, LAYER["batch"], dtype)
+
+        def step(hidden):
+            return mamba_layer_step(w, cache, hidden)
+
+        step.dtype = dtype
+        step.caches = [cache.conv_state, cache.ssm_state]
+        return step, True
+    return make
+
+
 def _ours_conv_fwd_bwd(x, w, b, dout):
     # the extension's entry points (what causal_conv1d_fn's forward and backward call)
     from ssm_mamba_b200._ext import _C
@@ -577,6 +645,12 @@ def run_ours(args, world, rank, local, pg):
     if world == 1 and not args.no_conv:
         conv = run_conv(dev, _ours_conv_fwd_bwd, _ours_conv_step,
                         "ssm_mamba_b200.causal_conv1d_fn / causal_conv1d_update")
+    layer = None
+    if world == 1 and not args.no_layer:
+        layer = {"bf16": run_decode_layer(dev, _ours_layer_factory(dev, torch.bfloat16),
+                                          "ssm_mamba_b200.decode.mamba_layer_step (+ GraphedStep)"),
+                 "fp32": run_decode_layer(dev, _ours_layer_factory(dev, torch.float32),
+                                          "ssm_mamba_b200.decode.mamba_layer_step (+ GraphedStep)")}
     eq = None
     if world == 1 and not args.no_fp32:
         eq = run_equal_precision(dev, _ours_fwd_bwd, _ours_update)
@@ -605,7 +679,7 @@ def run_ours(args, world, rank, local, pg):
                          "unit": "GB/s", "frac": fwd_gbs / peak, "traffic": traffic_from_profiles("scan_fwd_kernel"),
                          "algorithmic_bytes_per_launch": fwd_bytes},
         "e2e": e2e, "gpu_launches": 3 * args.steps, "clocks": clk, "decode": decode, "long_seq": long_seq,
-        "cpu_baseline": cpu, "fp32_equal_precision": eq, "conv1d": conv,
+        "cpu_baseline": cpu, "fp32_equal_precision": eq, "conv1d": conv, "decode_layer": layer,
     }
     return line
 
@@ -709,6 +783,32 @@ def run_reference(args, world, rank, local, pg):
 
             line["ref_conv1d_b200"] = run_conv(dev, conv_fwd_bwd, conv_step,
                                                "reference module's torch ops: nn.Conv1d + F.silu, cat/sum step")
+
+            # the reference module's decoding step (modules/mamba.py:188-241): torch ops with the
+            # reference's selective_update extension (float32 only), a new state every step
+            def ref_layer_factory():
+                w = _layer_weights(dev, torch.float32)
+                Bsz = LAYER["batch"]
+                st = {"ctx": torch.zeros(Bsz, LAYER["inner"], LAYER["width"] - 1, device=dev),
+                      "h": torch.zeros(Bsz, LAYER["inner"], LAYER["state"], device=dev)}
+
+                def step(hidden):
+                    xz = F.linear(hidden, w.in_proj_weight)
+                    x, gate = xz.chunk(2, dim=-1)
+                    window = torch.cat([st["ctx"], x.unsqueeze(-1)], dim=-1)
+                    st["ctx"] = window[:, :, 1:]
+                    x = F.silu((window * w.conv_weight.unsqueeze(0)).sum(dim=-1) + w.conv_bias)
+                    delta, Bm, Cm = torch.split(F.linear(x, w.x_proj_weight), [w.rank, w.state, w.state], dim=-1)
+                    delta = (w.dt_proj_weight @ delta.t()).t().contiguous()
+                    y, st["h"] = ref_up.apply(x.contiguous(), w.A, Bm.contiguous(), Cm.contiguous(), w.D, delta,
+                                              w.dt_proj_bias, st["h"])
+                    return F.linear(y * F.silu(gate), w.out_proj_weight)
+
+                step.dtype = torch.float32
+                return step, False
+
+            line["ref_decode_layer_b200"] = run_decode_layer(
+                dev, ref_layer_factory, "reference module's step: torch ops + its selective_update kernel, fp32")
             line["ref_cuda_b200"]["what"] = ("reference CUDA kernels (oracle/_ref, built from its sources), "
                                              "float32, no z gate (the reference has none)")
     except Exception as e:  # context only; never fail the reference arm on it
@@ -728,6 +828,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-long", action="store_true", help="skip the long-sequence (config 5) measurement")
     ap.add_argument("--no-conv", action="store_true", help="skip the conv1d + SiLU measurement")
+    ap.add_argument("--no-layer", action="store_true", help="skip the whole-layer decode measurement")
     ap.add_argument("--no-fp32", action="store_true",
                     help="skip the float32 workloads timed like the reference's kernels")
     ap.add_argument("--decode-only", action="store_true", help="profiling aid: only the decode loop")

@@ -67,7 +67,9 @@ def selective_state_update(state: torch.Tensor, x: torch.Tensor, dt: torch.Tenso
     A = A.float()
     D = D.float() if D is not None else None
     dt_bias = dt_bias.float() if dt_bias is not None else None
-    x, dt, A, B, C, D, z, dt_bias = map(ensure_contiguous, (x, dt, A, B, C, D, z, dt_bias))
+    # the kernel takes any batch stride: only a non-unit innermost stride needs a copy
+    x, dt, B, C, z = (t if t is None or t.stride(-1) == 1 else t.contiguous() for t in (x, dt, B, C, z))
+    A, D, dt_bias = map(ensure_contiguous, (A, D, dt_bias))
     return _C.state_update(state, state, x, dt, A, B, C, D, z, dt_bias, bool(dt_softplus))
 
 
