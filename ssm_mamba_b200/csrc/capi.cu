@@ -25,6 +25,7 @@ cudaError_t launch_scan_bwd(const BwdParams& p, int is_bf16, int lpc, int spt, c
                             cudaStream_t stream);
 cudaError_t launch_scan_reduce(const ReduceParams& p, cudaStream_t stream);
 cudaError_t launch_state_update(const UpdParams& p, int is_bf16, int lpc, int spt, cudaStream_t stream);
+cudaError_t launch_state_update_stream(const UpdParams& p, int is_bf16, int lpc, int sms, cudaStream_t stream);
 cudaError_t launch_scan_chunk(const ChunkParams& p, int is_bf16, int lpc, int spt, int reverse,
                               const CUtensorMap* maps, cudaStream_t stream);
 int chunk_occupancy(int is_bf16, int lpc, int spt, int reverse, int dt, int has_z);
@@ -569,6 +570,31 @@ int ssm_state_update(const ssm_state_update_args* a, void* stream_) {
     p.dt_bias = a->dt_bias;
     p.out = a->out; p.out_sb = a->out_batch_stride;
     p.pdl = (a->launch_flags & SSM_LAUNCH_PDL) != 0;
+    // Streamed kernel (bulk-copy pipeline over persistent CTAs) for contiguous, 16-byte
+    // aligned layouts with dstate 8, 16 or 32 and dim a multiple of its channel tile;
+    // SSM_DEC_STREAM=0 turns it off for comparisons.
+    {
+        const int64_t N = a->dstate, es = a->dtype == SSM_BF16 ? 2 : 4;
+        const int lpc = (int)(N / 8), rpb = lpc > 0 ? 256 / lpc : 0;
+        auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+        const char* env = getenv("SSM_DEC_STREAM");
+        const bool ok = (N == 8 || N == 16 || N == 32) && a->dim % rpb == 0 && !(env && env[0] == '0') &&
+                        a->state_dim_stride == N && a->state_out_dim_stride == N && a->A_dim_stride == N &&
+                        ((a->state_batch_stride * 4) & 15) == 0 && ((a->state_out_batch_stride * 4) & 15) == 0 &&
+                        ((a->x_batch_stride * es) & 15) == 0 && ((a->dt_batch_stride * es) & 15) == 0 &&
+                        (!a->z || ((a->z_batch_stride * es) & 15) == 0) && ((a->B_batch_stride * es) & 15) == 0 &&
+                        ((a->C_batch_stride * es) & 15) == 0 && al(a->state) && al(a->state_out) && al(a->A) &&
+                        al(a->x) && al(a->dt) && (!a->z || al(a->z)) && al(a->B) && al(a->C);
+        if (ok) {
+            DevInfo* di = nullptr;
+            int rc = device_info(&di);
+            if (rc) return rc;
+            p.err = di->err;
+            cudaError_t e = launch_state_update_stream(p, a->dtype == SSM_BF16, lpc, di->sms, stream);
+            if (e != cudaSuccess) return cuda_fail(e, "state_update_stream launch");
+            return SSM_OK;
+        }
+    }
     cudaError_t e = launch_state_update(p, a->dtype == SSM_BF16, sp.lpc, sp.spt, stream);
     if (e != cudaSuccess) return cuda_fail(e, "state_update launch");
     return SSM_OK;

@@ -235,6 +235,16 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // 3-D tiled TMA load, global -> shared, completion counted on `bar` (no multicast).
+// 1-D bulk copy global -> shared completing on an mbarrier (both addresses 16-byte aligned,
+// bytes a multiple of 16); no multicast
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2) {
     asm volatile(

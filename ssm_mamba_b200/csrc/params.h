@@ -138,6 +138,7 @@ struct UpdParams {
     const float* dt_bias;
     void* out; int64_t out_sb;
     int pdl;             // launch with programmatic dependent launch
+    int* err;            // device error word (streamed kernel's bounded waits)
 };
 
 }  // namespace ssm

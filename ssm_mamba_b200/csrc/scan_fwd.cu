@@ -46,33 +46,22 @@ __device__ __forceinline__ void store_ckpt_row(float* dst, const float2 (&h)[SPT
     }
 }
 
-// State checkpoint k of channel d: compact (batch, nck, dim, dstate) fp32 states, or the
-// reference's interleaved (prod, state) chunk carries.  A free function rather than a
-// capturing lambda so that h and A2 stay in registers.
+// Reference-layout chunk carry k of channel d: the interleaved (prod, state) pairs of
+// selective_scan.cpp:271-274, prod = exp(A * sum of delta so far).  (Compact checkpoints go
+// through store_ckpt_row.)  A free function rather than a capturing lambda so that h and A2
+// stay in registers.
 template <int SPT>
 __device__ __forceinline__ void fwd_write_ckpt(const FwdParams& p, const float2 (&h)[SPT / 2],
                                                const float2 (&A2)[SPT / 2], float Ssum, int b, int d, int g,
                                                int k) {
     const int N = p.dstate;
-    if (p.ckpt_format == 0) {
-        float* dst = p.ckpt + (((int64_t)b * p.nck + k) * p.dim + d) * N + g * SPT;
-        if (g * SPT + SPT <= N && (N & 3) == 0) {
+    float* dst = p.ckpt + (((int64_t)b * p.dim + d) * p.nck + k) * 2 * N;
 #pragma unroll
-            for (int q = 0; q < SPT / 2; q++) *reinterpret_cast<float2*>(dst + 2 * q) = h[q];
-        } else {
-#pragma unroll
-            for (int s = 0; s < SPT; s++)
-                if (g * SPT + s < N) dst[s] = (s & 1) ? h[s / 2].y : h[s / 2].x;
-        }
-    } else {
-        float* dst = p.ckpt + (((int64_t)b * p.dim + d) * p.nck + k) * 2 * N;
-#pragma unroll
-        for (int s = 0; s < SPT; s++) {
-            const int n = g * SPT + s;
-            if (n < N) {
-                dst[2 * n] = ex2(((s & 1) ? A2[s / 2].y : A2[s / 2].x) * Ssum);
-                dst[2 * n + 1] = (s & 1) ? h[s / 2].y : h[s / 2].x;
-            }
+    for (int s = 0; s < SPT; s++) {
+        const int n = g * SPT + s;
+        if (n < N) {
+            dst[2 * n] = ex2(((s & 1) ? A2[s / 2].y : A2[s / 2].x) * Ssum);
+            dst[2 * n + 1] = (s & 1) ? h[s / 2].y : h[s / 2].x;
         }
     }
 }

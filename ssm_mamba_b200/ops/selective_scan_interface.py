@@ -30,6 +30,15 @@ def ensure_contiguous(x: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
     return x.contiguous()
 
 
+def unit_token_stride(x: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    """x itself when its innermost (token) stride is 1 -- the kernels take any batch and
+    channel strides, e.g. delta straight from a dt_proj GEMM viewed as (batch, dim, L) --
+    else a contiguous copy."""
+    if x is None or x.stride(-1) == 1:
+        return x
+    return x.contiguous()
+
+
 def _padding_right(padding_size: Optional[str]) -> bool:
     # The reference's C++ treats a missing padding side as "right"
     # (csrc/selective_scan/selective_scan.cpp:248, 335).
@@ -151,7 +160,7 @@ class _SelectiveScanExt(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout, *rest):
         u, delta, A, B, C, D, z, delta_bias, y, ckpt = ctx.saved_tensors
-        dout = ensure_contiguous(dout)
+        dout = unit_token_stride(dout)
         du, ddelta, dA, dB, dC, dD, ddelta_bias, dz, _ = _C.scan_bwd(
             u, delta, A, B, C, D, z, delta_bias, None, None, True, ctx.delta_softplus, y, ckpt,
             dout, None)
@@ -188,8 +197,8 @@ def selective_scan_fn(u: torch.Tensor, delta: torch.Tensor, A: torch.Tensor, B: 
     A = A.float()
     D = D.float() if D is not None else None
     delta_bias = delta_bias.float() if delta_bias is not None else None
-    u, delta, A, B, C, D, z, delta_bias = map(
-        ensure_contiguous, (u, delta, A, B, C, D, z, delta_bias))
+    u, delta, B, C, z = map(unit_token_stride, (u, delta, B, C, z))
+    A, D, delta_bias = map(ensure_contiguous, (A, D, delta_bias))
     S = _segments_for(u, A.shape[1])
     if S > 1:
         out, h_last = sliced_scan(u, delta, A, B, C, D, z, delta_bias, None, bool(delta_softplus), segments=S)
@@ -198,4 +207,4 @@ def selective_scan_fn(u: torch.Tensor, delta: torch.Tensor, A: torch.Tensor, B: 
                                    return_last_state)
 
 
-__all__ = ["SelectiveScanFn", "selective_scan_fn", "ensure_contiguous"]
+__all__ = ["SelectiveScanFn", "selective_scan_fn", "ensure_contiguous", "unit_token_stride"]

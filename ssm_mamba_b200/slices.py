@@ -64,11 +64,14 @@ def plan_segments(batch: int, dim: int, seqlen: int, dstate: int, sms: int = 148
 
 
 def segment_view(t: Optional[torch.Tensor], s: int) -> Optional[torch.Tensor]:
-    """(1, X, L) contiguous -> (s, X, L // s) view with batch stride L // s; s == 1: t."""
+    """(1, X, L) with unit token stride -> (s, X, L // s) view with batch stride L // s and
+    the channel stride of t; s == 1: t."""
     if t is None or s == 1:
         return t
     _, x, L = t.shape
-    return t.as_strided((s, x, L // s), (L // s, L, 1), t.storage_offset())
+    if t.stride(2) != 1:
+        raise ValueError("segment_view needs a unit token stride")
+    return t.as_strided((s, x, L // s), (L // s, t.stride(1), 1), t.storage_offset())
 
 
 class SliceGroup:

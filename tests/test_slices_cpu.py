@@ -88,6 +88,13 @@ def test_segment_view_is_a_view():
     v = segment_view(t, 4)
     assert v.shape == (4, 6, 2) and v.data_ptr() == t.data_ptr()
     assert torch.equal(v[1, 2], t[0, 2, 2:4])
+    # a channel-strided input (the first half of an in_proj output) keeps its channel stride
+    big = torch.arange(2 * 6 * 8, dtype=torch.float32).reshape(1, 12, 8)
+    half = big[:, :6]
+    vh = segment_view(half, 2)
+    assert vh.stride() == (4, 8, 1) and torch.equal(vh[1, 5], half[0, 5, 4:8])
+    with pytest.raises(ValueError):
+        segment_view(big.transpose(1, 2), 2)
 
 
 @pytest.mark.parametrize("segments", [1, 2, 4])

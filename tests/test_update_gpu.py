@@ -63,3 +63,40 @@ def test_reference_update_api_is_out_of_place(cuda):
                                              np64(dec.B[0]), np64(dec.C[0]), np64(dec.D), None, np64(dec.dt_bias), True)
     assert_close(out, ref_out, 1e-4, 1e-5, name="out")
     assert_close(new_h, ref_state, 1e-4, 1e-5, name="new_h")
+
+
+@pytest.mark.parametrize("B,D,N,dtype,gate", [
+    (5, 256, 16, torch.bfloat16, True),     # streamed: tiles of 128 channels
+    (3, 512, 8, torch.float32, False),      # streamed: tiles of 256 channels
+    (2, 128, 32, torch.float32, True),      # streamed: tiles of 64 channels
+    (4, 200, 16, torch.bfloat16, True),     # dim not a multiple of the tile: the per-CTA kernel
+])
+def test_streamed_and_per_cta_decode_kernels_agree(cuda, monkeypatch, B, D, N, dtype, gate):
+    """The streamed decode kernel (bulk-copy pipeline, picked for contiguous 16-byte aligned
+    layouts) and the per-CTA kernel (SSM_DEC_STREAM=0) give the oracle's step, out of place
+    and in place, over 4 consecutive steps."""
+    dec = decode_inputs(B, D, N, 4, dtype, seed=D + N, device=cuda)
+    results = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("SSM_DEC_STREAM", mode)
+        state = dec.state.clone()
+        outs = []
+        for s in range(4):
+            out = torch.empty(B, D, dtype=dtype, device=cuda)
+            a = capi.fill_update(state, state, dec.x[s], dec.dt[s], dec.A, dec.B[s], dec.C[s], out, D=dec.D,
+                                 z=dec.z[s] if gate else None, dt_bias=dec.dt_bias, dt_softplus=True)
+            capi.call_update(a)
+            outs.append(out)
+        torch.cuda.synchronize()
+        results[mode] = (torch.stack(outs), state)
+    ref_state = np64(dec.state)
+    for s in range(4):
+        ref_out, ref_state = oracle.state_update(ref_state, np64(dec.x[s]), np64(dec.dt[s]), np64(dec.A),
+                                                 np64(dec.B[s]), np64(dec.C[s]), np64(dec.D),
+                                                 np64(dec.z[s]) if gate else None, np64(dec.dt_bias), True)
+        tol = (1e-4, 1e-5) if dtype == torch.float32 else (1e-2, 5e-2)
+        for mode in ("1", "0"):
+            assert_close(results[mode][0][s], ref_out, *tol, name=f"mode {mode} step {s} out")
+    for mode in ("1", "0"):
+        assert_close(results[mode][1], ref_state, 1e-4, 1e-5, name=f"mode {mode} state")
+    assert_close(results["1"][1], results["0"][1], 0, 0, name="streamed vs per-CTA state")
