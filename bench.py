@@ -482,6 +482,104 @@ def _ours_layer_factory(dev, dtype):
     return make
 
 
+CFG4 = dict(batch=4, seqlen=2048, model=2560, layers=64, inner=5120, state=16, rank=160, width=4,
+            vocab=50288, ids=50280)
+
+
+def _lm_weights(dev, dtype, seed=3):
+    """Random-init Mamba-2.8B-architecture causal LM (models/causal_lm.py:27-98 with the
+    modules/block.py and modules/mamba.py:34-79 defaults): every projection, the conv and
+    the tied embedding ~ N(0, 0.02) in `dtype`; dt_proj bias from dt ~ logUniform(1e-3, 1e-1);
+    A from the S4D-real log_A; D = 1; RMSNorm weights 0 (the norm scales by 1 + weight); no
+    biases.  Returns (embedding, [(norm weight, MambaLayerWeights)], final norm weight)."""
+    import torch
+    from ssm_mamba_b200.decode import MambaLayerWeights
+    from ssm_mamba_b200.workloads import dt_bias_init, s4d_real_A
+    c = CFG4
+    g = torch.Generator(device=dev).manual_seed(seed)
+    r = lambda *sh: torch.randn(*sh, device=dev, generator=g, dtype=torch.float32).mul_(0.02).to(dtype)  # noqa: E731
+    A, Dv = s4d_real_A(c["inner"], c["state"], dev), torch.ones(c["inner"], device=dev)
+    layers = []
+    for _ in range(c["layers"]):
+        layers.append((torch.zeros(c["model"], device=dev), MambaLayerWeights(
+            in_proj_weight=r(2 * c["inner"], c["model"]), conv_weight=r(c["inner"], c["width"]).float(),
+            x_proj_weight=r(c["rank"] + 2 * c["state"], c["inner"]), dt_proj_weight=r(c["inner"], c["rank"]),
+            dt_proj_bias=dt_bias_init(c["inner"], g, dev), A=A, D=Dv, out_proj_weight=r(c["model"], c["inner"]))))
+    return r(c["vocab"], c["model"]), layers, torch.zeros(c["model"], device=dev)
+
+
+def _rms_norm(x, weight, eps=1e-6):
+    # modules/rms_norm.py:17-31: computed in float32, scaled by 1 + weight
+    import torch
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * (1.0 + weight)).type_as(x)
+
+
+def _ref_glue_layer(w, hidden, scan):
+    """The reference's Mamba.forward (modules/mamba.py:100-186; no cache, no lengths) in torch
+    ops, with its layout copies, around `scan(u, A, B, C, D, delta, delta_bias) -> out`."""
+    import torch
+    import torch.nn.functional as F
+    Bsz, L, _ = hidden.shape
+    Dm, R, N = w.inner, w.rank, w.state
+    x, gate = torch.chunk(F.linear(hidden, w.in_proj_weight).permute(0, 2, 1).contiguous(), 2, dim=1)
+    gate = gate.permute(0, 2, 1).contiguous()
+    x = F.silu(F.conv1d(x, w.conv_weight.to(x.dtype)[:, None], None, padding=w.conv_weight.shape[1] - 1,
+                        groups=Dm)[..., :L])
+    p = F.linear(x.permute(0, 2, 1).contiguous().view(Bsz * L, Dm), w.x_proj_weight)
+    delta, Bm, Cm = torch.split(p, [R, N, N], dim=-1)
+    delta = (w.dt_proj_weight @ delta.t()).view(Dm, Bsz, L).permute(1, 0, 2).contiguous()
+    Bm = Bm.reshape(Bsz, L, N).permute(0, 2, 1).contiguous()
+    Cm = Cm.reshape(Bsz, L, N).permute(0, 2, 1).contiguous()
+    out = scan(x, w.A, Bm, Cm, w.D, delta, w.dt_proj_bias)
+    out = out.permute(0, 2, 1).contiguous() * F.silu(gate)
+    return F.linear(out, w.out_proj_weight)
+
+
+def run_prefill_lm(dev, dtype, variants, reps=3):
+    """Config 4: prefill forward of the random-init Mamba-2.8B-architecture causal LM
+    (CausalLM.forward, models/causal_lm.py:79-98: embedding, 64 x (RMSNorm, Mamba layer,
+    residual), RMSNorm, tied lm_head) on batch 4 x 2048 token ids (seed 3), timed with CUDA
+    events over `reps` forwards after one warm-up.  `variants` maps a label to
+    layer(weights, normed hidden) -> layer output; returns ms and tokens/s per label."""
+    import torch
+    import torch.nn.functional as F
+    c = CFG4
+    emb, layers, norm_w = _lm_weights(dev, dtype)
+    g = torch.Generator(device=dev).manual_seed(3)
+    ids = torch.randint(0, c["ids"], (c["batch"], c["seqlen"]), device=dev, generator=g)
+    tokens = c["batch"] * c["seqlen"]
+    res = {}
+    with torch.no_grad():
+        for label, layer in variants.items():
+            def fwd():
+                h = F.embedding(ids, emb)
+                for nw, w in layers:
+                    h = h + layer(w, _rms_norm(h, nw))
+                return F.linear(_rms_norm(h, norm_w), emb)
+            try:
+                ms = _time_steps(fwd, 1, reps)
+                res[label] = {"ms_per_forward": ms, "tokens_per_s": tokens / (ms / 1e3)}
+            except Exception as e:  # one variant failing must not hide the others
+                res[label] = {"error": str(e)[:200]}
+            torch.cuda.empty_cache()
+    res["config"] = (f"config 4: Mamba-2.8B-architecture causal LM prefill forward, batch {c['batch']}, seqlen "
+                     f"{c['seqlen']}, {c['layers']} layers, model {c['model']}, vocab {c['vocab']}, "
+                     f"{'bf16' if dtype == torch.bfloat16 else 'fp32'} random-init weights, eval (no dropout)")
+    del emb, layers
+    torch.cuda.empty_cache()
+    return res
+
+
+def _ours_prefill_variants():
+    from ssm_mamba_b200 import SelectiveScanFn
+    from ssm_mamba_b200.layer import mamba_layer_forward
+    return {"ssm_mamba_b200.layer.mamba_layer_forward (no layout copies, fused gate)":
+            lambda w, x: mamba_layer_forward(w, x)[0],
+            "reference module glue + ssm_mamba_b200.SelectiveScanFn (ops swapped only)":
+            lambda w, x: _ref_glue_layer(w, x, lambda *a: SelectiveScanFn.apply(*a)[0])}
+
+
 def _ours_conv_fwd_bwd(x, w, b, dout):
     # the extension's entry points (what causal_conv1d_fn's forward and backward call)
     from ssm_mamba_b200._ext import _C
@@ -516,6 +614,8 @@ def run_ours(args, world, rank, local, pg):
     dev = torch.device("cuda", local)
     if args.decode_only:
         return {"decode": run_decode(args, world, rank, local, pg, measured_peaks()[0])}
+    if args.prefill_only:
+        return {"prefill_lm": {"bf16": run_prefill_lm(dev, torch.bfloat16, _ours_prefill_variants())}}
     B, D, L, N = CFG2["batch"], CFG2["dim"], CFG2["seqlen"], CFG2["dstate"]
     inp = scan_inputs(B, D, L, N, torch.bfloat16, seed=1 + rank, device=dev, with_z=True)
     fwd_bytes, bwd_bytes = scan_bytes(B, D, L, N)
@@ -655,6 +755,11 @@ def run_ours(args, world, rank, local, pg):
     if world == 1 and not args.no_fp32:
         eq = run_equal_precision(dev, _ours_fwd_bwd, _ours_update)
         eq["api"] = "ssm_mamba_b200.SelectiveScanFn / SelectiveUpdateFn (the reference's signatures)"
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        prefill = {"bf16": run_prefill_lm(dev, torch.bfloat16, _ours_prefill_variants())}
+        if not args.no_fp32:
+            prefill["fp32"] = run_prefill_lm(dev, torch.float32, _ours_prefill_variants(), reps=2)
 
     bwd_gbs = bwd_bytes / (bwd_ms / 1e3) / 1e9
     fwd_gbs = fwd_bytes / (fwd_ms / 1e3) / 1e9
@@ -680,6 +785,7 @@ def run_ours(args, world, rank, local, pg):
                          "algorithmic_bytes_per_launch": fwd_bytes},
         "e2e": e2e, "gpu_launches": 3 * args.steps, "clocks": clk, "decode": decode, "long_seq": long_seq,
         "cpu_baseline": cpu, "fp32_equal_precision": eq, "conv1d": conv, "decode_layer": layer,
+        "prefill_lm": prefill,
     }
     return line
 
@@ -809,6 +915,17 @@ def run_reference(args, world, rank, local, pg):
 
             line["ref_decode_layer_b200"] = run_decode_layer(
                 dev, ref_layer_factory, "reference module's step: torch ops + its selective_update kernel, fp32")
+
+            # config 4: the reference module's forward (its layout copies, gate after the scan)
+            # around its selective_scan kernel, float32 (the kernel's only dtype)
+            def ref_scan(u, A, B, C, D, delta, bias):
+                return ref.forward(u, A, B, C, D, delta, bias, None, None, None)[0]
+
+            if not args.no_prefill:
+                line["ref_prefill_lm_b200"] = run_prefill_lm(
+                    dev, torch.float32,
+                    {"reference module glue + its selective_scan kernel": lambda w, x: _ref_glue_layer(w, x, ref_scan)},
+                    reps=2)
             line["ref_cuda_b200"]["what"] = ("reference CUDA kernels (oracle/_ref, built from its sources), "
                                              "float32, no z gate (the reference has none)")
     except Exception as e:  # context only; never fail the reference arm on it
@@ -829,6 +946,8 @@ def main():
     ap.add_argument("--no-long", action="store_true", help="skip the long-sequence (config 5) measurement")
     ap.add_argument("--no-conv", action="store_true", help="skip the conv1d + SiLU measurement")
     ap.add_argument("--no-layer", action="store_true", help="skip the whole-layer decode measurement")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 causal LM prefill measurement")
+    ap.add_argument("--prefill-only", action="store_true", help="profiling aid: only the config-4 prefill")
     ap.add_argument("--no-fp32", action="store_true",
                     help="skip the float32 workloads timed like the reference's kernels")
     ap.add_argument("--decode-only", action="store_true", help="profiling aid: only the decode loop")
