@@ -213,6 +213,61 @@ def cpu_baseline_sample(target_s=10.0, batch=1, dim=96):
             (CFG2["batch"] * CFG2["dim"]) / (batch * dim)}
 
 
+def cpu_decode_sample(target_s=3.0):
+    """Config 3 on the host: the oracle's float build of one decode step (batch 64, d_inner
+    5120, d_state 16, bf16-valued inputs in float32), repeated for about `target_s`."""
+    import numpy as np
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    from ssm_mamba_b200.workloads import decode_inputs
+    Bd, Dd, Nd = CFG3["batch"], CFG3["dim"], CFG3["dstate"]
+    dec = decode_inputs(Bd, Dd, Nd, 4, torch.bfloat16, seed=2, device="cpu")
+    f = lambda t: t.float().numpy()  # noqa: E731
+    st = f(dec.state)
+    reps, t_total = 0, 0.0
+    while t_total < target_s and reps < 200:
+        i = reps % 4
+        t0 = time.perf_counter()
+        _, st = oracle.state_update(st, f(dec.x[i]), f(dec.dt[i]), f(dec.A), f(dec.B[i]), f(dec.C[i]), D=f(dec.D),
+                                    z=f(dec.z[i]), dt_bias=f(dec.dt_bias), dt_softplus=True, dtype=np.float32)
+        t_total += time.perf_counter() - t0
+        reps += 1
+    us = t_total / reps * 1e6
+    return {"us_per_step": us, "tokens_per_s": Bd / (us / 1e6), "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"oracle float32 state update, batch {Bd} x d_inner {Dd} x d_state {Nd}, {reps} steps "
+                      f"in {t_total:.1f} s (includes the oracle's input conversion)"}
+
+
+def cpu_long_seq_sample(target_s=3.0, dim=48, seqlen=8192):
+    """Config 5 on the host, extrapolated: the oracle's float build of fwd+bwd on `dim`
+    channels of a truncated seqlen, scaled linearly to 5120 channels x 131072 tokens."""
+    import numpy as np
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    from ssm_mamba_b200.workloads import scan_inputs
+    N = CFG5["dstate"]
+    inp = scan_inputs(1, dim, seqlen, N, torch.bfloat16, seed=4, device="cpu", with_z=True)
+    f = lambda t: t.float().numpy()  # noqa: E731
+    a = [f(inp.u), f(inp.delta), f(inp.A), f(inp.B), f(inp.C)]
+    kw = dict(D=f(inp.D), z=f(inp.z), delta_bias=f(inp.delta_bias), dtype=np.float32)
+    reps, t_total = 0, 0.0
+    while t_total < target_s and reps < 20:
+        t0 = time.perf_counter()
+        fw = oracle.scan_fwd(*a, **kw)
+        oracle.scan_bwd(*a, f(inp.dout), fwd=fw, **kw)
+        t_total += time.perf_counter() - t0
+        reps += 1
+    scale = (CFG5["dim"] * CFG5["seqlen"]) / (dim * seqlen)
+    s_full = t_total / reps * scale
+    fb, bb = scan_bytes(1, CFG5["dim"], CFG5["seqlen"], N)
+    return {"seconds_per_step_extrapolated": s_full, "tb_s": (fb + bb) / s_full / 1e12,
+            "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"oracle float32 fwd+bwd of 1 x {dim} channels x {seqlen} tokens, {reps} reps in "
+                      f"{t_total:.1f} s, extrapolated linearly (x{scale:.0f}) to 1 x 5120 x 131072: EXTRAPOLATED"}
+
+
 def run_decode(args, world, rank, local, pg, peak):
     """Config 3: 1024 decode steps in one CUDA graph, state rotated over 8 layer buffers
     (168 MB > L2) so every step reads and writes its state in HBM."""
@@ -515,6 +570,13 @@ def _rms_norm(x, weight, eps=1e-6):
     return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * (1.0 + weight)).type_as(x)
 
 
+def _fused_rms_norm(x, weight, eps=1e-6):
+    # the same arithmetic as _rms_norm (float32 normalisation, scaled by 1 + weight, cast
+    # back) through torch's fused rms_norm kernel instead of seven elementwise passes
+    import torch.nn.functional as F
+    return F.rms_norm(x.float(), (x.shape[-1],), weight=1.0 + weight, eps=eps).type_as(x)
+
+
 def _ref_glue_layer(w, hidden, scan):
     """The reference's Mamba.forward (modules/mamba.py:100-186; no cache, no lengths) in torch
     ops, with its layout copies, around `scan(u, A, B, C, D, delta, delta_bias) -> out`."""
@@ -536,36 +598,48 @@ def _ref_glue_layer(w, hidden, scan):
     return F.linear(out, w.out_proj_weight)
 
 
-def run_prefill_lm(dev, dtype, variants, reps=3):
+def run_prefill_lm(dev, dtype, variants, reps=3, pg=None, world=1, rank=0, norm=None):
     """Config 4: prefill forward of the random-init Mamba-2.8B-architecture causal LM
     (CausalLM.forward, models/causal_lm.py:79-98: embedding, 64 x (RMSNorm, Mamba layer,
-    residual), RMSNorm, tied lm_head) on batch 4 x 2048 token ids (seed 3), timed with CUDA
-    events over `reps` forwards after one warm-up.  `variants` maps a label to
-    layer(weights, normed hidden) -> layer output; returns ms and tokens/s per label."""
+    residual), RMSNorm, tied lm_head) on batch 4 x 2048 token ids (seed 3 + rank), timed with
+    CUDA events over `reps` forwards after one warm-up.  Data-parallel over ranks (weak
+    scaling: every rank runs its own batch of 4, no collective); the time is the slowest
+    rank's.  `variants` maps a label to layer(weights, normed hidden) -> layer output;
+    `norm` is the RMSNorm (default: the reference module's torch ops, _rms_norm).  Returns
+    ms and whole-job tokens/s per label."""
     import torch
     import torch.nn.functional as F
     c = CFG4
+    norm = norm or _rms_norm
     emb, layers, norm_w = _lm_weights(dev, dtype)
-    g = torch.Generator(device=dev).manual_seed(3)
+    g = torch.Generator(device=dev).manual_seed(3 + rank)
     ids = torch.randint(0, c["ids"], (c["batch"], c["seqlen"]), device=dev, generator=g)
-    tokens = c["batch"] * c["seqlen"]
+    tokens = c["batch"] * c["seqlen"] * world
     res = {}
     with torch.no_grad():
         for label, layer in variants.items():
             def fwd():
                 h = F.embedding(ids, emb)
                 for nw, w in layers:
-                    h = h + layer(w, _rms_norm(h, nw))
-                return F.linear(_rms_norm(h, norm_w), emb)
+                    h = h + layer(w, norm(h, nw))
+                return F.linear(norm(h, norm_w), emb)
+            err = None
+            barrier(pg)
             try:
                 ms = _time_steps(fwd, 1, reps)
-                res[label] = {"ms_per_forward": ms, "tokens_per_s": tokens / (ms / 1e3)}
             except Exception as e:  # one variant failing must not hide the others
-                res[label] = {"error": str(e)[:200]}
+                ms, err = 1e30, str(e)[:200]
+            ms = max_over_ranks(ms, pg)   # every rank takes this collective, failed or not
+            if err is not None or ms >= 1e29:
+                res[label] = {"error": err or "failed on another rank"}
+            else:
+                res[label] = {"ms_per_forward": ms, "tokens_per_s": tokens / (ms / 1e3)}
             torch.cuda.empty_cache()
-    res["config"] = (f"config 4: Mamba-2.8B-architecture causal LM prefill forward, batch {c['batch']}, seqlen "
-                     f"{c['seqlen']}, {c['layers']} layers, model {c['model']}, vocab {c['vocab']}, "
-                     f"{'bf16' if dtype == torch.bfloat16 else 'fp32'} random-init weights, eval (no dropout)")
+    res["config"] = (f"config 4: Mamba-2.8B-architecture causal LM prefill forward, batch {c['batch']} per GPU x "
+                     f"{world} GPU(s) (data-parallel, no collective), seqlen {c['seqlen']}, {c['layers']} layers, "
+                     f"model {c['model']}, vocab {c['vocab']}, "
+                     f"{'bf16' if dtype == torch.bfloat16 else 'fp32'} random-init weights, eval (no dropout); "
+                     f"RMSNorm: {'torch fused rms_norm' if norm is _fused_rms_norm else 'the module torch ops'}")
     del emb, layers
     torch.cuda.empty_cache()
     return res
@@ -615,7 +689,8 @@ def run_ours(args, world, rank, local, pg):
     if args.decode_only:
         return {"decode": run_decode(args, world, rank, local, pg, measured_peaks()[0])}
     if args.prefill_only:
-        return {"prefill_lm": {"bf16": run_prefill_lm(dev, torch.bfloat16, _ours_prefill_variants())}}
+        v = dict(list(_ours_prefill_variants().items())[:1])     # mamba_layer_forward only
+        return {"prefill_lm": {"bf16": run_prefill_lm(dev, torch.bfloat16, v, norm=_fused_rms_norm)}}
     B, D, L, N = CFG2["batch"], CFG2["dim"], CFG2["seqlen"], CFG2["dstate"]
     inp = scan_inputs(B, D, L, N, torch.bfloat16, seed=1 + rank, device=dev, with_z=True)
     fwd_bytes, bwd_bytes = scan_bytes(B, D, L, N)
@@ -756,10 +831,15 @@ def run_ours(args, world, rank, local, pg):
         eq = run_equal_precision(dev, _ours_fwd_bwd, _ours_update)
         eq["api"] = "ssm_mamba_b200.SelectiveScanFn / SelectiveUpdateFn (the reference's signatures)"
     prefill = None
-    if world == 1 and not args.no_prefill:
-        prefill = {"bf16": run_prefill_lm(dev, torch.bfloat16, _ours_prefill_variants())}
-        if not args.no_fp32:
-            prefill["fp32"] = run_prefill_lm(dev, torch.float32, _ours_prefill_variants(), reps=2)
+    if not args.no_prefill:
+        variants = _ours_prefill_variants()
+        if world > 1:   # data-parallel over ranks: the layer only
+            variants = dict(list(variants.items())[:1])
+        prefill = {"bf16": run_prefill_lm(dev, torch.bfloat16, variants, pg=pg, world=world, rank=rank,
+                                          norm=_fused_rms_norm)}
+        if world == 1 and not args.no_fp32:
+            prefill["fp32"] = run_prefill_lm(dev, torch.float32, _ours_prefill_variants(), reps=2,
+                                             norm=_fused_rms_norm)
 
     bwd_gbs = bwd_bytes / (bwd_ms / 1e3) / 1e9
     fwd_gbs = fwd_bytes / (fwd_ms / 1e3) / 1e9
@@ -832,6 +912,10 @@ def run_reference(args, world, rank, local, pg):
                                    "C restatement of its kernels, float32, OpenMP)"},
         "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    # the other configs' host baselines (the reference has no CPU path; same C restatement)
+    if not args.no_cpu:
+        line["cpu_cfg3_decode"] = cpu_decode_sample()
+        line["cpu_cfg5_long_seq"] = cpu_long_seq_sample()
     # the reference's own CUDA kernels (float32 only) on the GPU, same shapes as the float32
     # set of the other arm, through its pybind functions (what its SelectiveScanFn calls)
     try:
@@ -947,7 +1031,8 @@ def main():
     ap.add_argument("--no-conv", action="store_true", help="skip the conv1d + SiLU measurement")
     ap.add_argument("--no-layer", action="store_true", help="skip the whole-layer decode measurement")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 causal LM prefill measurement")
-    ap.add_argument("--prefill-only", action="store_true", help="profiling aid: only the config-4 prefill")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="profiling aid: only the config-4 prefill through mamba_layer_forward")
     ap.add_argument("--no-fp32", action="store_true",
                     help="skip the float32 workloads timed like the reference's kernels")
     ap.add_argument("--decode-only", action="store_true", help="profiling aid: only the decode loop")

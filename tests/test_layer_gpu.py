@@ -141,3 +141,42 @@ def test_prefill_has_no_layout_copies(cuda):
         torch.cuda.synchronize()
     names = {e.name for e in prof.events()}
     assert not (names & {"aten::copy_", "aten::clone", "aten::contiguous"}), sorted(names)
+
+
+def test_prefill_with_lengths_matches_reference_forward(cuda):
+    """Mamba.forward(hidden, ssm_hiddens, lengths, use_cache=True) (modules/mamba.py:100-186):
+    the conv context gathered at each row's length (:113-133), the scan with `length` and the
+    reference call's default left padding, and the final state -- here the scan half comes
+    from the float64 oracle, the rest from float64 torch ops."""
+    import numpy as np
+    import oracle
+    from ssm_mamba_b200.decode import MambaLayerCache
+    from ssm_mamba_b200.layer import mamba_layer_forward
+    w = _weights(cuda, seed=12)
+    g = torch.Generator(device=cuda).manual_seed(13)
+    Bsz, L = 3, 160
+    hid = torch.randn(Bsz, L, MODEL, device=cuda, generator=g)
+    h0 = torch.randn(Bsz, INNER, STATE, device=cuda, generator=g) * 0.3
+    lengths = torch.tensor([160, 97, 2], device=cuda)
+    cache = MambaLayerCache.zeros(w, Bsz, torch.float32)
+    out, last = mamba_layer_forward(w, hid, h_init=h0, lengths=lengths, cache=cache)
+
+    d = lambda t: None if t is None else t.double()  # noqa: E731
+    xz = F.linear(d(hid), d(w.in_proj_weight)).permute(0, 2, 1)
+    x, gate = xz.chunk(2, dim=1)
+    idx = (lengths - (WIDTH - 1)).unsqueeze(1) + torch.arange(WIDTH - 1, device=cuda).unsqueeze(0)
+    valid = (idx >= 0).unsqueeze(1).expand(-1, INNER, -1)
+    ctx = torch.gather(x, 2, idx.clamp(min=0).unsqueeze(1).expand(-1, INNER, -1)) * valid
+    x = F.silu(F.conv1d(x, d(w.conv_weight)[:, None], d(w.conv_bias), padding=WIDTH - 1, groups=INNER)[..., :L])
+    delta, Bm, Cm = torch.split(F.linear(x.permute(0, 2, 1), d(w.x_proj_weight)), [RANK, STATE, STATE], dim=-1)
+    delta = F.linear(delta, d(w.dt_proj_weight)).permute(0, 2, 1)
+    n = lambda t: t.detach().cpu().numpy()  # noqa: E731
+    r = oracle.scan_fwd(n(x), n(delta), n(d(w.A)), n(Bm.permute(0, 2, 1)), n(Cm.permute(0, 2, 1)), D=n(d(w.D)),
+                        delta_bias=n(d(w.dt_proj_bias)), h_init=n(d(h0)), length=n(lengths),
+                        padding_right=False, delta_softplus=True, dtype=np.float64)
+    y = torch.from_numpy(r["out"]).to(cuda) * F.silu(gate)
+    ref = F.linear(y.permute(0, 2, 1), d(w.out_proj_weight))
+    assert_close(out, ref, 1e-4, 1e-5, "out")
+    assert_close(last, torch.from_numpy(r["h_last"]), 1e-4, 1e-5, "last state")
+    assert_close(cache.ssm_state, torch.from_numpy(r["h_last"]), 1e-4, 1e-5, "cached state")
+    assert_close(cache.conv_state, ctx, 1e-5, 1e-6, "cached conv context")
