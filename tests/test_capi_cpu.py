@@ -73,6 +73,14 @@ def test_validation_errors_without_gpu():
     assert b"state_dim <= 256" in lib.ssm_last_error()
     a.dstate = 0
     assert lib.ssm_scan_fwd(ctypes.byref(a), None) == capi.SSM_ERR_INVALID
+    # empty inputs are refused with a status (the reference fails on them as well: a 0-chunk
+    # h that ops/selective_scan_interface.py:60 indexes, or a launch with an empty grid)
+    for field in ("batch", "dim", "seqlen"):
+        e = capi.ScanFwdArgs()
+        e.batch, e.dim, e.seqlen, e.dstate = 1, 1, 1, 16
+        setattr(e, field, 0)
+        assert lib.ssm_scan_fwd(ctypes.byref(e), None) == capi.SSM_ERR_INVALID
+        assert b"sizes must be positive" in lib.ssm_last_error()
     u = capi.StateUpdateArgs()
     u.batch, u.dim, u.dstate, u.dtype = 1, 1, 16, 7
     assert lib.ssm_state_update(ctypes.byref(u), None) == capi.SSM_ERR_INVALID

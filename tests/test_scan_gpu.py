@@ -194,6 +194,11 @@ def test_errors_raise(cuda):
                           torch.randn(1, 300, 16, device=cuda))
     with pytest.raises(RuntimeError, match="CUDA tensor"):
         selective_scan_fn(u.cpu(), u.cpu(), torch.randn(4, 16), torch.randn(1, 16, 16), torch.randn(1, 16, 16))
+    # empty sequences and batches are refused (the reference fails on them too)
+    e = torch.randn(1, 4, 0, device=cuda)
+    with pytest.raises(RuntimeError, match="positive"):
+        selective_scan_fn(e, e, torch.randn(4, 16, device=cuda), torch.randn(1, 16, 0, device=cuda),
+                          torch.randn(1, 16, 0, device=cuda))
 
 
 def test_large_config2_shape_properties(cuda):
