@@ -17,6 +17,18 @@
 #include "../../include/ssm_b200.h"
 #include "params.h"
 #include "scan_layout.h"
+#include <nvtx3/nvToolsExt.h>
+
+namespace {
+// NVTX range around each entry point (named after it), for nsys / ncu timelines; a no-op
+// unless a tool is attached
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
+}  // namespace
 
 namespace ssm {
 cudaError_t launch_scan_fwd(const FwdParams& p, int is_bf16, int lpc, int spt, const CUtensorMap* maps,
@@ -349,9 +361,13 @@ static int fwd_impl(const ssm_scan_fwd_args* a, const float* restart, void* stre
     return SSM_OK;
 }
 
-int ssm_scan_fwd(const ssm_scan_fwd_args* a, void* stream) { return fwd_impl(a, nullptr, stream); }
+int ssm_scan_fwd(const ssm_scan_fwd_args* a, void* stream) {
+    NvtxRange r_("ssm_scan_fwd");
+    return fwd_impl(a, nullptr, stream);
+}
 
 int ssm_scan_ckpt_from_reference(const ssm_scan_fwd_args* a, const float* ref_ckpt, void* stream) {
+    NvtxRange r_("ssm_scan_ckpt_from_reference");
     if (!ref_ckpt) return fail(SSM_ERR_INVALID, "ssm_scan_ckpt_from_reference: ref_ckpt is NULL");
     return fwd_impl(a, ref_ckpt, stream);
 }
@@ -536,6 +552,7 @@ void set_last_error(const char* msg) { g_err = msg; }
 extern "C" {
 
 int ssm_scan_bwd(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, void* stream) {
+    NvtxRange r_("ssm_scan_bwd");
     if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: args is NULL");
     DevInfo* di = nullptr;
     int rc = device_info(&di);
@@ -544,6 +561,7 @@ int ssm_scan_bwd(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, v
 }
 
 int ssm_state_update(const ssm_state_update_args* a, void* stream_) {
+    NvtxRange r_("ssm_state_update");
     if (!a) return fail(SSM_ERR_INVALID, "ssm_state_update: args is NULL");
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     if (a->batch < 1 || a->dim < 1 || a->dstate < 1)
@@ -666,6 +684,7 @@ static int chunk_impl(const char* name, int reverse, int64_t batch, int64_t dim,
 }
 
 int ssm_scan_chunk_state_fwd(const ssm_scan_fwd_args* a, float* h_end, float* delta_sum, void* stream) {
+    NvtxRange r_("ssm_scan_chunk_state_fwd");
     if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_chunk_state_fwd: args is NULL");
     if (a->out || a->y || a->ckpt || a->h_init || a->h_last || a->length)
         return fail(SSM_ERR_INVALID, "ssm_scan_chunk_state_fwd: out, y, ckpt, h_init, h_last and length must be NULL");
@@ -678,6 +697,7 @@ int ssm_scan_chunk_state_fwd(const ssm_scan_fwd_args* a, float* h_end, float* de
 }
 
 int ssm_scan_chunk_state_bwd(const ssm_scan_bwd_args* a, float* g_start, void* stream) {
+    NvtxRange r_("ssm_scan_chunk_state_bwd");
     if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_chunk_state_bwd: args is NULL");
     if (a->length) return fail(SSM_ERR_INVALID, "ssm_scan_chunk_state_bwd: length must be NULL");
     if (!g_start) return fail(SSM_ERR_INVALID, "ssm_scan_chunk_state_bwd: g_start is required");
@@ -689,6 +709,7 @@ int ssm_scan_chunk_state_bwd(const ssm_scan_bwd_args* a, float* g_start, void* s
 }
 
 int ssm_scan_carry_compose(const ssm_carry_args* a, void* stream) {
+    NvtxRange r_("ssm_scan_carry_compose");
     if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_carry_compose: args is NULL");
     if (a->batch < 1 || a->dim < 1 || a->dstate < 1 || a->nslices < 1 || a->nslices > (1 << 20))
         return fail(SSM_ERR_INVALID, "ssm_scan_carry_compose: sizes must be positive");
@@ -764,6 +785,7 @@ static int conv_nchunk(const ssm_conv1d_args* a, bool vec) {
 }
 
 int ssm_conv1d_fwd(const ssm_conv1d_args* a, void* stream) {
+    NvtxRange r_("ssm_conv1d_fwd");
     int rc = conv_common("ssm_conv1d_fwd", a, true);
     if (rc) return rc;
     DevInfo* di = nullptr;
@@ -785,6 +807,7 @@ size_t ssm_conv1d_bwd_workspace_size(const ssm_conv1d_args* a) {
 }
 
 int ssm_conv1d_bwd(const ssm_conv1d_args* a, void* workspace, size_t ws_bytes, void* stream) {
+    NvtxRange r_("ssm_conv1d_bwd");
     int rc = conv_common("ssm_conv1d_bwd", a, true, false);
     if (rc) return rc;
     if (!a->dout || !a->dx || !a->dweight)
@@ -809,6 +832,7 @@ int ssm_conv1d_bwd(const ssm_conv1d_args* a, void* workspace, size_t ws_bytes, v
 }
 
 int ssm_conv1d_update(const ssm_conv1d_args* a, void* stream) {
+    NvtxRange r_("ssm_conv1d_update");
     int rc = conv_common("ssm_conv1d_update", a, false);
     if (rc) return rc;
     if (!a->state) return fail(SSM_ERR_INVALID, "ssm_conv1d_update: state is required");

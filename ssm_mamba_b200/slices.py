@@ -100,6 +100,16 @@ class SliceGroup:
             dist.all_gather(list(out.unbind(0)), t, group=self.group)
         return out
 
+    def check_agreement(self, what: str, values, device) -> None:
+        """Every rank must pass the same `values` (a fixed-length list of ints).  One small
+        all_gather; when the ranks disagree, every rank raises the same RuntimeError instead
+        of exchanging carries of mismatched shapes."""
+        if self.world == 1:
+            return
+        rows = self.all_gather(torch.tensor(list(values), dtype=torch.int64, device=device)).cpu()
+        if not bool((rows == rows[0]).all()):
+            raise RuntimeError(f"sliced scan: ranks disagree on {what}: {rows.tolist()}")
+
     def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
             import torch.distributed as dist
@@ -141,6 +151,10 @@ class SlicedScanFn(torch.autograd.Function):
         N = A.shape[1]
         if S > 1 and (Bt != 1 or L % S != 0):
             raise ValueError("segmented scan needs batch 1 and seqlen divisible by the segment count")
+        # a peer with other shapes or options would exchange carries of another size: refuse
+        group.check_agreement("batch, dim, dstate, segments, z, D, delta_bias, h_init, softplus, dtype",
+                              [Bt, Dm, N, S, z is not None, D is not None, delta_bias is not None,
+                               h_init is not None, bool(delta_softplus), u.element_size()], u.device)
         Bc = Bt if S == 1 else 1            # batch of one slice
         rows = Bt if S == 1 else S          # rows of the segmented views
         sv = lambda t: segment_view(t, S)  # noqa: E731

@@ -144,3 +144,32 @@ def test_oracle_state_update_matches_one_scan_step():
                          bias, state)
     np.testing.assert_allclose(out, fw["out"][..., 0], rtol=1e-12, atol=1e-12)
     np.testing.assert_allclose(new, fw["h_last"], rtol=1e-12, atol=1e-12)
+
+
+class _OracleScan(torch.autograd.Function):
+    """The oracle's forward and analytic backward as one autograd function (float64)."""
+
+    @staticmethod
+    def forward(ctx, u, delta, A, B, C, D, z, bias, h0):
+        f = lambda t: t.detach().numpy()  # noqa: E731
+        fw = oracle.scan_fwd(f(u), f(delta), f(A), f(B), f(C), f(D), f(z), f(bias), f(h0))
+        ctx.save_for_backward(u, delta, A, B, C, D, z, bias, h0)
+        ctx.fw = fw
+        return torch.from_numpy(fw["out"]), torch.from_numpy(fw["h_last"])
+
+    @staticmethod
+    def backward(ctx, dout, dh):
+        u, delta, A, B, C, D, z, bias, h0 = ctx.saved_tensors
+        f = lambda t: t.detach().numpy()  # noqa: E731
+        g = oracle.scan_bwd(f(u), f(delta), f(A), f(B), f(C), f(dout.contiguous()), f(D), f(z), f(bias), f(h0),
+                            dh_last=f(dh.contiguous()), fwd=ctx.fw)
+        t = lambda k: torch.from_numpy(np.ascontiguousarray(g[k]))  # noqa: E731
+        return t("du"), t("ddelta"), t("dA"), t("dB"), t("dC"), t("dD"), t("dz"), t("ddelta_bias"), t("dh_init")
+
+
+def test_oracle_backward_passes_gradcheck():
+    """torch.autograd.gradcheck (central finite differences in float64) on the oracle's
+    analytic backward, every input at once, including the final-state output."""
+    u, delta, A, B, C, D, z, bias, h0 = _rand(1, 2, 40, 3, True, True, seed=11)
+    assert torch.autograd.gradcheck(_OracleScan.apply, (u, delta, A, B, C, D, z, bias, h0), eps=1e-6,
+                                    atol=1e-7, rtol=1e-5)

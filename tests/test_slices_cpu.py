@@ -147,3 +147,53 @@ def test_ranks_over_gloo_match_the_whole_sequence(world, segments):
             if p.is_alive():
                 p.kill()
     assert res == {r: "ok" for r in range(world)}, res
+
+
+# ---- failures of a peer rank (host-side; no GPU involved) ---------------------------------
+def _faulty_rank_main(rank, world, port, mode, q):
+    import datetime
+    import torch.distributed as dist
+    try:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=20))
+        if mode == "dies" and rank == 1:
+            os._exit(3)                      # a rank that is gone before the exchange
+        x = _inputs()
+        L = x["u"].shape[-1]
+        lo, hi = rank * L // world, (rank + 1) * L // world
+        segments = 2 if (mode == "shape" and rank == 1) else 1
+        _run_slice(x, lo, hi, segments, SliceGroup(dist.group.WORLD), last=rank == world - 1)
+        q.put((rank, "ok"))
+    except Exception as e:  # the clean error this test expects
+        q.put((rank, f"{type(e).__name__}: {e}"))
+
+
+@pytest.mark.parametrize("mode", ["shape", "dies"])
+def test_peer_failure_gives_a_clean_error(mode):
+    """A rank that passes other shapes makes every rank raise the agreement error; a rank
+    that dies before the exchange makes the survivor's collective raise (connection lost or
+    the process group's timeout) instead of hanging."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = 2
+    procs = [ctx.Process(target=_faulty_rank_main, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(world if mode == "shape" else 1):
+            r, msg = q.get(timeout=120)
+            res[r] = msg
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    if mode == "shape":
+        assert set(res) == {0, 1}
+        for r in (0, 1):
+            assert "ranks disagree" in res[r], res
+    else:
+        assert procs[1].exitcode == 3
+        assert 0 in res and res[0] != "ok", res
