@@ -426,6 +426,39 @@ def run_equal_precision(dev, forward_backward, update_apply):
     return res
 
 
+def run_varlen(dev, forward_backward, dtypes=("fp32",)):
+    """Variable-length rows (`length`, the reference API's padding sides): config-2 shape
+    with per-row lengths drawn in [L/2, L] (seed 5), forward + backward through a
+    reference-shaped call `forward_backward(inputs, length, padding)`; float32 (the
+    reference kernels' only dtype) and, where given, bf16."""
+    import torch
+    from ssm_mamba_b200.workloads import scan_inputs
+    Bs, Dm, L, N = CFG2["batch"], CFG2["dim"], CFG2["seqlen"], CFG2["dstate"]
+    g = torch.Generator().manual_seed(5)
+    length = torch.randint(L // 2, L + 1, (Bs,), generator=g).to(dev)
+    res = {"lengths": length.tolist()}
+    for dn in dtypes:
+        dt = torch.float32 if dn == "fp32" else torch.bfloat16
+        inp = scan_inputs(Bs, Dm, L, N, dt, seed=1, device=dev, with_z=False)
+        for pad in ("right", "left"):
+            ms = _time_steps(lambda: forward_backward(inp, length, pad), 2, 10)
+            res[f"{dn}_{pad}"] = {"ms_per_fwd_bwd": ms}
+        del inp
+        torch.cuda.empty_cache()
+    res["config"] = (f"config-2 shape ({Bs}, {Dm}, {L}, d_state {N}), no z, softplus, per-row lengths, "
+                     "padding right and left (the reference API's default)")
+    return res
+
+
+def _ours_varlen_fwd_bwd(inp, length, pad):
+    from ssm_mamba_b200 import SelectiveScanFn
+    leaves = [t.requires_grad_() for t in (inp.u, inp.A, inp.B, inp.C, inp.D, inp.delta, inp.delta_bias)]
+    out, _ = SelectiveScanFn.apply(*leaves, None, length, pad)
+    out.backward(inp.dout)
+    for t in leaves:
+        t.grad = None
+
+
 CONV = dict(batch=8, dim=1536, seqlen=2048, width=4)
 
 
@@ -830,6 +863,10 @@ def run_ours(args, world, rank, local, pg):
     if world == 1 and not args.no_fp32:
         eq = run_equal_precision(dev, _ours_fwd_bwd, _ours_update)
         eq["api"] = "ssm_mamba_b200.SelectiveScanFn / SelectiveUpdateFn (the reference's signatures)"
+    varlen = None
+    if world == 1 and not args.no_fp32:
+        varlen = run_varlen(dev, _ours_varlen_fwd_bwd, ("fp32", "bf16"))
+        varlen["api"] = "ssm_mamba_b200.SelectiveScanFn with length and padding_size"
     prefill = None
     if not args.no_prefill:
         variants = _ours_prefill_variants()
@@ -865,7 +902,7 @@ def run_ours(args, world, rank, local, pg):
                          "algorithmic_bytes_per_launch": fwd_bytes},
         "e2e": e2e, "gpu_launches": 3 * args.steps, "clocks": clk, "decode": decode, "long_seq": long_seq,
         "cpu_baseline": cpu, "fp32_equal_precision": eq, "conv1d": conv, "decode_layer": layer,
-        "prefill_lm": prefill,
+        "prefill_lm": prefill, "varlen": varlen,
     }
     return line
 
@@ -954,6 +991,34 @@ def run_reference(args, world, rank, local, pg):
                     t.grad = None
 
             line["ref_cuda_b200"] = run_equal_precision(dev, fwd_bwd, lambda *a: ref_up.apply(*a))
+
+            class RefScanLenFn(torch.autograd.Function):
+                """RefScanFn with `length` and the padding side passed to the pybind functions."""
+
+                @staticmethod
+                def forward(ctx, u, A, B, C, D, delta, bias, length, pad):
+                    out, h = ref.forward(u, A, B, C, D, delta, bias, None, length, pad)
+                    ctx.save_for_backward(u, A, B, C, D, delta, bias, h, length)
+                    ctx.pad = pad
+                    return out, h[..., -1, 1::2]
+
+                @staticmethod
+                def backward(ctx, dout, dh):
+                    u, A, B, C, D, delta, bias, h, length = ctx.saved_tensors
+                    g = ref.backward(u, A, B, C, D, delta, bias, h, None, dout.contiguous(), dh.contiguous(),
+                                     length, ctx.pad)
+                    return g[0], g[1], g[2], g[3], g[4], g[5], g[6], None, None
+
+            def ref_varlen(inp, length, pad):
+                leaves = [t.requires_grad_() for t in (inp.u, inp.A, inp.B, inp.C, inp.D, inp.delta,
+                                                       inp.delta_bias)]
+                out, _ = RefScanLenFn.apply(*leaves, length, pad)
+                out.backward(inp.dout)
+                for t in leaves:
+                    t.grad = None
+
+            line["ref_varlen_b200"] = run_varlen(dev, ref_varlen)
+            line["ref_varlen_b200"]["api"] = "reference CUDA kernels with length and padding_side, float32"
 
             # the reference module's conv1d + SiLU (modules/mamba.py:137-139, 203-213): torch ops
             import torch.nn.functional as F

@@ -110,13 +110,18 @@ class _SelectiveScanRefFn(torch.autograd.Function):
             ensure_contiguous, (u, A, B, C, D, delta, delta_bias, h_init, length))
         pr = _padding_right(padding_size)
         need_grad = any(ctx.needs_input_grad)
-        if length is not None:
+        if length is not None and not pr:
+            # left padding: the reference backward recomputes as if the rows were right padded
+            # (backward_kernel.cu:225-246, 374), so its states differ from the forward's; keep
+            # the reference's chunk carries and rebuild the checkpoints under its rules later
             out, _, h, _ = _C.scan_fwd(u, delta, A, B, C, D, None, delta_bias, h_init, length, pr,
                                        True, False, 2, False)
             h_last = h[..., -1, 1::2]
             ckpt_kind = 2
         else:
-            out, _, h, h_last = _C.scan_fwd(u, delta, A, B, C, D, None, delta_bias, h_init, None, pr,
+            # no length, or right padding: the backward's recompute of every token it uses
+            # (t < len) equals the forward's states, so the forward's own checkpoints serve
+            out, _, h, h_last = _C.scan_fwd(u, delta, A, B, C, D, None, delta_bias, h_init, length, pr,
                                             True, False, 1 if need_grad else 0, True)
             ckpt_kind = 1
         if need_grad:

@@ -161,6 +161,24 @@ def test_reference_api_with_length_matches_oracle(cuda, L, lengths, pr):
         assert_grad_close(t.grad, g[name], name)
 
 
+@pytest.mark.parametrize("L,lengths", [(256, [256, 199, 100]), (300, [300, 211, 57]), (384, [0, 128, 383])])
+@pytest.mark.parametrize("dtype", [F32, BF16])
+def test_right_padding_forward_checkpoints_equal_the_rebuilt_ones(cuda, L, lengths, dtype):
+    """With right padding, SelectiveScanFn's backward uses the forward's own checkpoints:
+    they equal, bit for bit, the checkpoints rebuilt from the reference-format chunk carries
+    under the reference backward's load rules (the path left padding needs)."""
+    from ssm_mamba_b200._ext import _C
+    inp = scan_inputs(len(lengths), 24, L, 16, dtype, seed=L, device=cuda, with_z=False, with_h_init=True)
+    length = torch.tensor(lengths, dtype=torch.int64, device=cuda)
+    a = (inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, None, inp.delta_bias, inp.h_init, length, True, True, False)
+    _, _, direct, _ = _C.scan_fwd(*a, 1, False)
+    _, _, ref_h, _ = _C.scan_fwd(*a, 2, False)
+    rebuilt = _C.ckpt_from_reference(inp.u, inp.delta, inp.A, inp.B, inp.C, inp.delta_bias, inp.h_init, length,
+                                     True, True, ref_h)
+    assert direct.shape == rebuilt.shape
+    assert torch.equal(direct, rebuilt)
+
+
 def test_reference_api_without_length(cuda):
     from ssm_mamba_b200 import SelectiveScanFn
     inp = scan_inputs(2, 48, 640, 16, F32, seed=9, device=cuda, with_z=False, with_h_init=True)
