@@ -83,10 +83,13 @@ def test_streamed_and_per_cta_decode_kernels_agree(cuda, monkeypatch, B, D, N, d
         outs = []
         for s in range(4):
             out = torch.empty(B, D, dtype=dtype, device=cuda)
-            a = capi.fill_update(state, state, dec.x[s], dec.dt[s], dec.A, dec.B[s], dec.C[s], out, D=dec.D,
+            # even steps in place, odd steps into a fresh state buffer
+            nxt = state if s % 2 == 0 else torch.empty_like(state)
+            a = capi.fill_update(state, nxt, dec.x[s], dec.dt[s], dec.A, dec.B[s], dec.C[s], out, D=dec.D,
                                  z=dec.z[s] if gate else None, dt_bias=dec.dt_bias, dt_softplus=True)
             capi.call_update(a)
             outs.append(out)
+            state = nxt
         torch.cuda.synchronize()
         results[mode] = (torch.stack(outs), state)
     ref_state = np64(dec.state)
