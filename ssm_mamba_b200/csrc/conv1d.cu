@@ -145,11 +145,141 @@ __global__ void __launch_bounds__(256) conv1d_fwd_kernel(const __grid_constant__
     }
 }
 
+// g[i] = dout[t0 + i] * act'(pre[t0 + i]) for the N tokens from t0, all inside the row,
+// with xw = x[t0 - (K-1) .. t0 + N - 1] and dw = dout[t0 .. t0 + N - 1].
+template <typename IT, int K, int N>
+__device__ __forceinline__ void conv_grad_tokens(const float (&w)[K], float bias, bool silu, const float* xw,
+                                                 const float* dw, float (&g)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+        float pre = bias;
+#pragma unroll
+        for (int k = 0; k < K; k++) pre = fmaf(w[k], xw[i + k], pre);
+        float gi = dw[i];
+        if (silu) {
+            const float s = sigmoid_io<IT>(pre);
+            gi *= s * (1.f + pre * (1.f - s));
+        }
+        g[i] = gi;
+    }
+}
+
 // Backward.  g[t] = dout[t] * act'(pre[t]); dx[t] = sum_k w[k] g[t + (K-1) - k];
 // dw[k] = sum g[t] x[t - (K-1) + k]; dbias = sum g[t].  The warp's partials of dw, dbias go
 // to ws[(chunk * batch + b), d, :].
+//
+// With 16-byte vectors a lane computes g only for its own VT tokens; the K-1 tokens of g
+// after them (the halo dx needs) are the first tokens of the next vector, which the next
+// lane owns in the same round -- or, for lane 31, lane 0 in the next round.  So every round
+// finishes the dx of the PREVIOUS round's vector, taking its halo by shuffles, and after the
+// last round lane 31 computes the halo of the vector after the chunk itself.
 template <typename IT, int VT, int K>
 __global__ void __launch_bounds__(256) conv1d_bwd_kernel(const __grid_constant__ ConvParams p) {
+    if constexpr (VT > 1) {
+        const int lane = threadIdx.x & 31;
+        const int nvec = p.seqlen / VT;
+        const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+        if (row >= p.batch * p.dim) return;   // whole warps: the shuffles below see full warps
+        const int b = row / p.dim, d = row - b * p.dim;
+        const IT* xr = static_cast<const IT*>(p.x) + b * p.x_sb + d * p.x_sd;
+        const IT* gr = static_cast<const IT*>(p.dout) + b * p.dout_sb + d * p.dout_sd;
+        IT* dxr = static_cast<IT*>(p.dx) + b * p.dx_sb + d * p.dx_sd;
+        float w[K];
+#pragma unroll
+        for (int k = 0; k < K; k++) w[k] = __ldg(p.w + d * p.w_sd + k);
+        const float bias = p.bias ? __ldg(p.bias + d) : 0.f;
+        float part[K + 1];
+#pragma unroll
+        for (int k = 0; k <= K; k++) part[k] = 0.f;
+        const int vbase = blockIdx.y * 32 * kConvRows + lane;
+        float gp[VT];                        // g of this lane's vector of the previous round
+        // dx of the vector v from its g and the K-1 following values of g
+        auto finish = [&](int v, const float (&gv)[VT], const float (&halo)[K - 1]) {
+            if (v >= nvec) return;
+            float dxv[VT];
+#pragma unroll
+            for (int i = 0; i < VT; i++) {
+                float acc = 0.f;
+#pragma unroll
+                for (int k = 0; k < K; k++) {
+                    const int j = i + (K - 1) - k;
+                    acc = fmaf(w[k], j < VT ? gv[j] : halo[j - VT], acc);
+                }
+                dxv[i] = acc;
+            }
+            store_vec<IT, VT>(dxr + v * VT, dxv);
+        };
+#pragma unroll
+        for (int r = 0; r < kConvRows; r++) {
+            const int v = vbase + 32 * r;
+            float g[VT];
+            if (v < nvec) {
+                const int t0 = v * VT;
+                float xw[VT + K - 1];        // x[t0 - (K-1) .. t0 + VT - 1]
+                float dv[VT];
+                load_window<IT, VT, VT + K - 1>(xr, t0, -(K - 1), p.seqlen, xw);
+                load_vec<IT, VT>(gr + t0, dv);
+                conv_grad_tokens<IT, K, VT>(w, bias, p.silu, xw, dv, g);
+#pragma unroll
+                for (int i = 0; i < VT; i++) {
+#pragma unroll
+                    for (int k = 0; k < K; k++) part[k] = fmaf(g[i], xw[i + k], part[k]);
+                    part[K] += g[i];
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < VT; i++) g[i] = 0.f;
+            }
+            if (r > 0) {
+                // halo of the previous round's vector: the next lane's previous g, or for
+                // lane 31 lane 0's current g
+                float halo[K - 1];
+#pragma unroll
+                for (int i = 0; i < K - 1; i++) {
+                    const float nb = __shfl_down_sync(0xffffffffu, gp[i], 1);
+                    const float l0 = __shfl_sync(0xffffffffu, g[i], 0);
+                    halo[i] = lane == 31 ? l0 : nb;
+                }
+                finish(v - 32, gp, halo);
+            }
+#pragma unroll
+            for (int i = 0; i < VT; i++) gp[i] = g[i];
+        }
+        {
+            // the last round: lanes 0..30 take the next lane's g; lane 31 needs the first K-1
+            // tokens after this chunk, computed here
+            float halo[K - 1];
+#pragma unroll
+            for (int i = 0; i < K - 1; i++) halo[i] = __shfl_down_sync(0xffffffffu, gp[i], 1);
+            const int vl = vbase + 32 * (kConvRows - 1);
+            if (lane == 31 && vl + 1 < nvec) {
+                const int t1 = (vl + 1) * VT;
+                float xh[2 * K - 2];         // x[t1 - (K-1) .. t1 + K - 2]
+                float dh[K - 1];
+#pragma unroll
+                for (int j = 0; j < 2 * K - 2; j++) xh[j] = to_f(xr[t1 - (K - 1) + j]);
+#pragma unroll
+                for (int j = 0; j < K - 1; j++) dh[j] = to_f(gr[t1 + j]);
+                conv_grad_tokens<IT, K, K - 1>(w, bias, p.silu, xh, dh, halo);
+            } else if (lane == 31) {
+#pragma unroll
+                for (int i = 0; i < K - 1; i++) halo[i] = 0.f;
+            }
+            finish(vl, gp, halo);
+        }
+#pragma unroll
+        for (int k = 0; k <= K; k++) {
+#pragma unroll
+            for (int m = 16; m >= 1; m >>= 1) part[k] += __shfl_xor_sync(0xffffffffu, part[k], m);
+        }
+        if (lane == 0) {
+            float* dst = p.ws + (((int64_t)blockIdx.y * p.batch + b) * p.dim + d) * (K + 1);
+#pragma unroll
+            for (int k = 0; k <= K; k++) dst[k] = part[k];
+        }
+        return;
+    }
+    // one token per lane (rows that are not 16-byte aligned): recompute the halo of g
     const int lane = threadIdx.x & 31;
     const int nvec = (p.seqlen + VT - 1) / VT;
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);

@@ -12,7 +12,8 @@ import oracle
 pytestmark = pytest.mark.gpu
 
 # (batch, dim, seqlen, width): vector path (seqlen a multiple of 8) and element path
-SHAPES = [(2, 64, 256, 4), (3, 40, 1000, 4), (2, 33, 77, 3), (1, 16, 5, 2), (4, 128, 2048, 4)]
+SHAPES = [(2, 64, 256, 4), (3, 40, 1000, 4), (2, 33, 77, 3), (1, 16, 5, 2), (4, 128, 2048, 4),
+          (2, 24, 4096, 4), (2, 16, 1032, 3), (1, 8, 2056, 2)]   # several chunks per row, widths 3, 2
 
 
 @pytest.mark.parametrize("shape", SHAPES)
