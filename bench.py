@@ -678,6 +678,50 @@ def run_prefill_lm(dev, dtype, variants, reps=3, pg=None, world=1, rank=0, norm=
     return res
 
 
+TRAIN = dict(batch=8, seqlen=2048, model=768, inner=1536, state=16, rank=48, width=4)
+
+
+def run_train_layer(dev, dtype, variants, reps=10):
+    """One Mamba-130M-shape layer (the config-2 scan inside it: batch 8, seqlen 2048, model
+    768, d_inner 1536, d_state 16, dt_rank 48, conv width 4) trained for one step: the
+    layer's forward and backward with every weight a leaf (modules/mamba.py:100-186 and its
+    autograd), random weights ~ N(0, 0.02) (seed 13).  `variants` maps a label to
+    layer(weights, hidden) -> output."""
+    import torch
+    from ssm_mamba_b200.decode import MambaLayerWeights
+    from ssm_mamba_b200.workloads import dt_bias_init, s4d_real_A
+    c = TRAIN
+    g = torch.Generator(device=dev).manual_seed(13)
+    r = lambda *sh: torch.randn(*sh, device=dev, generator=g, dtype=torch.float32).mul_(0.02).to(dtype)  # noqa: E731
+    w = MambaLayerWeights(
+        in_proj_weight=r(2 * c["inner"], c["model"]), conv_weight=r(c["inner"], c["width"]).float() * 10,
+        x_proj_weight=r(c["rank"] + 2 * c["state"], c["inner"]), dt_proj_weight=r(c["inner"], c["rank"]) * 5,
+        dt_proj_bias=dt_bias_init(c["inner"], g, dev), A=s4d_real_A(c["inner"], c["state"], dev),
+        D=torch.ones(c["inner"], device=dev), out_proj_weight=r(c["model"], c["inner"]))
+    leaves = [w.in_proj_weight, w.conv_weight, w.x_proj_weight, w.dt_proj_weight, w.dt_proj_bias, w.D,
+              w.out_proj_weight]
+    for t in leaves:
+        t.requires_grad_()
+    hid = torch.randn(c["batch"], c["seqlen"], c["model"], device=dev, generator=g).to(dtype).requires_grad_()
+    dout = torch.randn(c["batch"], c["seqlen"], c["model"], device=dev, generator=g).to(dtype)
+    res = {}
+    for label, layer in variants.items():
+        def step():
+            layer(w, hid).backward(dout)
+            for t in leaves + [hid]:
+                t.grad = None
+        try:
+            ms = _time_steps(step, 2, reps)
+            res[label] = {"ms_per_step": ms, "tokens_per_s": c["batch"] * c["seqlen"] / (ms / 1e3)}
+        except Exception as e:  # one variant failing must not hide the others
+            res[label] = {"error": str(e)[:200]}
+        torch.cuda.empty_cache()
+    res["config"] = (f"one Mamba-130M-shape layer, forward + backward, batch {c['batch']}, seqlen {c['seqlen']}, "
+                     f"model {c['model']}, d_inner {c['inner']}, d_state {c['state']}, dt_rank {c['rank']}, "
+                     f"{'bf16' if dtype == torch.bfloat16 else 'fp32'} weights and activations")
+    return res
+
+
 def _ours_prefill_variants():
     from ssm_mamba_b200 import SelectiveScanFn
     from ssm_mamba_b200.layer import mamba_layer_forward
@@ -863,6 +907,12 @@ def run_ours(args, world, rank, local, pg):
     if world == 1 and not args.no_fp32:
         eq = run_equal_precision(dev, _ours_fwd_bwd, _ours_update)
         eq["api"] = "ssm_mamba_b200.SelectiveScanFn / SelectiveUpdateFn (the reference's signatures)"
+    train = None
+    if world == 1 and not args.no_layer:
+        v = _ours_prefill_variants()
+        train = {"bf16": run_train_layer(dev, torch.bfloat16, v)}
+        if not args.no_fp32:
+            train["fp32"] = run_train_layer(dev, torch.float32, v, reps=5)
     varlen = None
     if world == 1 and not args.no_fp32:
         varlen = run_varlen(dev, _ours_varlen_fwd_bwd, ("fp32", "bf16"))
@@ -902,7 +952,7 @@ def run_ours(args, world, rank, local, pg):
                          "algorithmic_bytes_per_launch": fwd_bytes},
         "e2e": e2e, "gpu_launches": 3 * args.steps, "clocks": clk, "decode": decode, "long_seq": long_seq,
         "cpu_baseline": cpu, "fp32_equal_precision": eq, "conv1d": conv, "decode_layer": layer,
-        "prefill_lm": prefill, "varlen": varlen,
+        "prefill_lm": prefill, "varlen": varlen, "train_layer": train,
     }
     return line
 
@@ -1070,6 +1120,14 @@ def run_reference(args, world, rank, local, pg):
             def ref_scan(u, A, B, C, D, delta, bias):
                 return ref.forward(u, A, B, C, D, delta, bias, None, None, None)[0]
 
+            if not args.no_layer:
+                def ref_scan_ag(u, A, B, C, D, delta, bias):
+                    return RefScanFn.apply(u, A, B, C, D, delta, bias)[0]
+
+                line["ref_train_layer_b200"] = run_train_layer(
+                    dev, torch.float32,
+                    {"reference module glue + its selective_scan kernels": lambda w, x: _ref_glue_layer(w, x, ref_scan_ag)},
+                    reps=5)
             if not args.no_prefill:
                 line["ref_prefill_lm_b200"] = run_prefill_lm(
                     dev, torch.float32,
