@@ -588,25 +588,25 @@ int ssm_state_update(const ssm_state_update_args* a, void* stream_) {
     p.dt_bias = a->dt_bias;
     p.out = a->out; p.out_sb = a->out_batch_stride;
     p.pdl = (a->launch_flags & SSM_LAUNCH_PDL) != 0;
-    // Streamed kernel (bulk-copy pipeline over persistent CTAs) for bf16 streams in
-    // contiguous, 16-byte aligned layouts with dstate 8, 16 or 32 and dim a multiple of its
-    // channel tile.  Measured on B200 at batch 64 x 5120 x 16 (CUDA graph, 8 rotating
-    // states): bf16 10.5 us/step streamed vs 11.8-12.0 per-CTA; float32 streams 11.0-11.4
-    // streamed vs 10.5-10.7 per-CTA, so float32 keeps the per-CTA kernel.
-    // SSM_DEC_STREAM=0 turns the streamed kernel off, =1 forces it for float32 too.
+    // Streamed kernel (bulk-copy pipeline over persistent CTAs) for contiguous, 16-byte
+    // aligned layouts with dstate 8, 16 or 32 and dim a multiple of its channel tile.
+    // Measured on B200 at batch 64 x 5120 x 16 (CUDA graph, 8 rotating states): bf16
+    // 9.4-9.5 us/step streamed vs 11.8-12.0 per-CTA; float32 10.2-10.3 vs 10.5-10.7.
+    // SSM_DEC_STREAM=0 turns it off.
     {
         const int64_t N = a->dstate, es = a->dtype == SSM_BF16 ? 2 : 4;
         const int lpc = (int)(N / 8), rpb = lpc > 0 ? 256 / lpc : 0;
         auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
         const char* env = getenv("SSM_DEC_STREAM");
-        const bool want = env ? env[0] != '0' : a->dtype == SSM_BF16;
+        const bool want = !(env && env[0] == '0');
         const bool ok = (N == 8 || N == 16 || N == 32) && a->dim % rpb == 0 && want &&
                         a->state_dim_stride == N && a->state_out_dim_stride == N && a->A_dim_stride == N &&
                         ((a->state_batch_stride * 4) & 15) == 0 && ((a->state_out_batch_stride * 4) & 15) == 0 &&
                         ((a->x_batch_stride * es) & 15) == 0 && ((a->dt_batch_stride * es) & 15) == 0 &&
                         (!a->z || ((a->z_batch_stride * es) & 15) == 0) && ((a->B_batch_stride * es) & 15) == 0 &&
                         ((a->C_batch_stride * es) & 15) == 0 && al(a->state) && al(a->state_out) && al(a->A) &&
-                        al(a->x) && al(a->dt) && (!a->z || al(a->z)) && al(a->B) && al(a->C);
+                        al(a->x) && al(a->dt) && (!a->z || al(a->z)) && al(a->B) && al(a->C) &&
+                        (!a->dt_bias || al(a->dt_bias)) && (!a->D || al(a->D));
         if (ok) {
             DevInfo* di = nullptr;
             int rc = device_info(&di);

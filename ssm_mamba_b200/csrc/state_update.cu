@@ -142,7 +142,7 @@ static cudaError_t launch_upd_t(const UpdParams& p, cudaStream_t stream) {
 // aligned rows and N = 8 * LPC.
 // ---------------------------------------------------------------------------------------
 struct UpdStreamSmem {
-    uint32_t state, A, x, dt, z, B, C, stage, total;
+    uint32_t state, A, x, dt, z, B, C, bias, D, stage, total;
 };
 
 __host__ __device__ inline UpdStreamSmem upd_stream_layout(int rpb, int n, int es, int has_z) {
@@ -156,6 +156,8 @@ __host__ __device__ inline UpdStreamSmem upd_stream_layout(int rpb, int n, int e
     L.z = take(has_z ? (uint32_t)rpb * es : 0u);
     L.B = take((uint32_t)n * es);
     L.C = take((uint32_t)n * es);
+    L.bias = take((uint32_t)rpb * 4u);   // dt_bias and D runs travel with the unit: a global load
+    L.D = take((uint32_t)rpb * 4u);      // of them after the wait would serialise every unit
     L.stage = o;
     L.total = 2u * o + 16u;   // two stages, then two mbarriers
     return L;
@@ -171,7 +173,9 @@ __global__ void __launch_bounds__(256) state_update_stream_kernel(const __grid_c
     const int tid = threadIdx.x, c = tid / LPC, g = tid % LPC, n0 = g * SPT;
     const int ntile = p.dim / RPB;
     const int nunits = p.batch * ntile;
-    const uint32_t unit_bytes = 2u * RPB * N * 4u + (has_z ? 3u : 2u) * RPB * ES + 2u * N * ES;
+    const bool has_bias = p.dt_bias != nullptr, has_D = p.D != nullptr;
+    const uint32_t unit_bytes = 2u * RPB * N * 4u + (has_z ? 3u : 2u) * RPB * ES + 2u * N * ES +
+                                ((has_bias ? 1u : 0u) + (has_D ? 1u : 0u)) * RPB * 4u;
 
     auto issue = [&](int u, int st) {
         const int b = u / ntile, d0 = (u - b * ntile) * RPB;
@@ -184,6 +188,8 @@ __global__ void __launch_bounds__(256) state_update_stream_kernel(const __grid_c
         if (has_z) bulk_load(sm + L.z, static_cast<const IT*>(p.z) + (int64_t)b * p.z_sb + d0, RPB * ES, &bar[st]);
         bulk_load(sm + L.B, static_cast<const IT*>(p.B) + (int64_t)b * p.B_sb, N * ES, &bar[st]);
         bulk_load(sm + L.C, static_cast<const IT*>(p.C) + (int64_t)b * p.C_sb, N * ES, &bar[st]);
+        if (has_bias) bulk_load(sm + L.bias, p.dt_bias + d0, RPB * 4, &bar[st]);
+        if (has_D) bulk_load(sm + L.D, p.D + d0, RPB * 4, &bar[st]);
     };
 
     // programmatic dependent launch: everything read below may come from the previous kernel
@@ -229,7 +235,7 @@ __global__ void __launch_bounds__(256) state_update_stream_kernel(const __grid_c
         }
         const float xv = to_f(*reinterpret_cast<const IT*>(sm + L.x + c * ES));
         const float dtv = to_f(*reinterpret_cast<const IT*>(sm + L.dt + c * ES));
-        const float bias = p.dt_bias ? __ldg(p.dt_bias + d) : 0.f;
+        const float bias = has_bias ? *reinterpret_cast<const float*>(sm + L.bias + c * 4) : 0.f;
         const float x0 = dtv + bias;
         const float dl = p.dt_softplus ? softplus_series(x0) : x0;
         const float dx = dl * xv;
@@ -246,7 +252,7 @@ __global__ void __launch_bounds__(256) state_update_stream_kernel(const __grid_c
         for (int s4 = 0; s4 < SPT; s4 += 4)
             *reinterpret_cast<float4*>(ho + s4) = make_float4(h[s4], h[s4 + 1], h[s4 + 2], h[s4 + 3]);
         if (g == 0) {
-            float o = fmaf(p.D ? __ldg(p.D + d) : 0.f, xv, y);
+            float o = fmaf(has_D ? *reinterpret_cast<const float*>(sm + L.D + c * 4) : 0.f, xv, y);
             if (has_z) {
                 const float zv = to_f(*reinterpret_cast<const IT*>(sm + L.z + c * ES));
                 o = o * zv * sigmoid_io<IT>(zv);
