@@ -681,12 +681,13 @@ def run_prefill_lm(dev, dtype, variants, reps=3, pg=None, world=1, rank=0, norm=
 TRAIN = dict(batch=8, seqlen=2048, model=768, inner=1536, state=16, rank=48, width=4)
 
 
-def run_train_layer(dev, dtype, variants, reps=10):
+def run_train_layer(dev, dtype, variants, reps=10, graph=False):
     """One Mamba-130M-shape layer (the config-2 scan inside it: batch 8, seqlen 2048, model
     768, d_inner 1536, d_state 16, dt_rank 48, conv width 4) trained for one step: the
     layer's forward and backward with every weight a leaf (modules/mamba.py:100-186 and its
     autograd), random weights ~ N(0, 0.02) (seed 13).  `variants` maps a label to
-    layer(weights, hidden) -> output."""
+    layer(weights, hidden) -> output.  With `graph`, the first variant's step is also
+    captured once in a CUDA graph and replayed."""
     import torch
     from ssm_mamba_b200.decode import MambaLayerWeights
     from ssm_mamba_b200.workloads import dt_bias_init, s4d_real_A
@@ -713,6 +714,19 @@ def run_train_layer(dev, dtype, variants, reps=10):
         try:
             ms = _time_steps(step, 2, reps)
             res[label] = {"ms_per_step": ms, "tokens_per_s": c["batch"] * c["seqlen"] / (ms / 1e3)}
+            if graph and label == next(iter(variants)):
+                s = torch.cuda.Stream()
+                s.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(s):
+                    step()
+                torch.cuda.current_stream().wait_stream(s)
+                cg = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(cg):
+                    step()
+                gms = _time_steps(cg.replay, 2, reps)
+                res[label].update({"graph_ms_per_step": gms,
+                                   "graph_tokens_per_s": c["batch"] * c["seqlen"] / (gms / 1e3)})
+                del cg
         except Exception as e:  # one variant failing must not hide the others
             res[label] = {"error": str(e)[:200]}
         torch.cuda.empty_cache()
@@ -910,7 +924,7 @@ def run_ours(args, world, rank, local, pg):
     train = None
     if world == 1 and not args.no_layer:
         v = _ours_prefill_variants()
-        train = {"bf16": run_train_layer(dev, torch.bfloat16, v)}
+        train = {"bf16": run_train_layer(dev, torch.bfloat16, v, graph=True)}
         if not args.no_fp32:
             train["fp32"] = run_train_layer(dev, torch.float32, v, reps=5)
     varlen = None
