@@ -779,6 +779,9 @@ def run_ours(args, world, rank, local, pg):
     dev = torch.device("cuda", local)
     if args.decode_only:
         return {"decode": run_decode(args, world, rank, local, pg, measured_peaks()[0])}
+    if args.decode_layer_only:
+        return {"decode_layer": {"bf16": run_decode_layer(dev, _ours_layer_factory(dev, torch.bfloat16),
+                                                          "ssm_mamba_b200.decode.mamba_layer_step (+ GraphedStep)")}}
     if args.prefill_only:
         v = dict(list(_ours_prefill_variants().items())[:1])     # mamba_layer_forward only
         return {"prefill_lm": {"bf16": run_prefill_lm(dev, torch.bfloat16, v, norm=_fused_rms_norm)}}
@@ -1168,6 +1171,8 @@ def main():
     ap.add_argument("--no-conv", action="store_true", help="skip the conv1d + SiLU measurement")
     ap.add_argument("--no-layer", action="store_true", help="skip the whole-layer decode measurement")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 causal LM prefill measurement")
+    ap.add_argument("--decode-layer-only", action="store_true",
+                    help="profiling aid: only the bf16 whole-layer decode step")
     ap.add_argument("--prefill-only", action="store_true",
                     help="profiling aid: only the config-4 prefill through mamba_layer_forward")
     ap.add_argument("--no-fp32", action="store_true",
