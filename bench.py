@@ -322,7 +322,7 @@ def run_long_seq(args, world, rank, local, pg, peak):
     from ssm_mamba_b200.slices import SliceGroup, plan_segments, sliced_scan
     from ssm_mamba_b200.workloads import scan_inputs
     dev = torch.device("cuda", local)
-    Ltot, Dm, N = CFG5["seqlen"], CFG5["dim"], CFG5["dstate"]
+    Ltot, Dm, N = (args.long_seqlen or CFG5["seqlen"]), CFG5["dim"], CFG5["dstate"]
     Lr = Ltot // world
     inp = scan_inputs(1, Dm, Lr, N, torch.bfloat16, seed=4 + rank, device=dev, with_z=True)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
@@ -1171,6 +1171,8 @@ def main():
     ap.add_argument("--no-conv", action="store_true", help="skip the conv1d + SiLU measurement")
     ap.add_argument("--no-layer", action="store_true", help="skip the whole-layer decode measurement")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 causal LM prefill measurement")
+    ap.add_argument("--long-seqlen", type=int, default=0,
+                    help="profiling aid: config 5 at this total seqlen instead of 131072 (a small ncu case)")
     ap.add_argument("--decode-layer-only", action="store_true",
                     help="profiling aid: only the bf16 whole-layer decode step")
     ap.add_argument("--prefill-only", action="store_true",
