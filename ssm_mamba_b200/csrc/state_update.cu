@@ -135,11 +135,12 @@ static cudaError_t launch_upd_t(const UpdParams& p, cudaStream_t stream) {
 // ---------------------------------------------------------------------------------------
 // Streamed variant for contiguous layouts: persistent CTAs walk work units (batch row b,
 // tile of RPB = 256 / LPC channels).  A unit's inputs are contiguous runs -- the state and
-// A tiles (RPB * N floats each), the x, dt, z runs (RPB elements) and the B, C rows (N
-// elements) -- that thread 0 brings into a two-stage shared-memory pipeline with 1-D bulk
-// copies completing on an mbarrier, one unit ahead of the compute, so state loads stay in
-// flight across units instead of waiting for new CTAs.  Needs dim % RPB == 0, 16-byte
-// aligned rows and N = 8 * LPC.
+// A tiles (RPB * N floats each), the x, dt, z runs (RPB elements), the B, C rows (N
+// elements) and the dt_bias, D runs (RPB floats) -- that thread 0 brings into a two-stage
+// shared-memory pipeline with 1-D bulk copies completing on an mbarrier, one unit ahead of
+// the compute, so state loads stay in flight across units instead of waiting for new CTAs,
+// and no global load sits between a unit's wait and its arithmetic.  Needs dim % RPB == 0,
+// 16-byte aligned rows and N = 8 * LPC.
 // ---------------------------------------------------------------------------------------
 struct UpdStreamSmem {
     uint32_t state, A, x, dt, z, B, C, bias, D, stage, total;
