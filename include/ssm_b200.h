@@ -210,7 +210,14 @@ SSM_API int ssm_scan_bwd(const ssm_scan_bwd_args* args, void* workspace, size_t 
  * the array: calls whose kernels overlap on the GPU race and must be serialised. */
 SSM_API int ssm_scan_bwd_noalloc(const ssm_scan_bwd_args* args, void* stream);
 
-/* One decode step (replaces selective_update.apply).  state_out may alias state. */
+/* One decode step (replaces selective_update.apply).  state_out may alias state.
+ * Contiguous operands (state, state_out and A with a dim stride of dstate; 16-byte
+ * aligned pointers and batch strides, dt_bias and D included) with dstate 8, 16 or 32 and
+ * dim a multiple of 256 / (dstate / 8) take the streamed kernel (persistent CTAs, bulk
+ * copies); any other layout takes the per-CTA kernel.  Both compute the same arithmetic in
+ * the same order.  With launch_flags & SSM_LAUNCH_PDL the kernel is launched with
+ * programmatic dependent launch and waits for the previous kernel in the stream before
+ * reading any input. */
 SSM_API int ssm_state_update(const ssm_state_update_args* args, void* stream);
 
 /* ---- sequence slices ---------------------------------------------------------------------
