@@ -128,6 +128,35 @@ def test_long_sequence_segments_bf16_properties(cuda, monkeypatch):
     assert_close(h4, h1, 1e-3, 1e-4, "h_last")
 
 
+def test_config5_full_size_segmented_equals_one_pass(cuda, monkeypatch):
+    """Config 5 at its full size (batch 1, d_inner 5120, seqlen 131072, bf16, z gate), forward
+    and backward: the planned segmentation (16 segments) against one unsegmented pass of
+    the same kernels, as a size-independent property (same math, other association
+    order: outputs within bf16 rounding, the final state and the parameter gradients to
+    float32 accuracy)."""
+    from ssm_mamba_b200 import selective_scan_fn
+    inp = scan_inputs(1, 5120, 131072, 16, torch.bfloat16, seed=4, device=cuda, with_z=True)
+
+    def run(segments):
+        monkeypatch.setenv("SSM_SEGMENTS", str(segments))
+        leaves = [t.clone().requires_grad_() for t in (inp.A, inp.D, inp.delta_bias)]
+        u = inp.u.clone().requires_grad_()
+        out, h = selective_scan_fn(u, inp.delta, leaves[0], inp.B, inp.C, leaves[1], z=inp.z,
+                                   delta_bias=leaves[2], delta_softplus=True, return_last_state=True)
+        out.backward(inp.dout)
+        torch.cuda.synchronize()
+        return out.detach(), h.detach(), u.grad, [t.grad for t in leaves]
+
+    o16, h16, du16, g16 = run(16)
+    o1, h1, du1, g1 = run(1)
+    assert torch.isfinite(o16.float()).all() and torch.isfinite(du16.float()).all()
+    assert_close(o16, o1, 1e-2, 5e-2, "out")
+    assert_close(h16, h1, 1e-3, 1e-4, "h_last")
+    assert_close(du16, du1, 1e-2, 5e-2, "du")
+    for name, a, b in zip(["dA", "dD", "ddelta_bias"], g16, g1):
+        assert_grad_close(a, b, name, rtol=1e-3)
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_sequence_parallel_two_gpus():
     """Two ranks over NCCL, each with half of a sequence (and 2 segments of it), against
