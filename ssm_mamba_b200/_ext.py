@@ -12,6 +12,6 @@ try:
 except ImportError as e:  # pragma: no cover - exercised only on an unbuilt tree
     raise ImportError(
         "ssm_mamba_b200 native library is not built (ssm_mamba_b200/_C*.so and "
-        "ssm_mamba_b200/lib/libssm_b200.so); run `python -m ssm_mamba_b200.build`") from e
+        "ssm_mamba_b200/lib/libssm_b200.so); run `python ssm_mamba_b200/build.py`") from e
 
 __all__ = ["_C"]

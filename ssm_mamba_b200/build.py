@@ -5,7 +5,8 @@
   _C.<abi>.so         -- the torch binding (g++ against torch's headers), linked to the
                          library above through an $ORIGIN rpath
 
-Run `python -m ssm_mamba_b200.build` (or __graft_entry__.build()).  Objects go to _build/.
+Run `python ssm_mamba_b200/build.py` (or __graft_entry__.build()) -- by path: importing
+the package needs the extension this builds.  Objects go to _build/.
 Both outputs are written next to the sources so they travel with the tree.
 """
 from __future__ import annotations

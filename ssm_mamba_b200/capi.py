@@ -135,7 +135,7 @@ def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
         if not os.path.exists(LIB_PATH):
-            raise OSError(f"{LIB_PATH} is not built; run `python -m ssm_mamba_b200.build`")
+            raise OSError(f"{LIB_PATH} is not built; run `python ssm_mamba_b200/build.py`")
         L = ctypes.CDLL(LIB_PATH)
         L.ssm_last_error.restype = ctypes.c_char_p
         L.ssm_version.restype = ctypes.c_char_p
