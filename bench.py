@@ -149,6 +149,32 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
+def bind_host_to_gpu(local):
+    """Pin this process to the CPU cores NVML reports as local to GPU `local` (a read-only
+    NVML query; only this process's CPU affinity changes), so that pinned host buffers
+    allocated next live on the GPU's own NUMA node.  Best effort: any failure leaves the
+    affinity alone and returns None."""
+    try:
+        import pynvml
+        import torch
+        pr = torch.cuda.get_device_properties(local)
+        bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (int(w) >> b) & 1}
+        cpus &= set(range(os.cpu_count()))
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            return sorted(cpus)
+    except Exception:
+        pass
+    return None
+
+
 def dist_setup(want_nccl=True):
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -840,6 +866,10 @@ def run_ours(args, world, rank, local, pg):
     # the same); the timed region covers all copies of all steps.
     e2e = None
     e2e_steps = 0 if args.no_e2e else min(args.steps, 20)
+    # the host side of the end-to-end loop runs on the GPU's own NUMA node (restored after,
+    # so the host baselines below keep every core)
+    saved_cpus = os.sched_getaffinity(0)
+    bound_cpus = bind_host_to_gpu(local) if e2e_steps else None
     f = lambda t: t.detach().to("cpu").pin_memory()  # noqa: E731
     host_in = {k: f(getattr(inp, k)) for k in ("u", "delta", "z", "B", "C", "dout")}
     A = inp.A.clone().requires_grad_()
@@ -900,9 +930,11 @@ def run_ours(args, world, rank, local, pg):
         d2h = sum(v.numel() * v.element_size() for v in host_out[0].values())
         e2e = {"value": (fwd_bytes + bwd_bytes) * e2e_steps * world / (e2e_ms / 1e3) / 1e12, "unit": "TB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / e2e_steps,
-               "steps": e2e_steps,
+               "steps": e2e_steps, "host_cpus": len(bound_cpus) if bound_cpus else None,
                "api": "ssm_mamba_b200.selective_scan_fn forward + autograd backward; copies double-buffered "
                       "on separate streams"}
+    del host_in, host_out, dev_in
+    os.sched_setaffinity(0, saved_cpus)
 
     decode = None if args.no_decode else run_decode(args, world, rank, local, pg, peak)
     long_seq = None if args.no_long else run_long_seq(args, world, rank, local, pg, peak)
