@@ -210,13 +210,22 @@ def barrier(pg):
 
 
 # ---------------------------------------------------------------------------------------
+def host_oracle():
+    """The oracle module with its OpenMP pool sized to every core this process may run on:
+    a multi-rank launcher sets OMP_NUM_THREADS=1 for its ranks, and the host baselines are
+    timed on all cores."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    oracle.set_num_threads(len(os.sched_getaffinity(0)))
+    return oracle
+
+
 def cpu_baseline_sample(target_s=10.0, batch=1, dim=96):
     """The oracle's float build (C + OpenMP, all host cores) on a bounded sample of the
     config-2 workload: (batch, dim) rows of the same seqlen / d_state."""
     import numpy as np
     import torch
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle
+    oracle = host_oracle()
     from ssm_mamba_b200.workloads import scan_inputs
     L, N = CFG2["seqlen"], CFG2["dstate"]
     inp = scan_inputs(batch, dim, L, N, torch.bfloat16, seed=1, device="cpu", with_z=True)
@@ -244,8 +253,7 @@ def cpu_decode_sample(target_s=3.0):
     5120, d_state 16, bf16-valued inputs in float32), repeated for about `target_s`."""
     import numpy as np
     import torch
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle
+    oracle = host_oracle()
     from ssm_mamba_b200.workloads import decode_inputs
     Bd, Dd, Nd = CFG3["batch"], CFG3["dim"], CFG3["dstate"]
     dec = decode_inputs(Bd, Dd, Nd, 4, torch.bfloat16, seed=2, device="cpu")
@@ -270,8 +278,7 @@ def cpu_long_seq_sample(target_s=3.0, dim=48, seqlen=8192):
     channels of a truncated seqlen, scaled linearly to 5120 channels x 131072 tokens."""
     import numpy as np
     import torch
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle
+    oracle = host_oracle()
     from ssm_mamba_b200.workloads import scan_inputs
     N = CFG5["dstate"]
     inp = scan_inputs(1, dim, seqlen, N, torch.bfloat16, seed=4, device="cpu", with_z=True)
@@ -1012,9 +1019,8 @@ def run_reference(args, world, rank, local, pg):
     import torch
     if rank != 0:
         return None
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np
-    import oracle
+    oracle = host_oracle()
     from ssm_mamba_b200.workloads import scan_inputs
     L, N = CFG2["seqlen"], CFG2["dstate"]
     sb, sd = 1, 48

@@ -57,11 +57,20 @@ def lib():
             f.argtypes = [i64] * 3 + [p] * 4 + [i32, p]
             f.restype = i32
         _lib.oracle_num_threads.restype = i32
+        _lib.oracle_set_num_threads.argtypes = [i32]
+        _lib.oracle_set_num_threads.restype = None
     return _lib
 
 
 def num_threads() -> int:
     return int(lib().oracle_num_threads())
+
+
+def set_num_threads(n: int) -> int:
+    """Use n OpenMP threads in the following oracle calls from this thread; returns the
+    count now in effect."""
+    lib().oracle_set_num_threads(int(n))
+    return num_threads()
 
 
 def _ptr(a):

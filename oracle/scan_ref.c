@@ -38,3 +38,13 @@ int oracle_num_threads(void) {
     return 1;
 #endif
 }
+
+/* Threads for the following parallel regions of the calling thread (n > 0).  A launcher
+   may have set OMP_NUM_THREADS=1 for its ranks; a host baseline sets its own count. */
+void oracle_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}

@@ -173,3 +173,17 @@ def test_oracle_backward_passes_gradcheck():
     u, delta, A, B, C, D, z, bias, h0 = _rand(1, 2, 40, 3, True, True, seed=11)
     assert torch.autograd.gradcheck(_OracleScan.apply, (u, delta, A, B, C, D, z, bias, h0), eps=1e-6,
                                     atol=1e-7, rtol=1e-5)
+
+
+def test_oracle_thread_count_overrides_launcher_setting():
+    """A multi-rank launcher exports OMP_NUM_THREADS=1; the host baselines set their own
+    count through oracle.set_num_threads."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    code = ("import sys; sys.path.insert(0, %r); import oracle; "
+            "print(oracle.num_threads(), oracle.set_num_threads(3))" % os.path.join(os.path.dirname(here), "oracle"))
+    env = dict(os.environ, OMP_NUM_THREADS="1")
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, check=True)
+    assert out.stdout.split() == ["1", "3"]
