@@ -56,9 +56,10 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def traffic_from_profiles(name):
+def traffic_from_profiles(name, key="traffic_bytes_per_launch"):
     """Per-launch DRAM bytes of a kernel, from a committed ncu summary (profiles/*.txt
-    lines `traffic_bytes_per_launch <kernel> <bytes>`), or None."""
+    lines `traffic_bytes_per_launch <kernel> <bytes>`; another per-launch figure with
+    `key`), or None."""
     d = os.path.join(ROOT, "profiles")
     if not os.path.isdir(d):
         return None
@@ -68,7 +69,7 @@ def traffic_from_profiles(name):
         with open(os.path.join(d, fn)) as f:
             for line in f:
                 parts = line.split()
-                if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch" and parts[1] == name:
+                if len(parts) == 3 and parts[0] == key and parts[1] == name:
                     return float(parts[2])
     return None
 
@@ -986,6 +987,20 @@ def run_ours(args, world, rank, local, pg):
 
     bwd_gbs = bwd_bytes / (bwd_ms / 1e3) / 1e9
     fwd_gbs = fwd_bytes / (fwd_ms / 1e3) / 1e9
+    # The scan kernels are bound by instruction issue, not HBM: warp instructions per launch
+    # (ncu, committed summaries) over the measured duration, against 4 warp instructions per
+    # clock per SM at the SM clock sampled during the timed region.
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    mhz = (clk or {}).get("sm_mhz") or (clk or {}).get("sm_max_mhz") or 1965.0
+    issue_peak = 4.0 * sms * mhz * 1e6
+    issue = {"what": "warp instructions issued per second against 4 per clock per SM (the issue limit) "
+                     "at the sampled SM clock; instruction counts from ncu (profiles/)",
+             "sm_mhz": mhz, "sms": sms, "peak_warp_inst_per_s": issue_peak}
+    for kname, ms_k in (("scan_bwd_kernel", bwd_ms), ("scan_fwd_kernel", fwd_ms)):
+        n_inst = traffic_from_profiles(kname, key="warp_instructions_per_launch")
+        if n_inst:
+            issue[kname] = {"warp_inst_per_launch": n_inst, "achieved_warp_inst_per_s": n_inst / (ms_k / 1e3),
+                            "frac": n_inst / (ms_k / 1e3) / issue_peak}
     line = {
         "metric": "scan fwd+bwd achieved HBM TB/s (% of peak) at 1/2/4/8 B200; decode tokens/s",
         "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -1006,6 +1021,7 @@ def run_ours(args, world, rank, local, pg):
         "roofline_fwd": {"bound": "hbm", "kernel": "scan_fwd_kernel", "achieved": fwd_gbs, "peak": peak,
                          "unit": "GB/s", "frac": fwd_gbs / peak, "traffic": traffic_from_profiles("scan_fwd_kernel"),
                          "algorithmic_bytes_per_launch": fwd_bytes},
+        "issue_roof": issue,
         "e2e": e2e, "gpu_launches": 3 * args.steps, "clocks": clk, "decode": decode, "long_seq": long_seq,
         "cpu_baseline": cpu, "fp32_equal_precision": eq, "conv1d": conv, "decode_layer": layer,
         "prefill_lm": prefill, "varlen": varlen, "train_layer": train,
