@@ -197,8 +197,10 @@ int encode3d(CUtensorMap* map, const void* ptr, int is_bf16, int64_t d0, int64_t
 // minimises the estimated time on the busiest SM: CTAs are spread evenly over the SMs and
 // run `res` at a time (res from the occupancy calculator), an SM is assumed to reach full
 // throughput at 8 resident warps, and every CTA pays a fixed cost worth `ovh` channels
-// (staging B and C for its batch row; in the backward also its dB/dC partials).  Results
-// are cached per shape.
+// (staging B and C for its batch row; in the backward also its dB/dC partials).  For the
+// scan forward and backward ovh is 8: measured on B200, the forward at 4 x 5120 x 2048
+// takes 420 us with 32 channels per CTA and 433 us with 16, which an overhead of 4 ranked
+// the other way round.  Results are cached per shape.
 template <typename OccFn>
 int choose_dt(int64_t batch, int64_t dim, int lpc, int sms, double ovh, OccFn occupancy) {
     const int cpw = 32 / lpc;
@@ -243,7 +245,7 @@ int cached_dt(DtKey key, int sms, OccFn occ) {
         for (int i = 0; i < g_dt_n; i++)
             if (g_dt_keys[i] == key) return g_dt_vals[i];
     }
-    const int dt = choose_dt(key.batch, key.dim, key.lpc, sms, key.kind == 1 ? 8.0 : 4.0, occ);
+    const int dt = choose_dt(key.batch, key.dim, key.lpc, sms, key.kind <= 1 ? 8.0 : 4.0, occ);
     std::lock_guard<std::mutex> lk(g_dt_mu);
     const int slot = g_dt_n < 64 ? g_dt_n++ : (int)(key.dim % 64);
     g_dt_keys[slot] = key;
