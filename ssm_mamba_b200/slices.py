@@ -36,9 +36,10 @@ from ._ext import _C
 # The scan kernels run 3 CTAs of 128 threads per SM; segmenting stops once the rows give
 # this many full waves of them.  Measured on B200, long-sequence config (batch 1, d_inner
 # 5120, seqlen 131072, bf16, fwd+bwd): 1 segment 54.0 ms, 2: 43.3, 4: 39.1, 8: 33.7,
-# 16: 32.4 -- the gain continues to ~5-6 waves.
+# 16: 32.4 (an earlier build); with the current kernels 8: 30.8, 16: 29.6, 32: 28.7,
+# 64: 28.7 -- the gain continues to ~8 waves.
 _CTAS_PER_SM = 3
-_TARGET_WAVES = 4
+_TARGET_WAVES = 8
 
 
 def plan_segments(batch: int, dim: int, seqlen: int, dstate: int, sms: int = 148,
