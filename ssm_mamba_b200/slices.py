@@ -37,13 +37,14 @@ from ._ext import _C
 # this many full waves of them.  Measured on B200, long-sequence config (batch 1, d_inner
 # 5120, seqlen 131072, bf16, fwd+bwd): 1 segment 54.0 ms, 2: 43.3, 4: 39.1, 8: 33.7,
 # 16: 32.4 (an earlier build); with the current kernels 8: 30.8, 16: 29.6, 32: 28.7,
-# 64: 28.7 -- the gain continues to ~8 waves.
+# 64: 28.7 -- the gain continues to ~8 waves.  Segments of 512 tokens still pay: a 16384-token
+# slice (config 5 on each of 8 GPUs) takes 3.84 ms as 16 segments and 3.77 ms as 32.
 _CTAS_PER_SM = 3
 _TARGET_WAVES = 8
 
 
 def plan_segments(batch: int, dim: int, seqlen: int, dstate: int, sms: int = 148,
-                  min_segment: int = 1024) -> int:
+                  min_segment: int = 512) -> int:
     """Number of segments (a power of two) to split a sequence into on one GPU: 1 unless
     batch == 1 and batch * dim rows leave the SMs short of warps.  Every segment is a
     multiple of 128 tokens and at least `min_segment` long.  SSM_SEGMENTS overrides."""

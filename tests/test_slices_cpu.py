@@ -78,10 +78,10 @@ def _check(x, fw, g, lo, hi, out, hf, grads, rank0):
 
 def test_plan_segments():
     assert plan_segments(1, 5120, 131072, 16) == 32     # long-sequence config: 32 segments
-    assert plan_segments(1, 5120, 16384, 16) == 16      # its slice on each of 8 GPUs: 1024-token segments
+    assert plan_segments(1, 5120, 16384, 16) == 32      # its slice on each of 8 GPUs: 512-token segments
     assert plan_segments(8, 1536, 2048, 16) == 1        # batch > 1: never
     assert plan_segments(1, 64, 300, 16) == 1           # not a multiple of 256 tokens
-    assert plan_segments(1, 64, 2048, 16) == 2          # segments stay >= 1024 tokens
+    assert plan_segments(1, 64, 2048, 16) == 4          # segments stay >= 512 tokens
 
 
 def test_segment_view_is_a_view():
