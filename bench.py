@@ -360,7 +360,7 @@ def run_long_seq(args, world, rank, local, pg, peak):
     Lr = Ltot // world
     inp = scan_inputs(1, Dm, Lr, N, torch.bfloat16, seed=4 + rank, device=dev, with_z=True)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    S = plan_segments(1, Dm, Lr, N, sms=sms)
+    S = plan_segments(1, Dm, Lr, N, sms=sms, ranks=world)
     group = SliceGroup(pg.group.WORLD if pg is not None else None)
     leaves = [t.clone().requires_grad_() for t in (inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, inp.z,
                                                    inp.delta_bias)]

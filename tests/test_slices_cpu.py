@@ -78,7 +78,9 @@ def _check(x, fw, g, lo, hi, out, hf, grads, rank0):
 
 def test_plan_segments():
     assert plan_segments(1, 5120, 131072, 16) == 32     # long-sequence config: 32 segments
-    assert plan_segments(1, 5120, 16384, 16) == 32      # its slice on each of 8 GPUs: 512-token segments
+    assert plan_segments(1, 5120, 16384, 16) == 32      # a 16384-token sequence on one GPU: 512-token segments
+    assert plan_segments(1, 5120, 16384, 16, ranks=8) == 16   # the slice of config 5 on each of 8 GPUs
+    assert plan_segments(1, 5120, 65536, 16, ranks=2) == 32   # ... on each of 2 GPUs
     assert plan_segments(8, 1536, 2048, 16) == 1        # batch > 1: never
     assert plan_segments(1, 64, 300, 16) == 1           # not a multiple of 256 tokens
     assert plan_segments(1, 64, 2048, 16) == 4          # segments stay >= 512 tokens
