@@ -200,14 +200,17 @@ SSM_API int ssm_scan_bwd(const ssm_scan_bwd_args* args, void* workspace, size_t 
                  void* stream);
 
 /* Backward selective scan that allocates nothing.  No counterpart in the reference.
- * For callers that cannot allocate device memory when they run the backward (inside a
- * CUDA-graph capture, under a framework that owns all device memory, or through an FFI
- * with no allocation API): instead of a caller-provided workspace it uses a 16 MiB
- * scratch array compiled into the library (held on every GPU that loads the library until
- * exit).  Shapes whose ssm_scan_bwd_workspace_size exceeds 16 MiB - 256 bytes are rejected
- * with SSM_ERR_WORKSPACE.  The first call on a device looks up the array's device address
+ * For callers that cannot allocate device memory where they run the backward: a framework
+ * or runtime whose own allocator owns all device memory, or a host-language binding that
+ * reaches this library through a plain C FFI with no device-allocation API.  Instead of a
+ * caller-provided workspace it uses a 16 MiB scratch array compiled into the library (held
+ * on every GPU that loads the library until exit).  Shapes whose
+ * ssm_scan_bwd_workspace_size exceeds 16 MiB - 256 bytes are rejected with
+ * SSM_ERR_WORKSPACE.  The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress); make it before any stream capture.  Every call on a device shares
- * the array: calls whose kernels overlap on the GPU race and must be serialised. */
+ * the array: calls whose kernels overlap on the GPU race and must be serialised.  A bounded
+ * wait that runs out inside its kernels is reported by ssm_check_device_error, like those
+ * of the other entry points. */
 SSM_API int ssm_scan_bwd_noalloc(const ssm_scan_bwd_args* args, void* stream);
 
 /* One decode step (replaces selective_update.apply).  state_out may alias state.
@@ -290,8 +293,10 @@ SSM_API int ssm_conv1d_bwd(const ssm_conv1d_args* args, void* workspace, size_t 
  * out (batch, dim) = act(bias + sum_k weight[k] window[k]). */
 SSM_API int ssm_conv1d_update(const ssm_conv1d_args* args, void* stream);
 
-/* Reads and clears the device-side error word of the current device (synchronizes
- * `stream`).  Returns SSM_OK, or SSM_ERR_DEVICE with *code set to the kernel's code. */
+/* Reads and clears the device-side error words of the current device -- the library's own
+ * and the one in ssm_scan_bwd_noalloc's static scratch -- (synchronizes `stream`; allocates
+ * nothing).  Returns SSM_OK with *code = 0, or SSM_ERR_DEVICE with *code set to the
+ * kernel's code (1: a bounded wait for a TMA copy ran out; 2: misaligned shared memory). */
 SSM_API int ssm_check_device_error(int* code, void* stream);
 
 #ifdef __cplusplus

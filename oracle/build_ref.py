@@ -9,9 +9,17 @@ The only changes are the extension names, set through the TORCH_EXTENSION_NAME m
 in the same process as this repository's drop-in modules named `selective_scan` /
 `selective_update`.
 
+It also stages the reference's Python package (its __init__.py and ops/, modules/,
+models/, utils/) unchanged into oracle/_ref/ssm_mamba_ref/, so that GPU tests can run the
+reference's own modules (Mamba, CausalLM) once on its kernels and once on this library's
+drop-in extension modules (tests/test_reference_modules_gpu.py).
+
 Outputs go only to oracle/_ref/ (git-ignored; it travels to the GPU box with the tree).
 The reference kernels run on the GPU only (the reference has no CPU path), so they are
 used by GPU tests and by tests/golden/make_golden.py to pin the CPU oracle.
+
+The reference checkout is found through the environment variable SSM_REFERENCE_ROOT, or
+as a directory named `reference` beside this repository; without either, nothing is built.
 """
 import os
 import subprocess
@@ -21,8 +29,11 @@ from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-REF = os.environ.get("SSM_REFERENCE_ROOT", "/root/reference")
+REF = os.environ.get("SSM_REFERENCE_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+# the reference's Python package, staged under this name (its own name has a hyphen)
+PKG = "ssm_mamba_ref"
+PKG_PARTS = ["__init__.py", "ops", "modules", "models", "utils"]
 
 EXTS = {
     "ref_selective_scan": ["selective_scan/bindings.cpp", "selective_scan/selective_scan.cpp",
@@ -50,11 +61,39 @@ def available() -> bool:
     return all(os.path.exists(lib_path(n)) for n in EXTS)
 
 
+def package_available() -> bool:
+    return os.path.exists(os.path.join(OUT, PKG, "__init__.py"))
+
+
+def stage_package() -> bool:
+    """Copy the reference's Python package (unchanged) to oracle/_ref/ssm_mamba_ref/."""
+    import shutil
+    if not os.path.isfile(os.path.join(REF, "__init__.py")):
+        return False
+    dst = os.path.join(OUT, PKG)
+    tmp = dst + ".tmp"
+    shutil.rmtree(tmp, ignore_errors=True)
+    os.makedirs(tmp)
+    for part in PKG_PARTS:
+        src = os.path.join(REF, part)
+        if os.path.isdir(src):
+            shutil.copytree(src, os.path.join(tmp, part), ignore=shutil.ignore_patterns("__pycache__", "*.pyc"))
+        elif os.path.isfile(src):
+            shutil.copy2(src, os.path.join(tmp, part))
+    shutil.rmtree(dst, ignore_errors=True)
+    os.replace(tmp, dst)
+    return True
+
+
 def build(force: bool = False) -> bool:
-    """Build both reference extensions.  Returns False when the reference tree is absent."""
+    """Build both reference extensions and stage the reference's Python package.  Returns
+    False when the reference tree is absent."""
     csrc = os.path.join(REF, "csrc")
     if not os.path.isdir(csrc):
         return False
+    os.makedirs(OUT, exist_ok=True)
+    if force or not package_available():
+        stage_package()
     if available() and not force:
         return True
     os.makedirs(OUT, exist_ok=True)

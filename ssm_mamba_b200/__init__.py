@@ -12,7 +12,17 @@ Drop-in for the native hot path of nmquan1503/ssm-mamba:
     when compat/ is on sys.path.
 The kernels sit behind the C ABI in include/ssm_b200.h (lib/libssm_b200.so).
 """
-from .ops import (SelectiveScanFn, SelectiveUpdateFn, causal_conv1d_fn,  # noqa: F401
-                  causal_conv1d_update, selective_scan_fn, selective_state_update)
-
 __version__ = "0.1.0"
+
+_OPS = ("SelectiveScanFn", "SelectiveUpdateFn", "causal_conv1d_fn", "causal_conv1d_update",
+        "selective_scan_fn", "selective_state_update")
+__all__ = list(_OPS)
+
+
+def __getattr__(name):
+    # The ops (and with them the native library) load on first use, so that the pure-torch
+    # submodules (workloads, weights) import without the extension.
+    if name in _OPS:
+        from . import ops
+        return getattr(ops, name)
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")

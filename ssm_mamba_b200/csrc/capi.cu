@@ -48,6 +48,7 @@ cudaError_t launch_conv1d_reduce(const float* ws, int nparts, int dim, int width
                                  float* dbias, int sms, cudaStream_t stream);
 cudaError_t launch_conv1d_update(const ConvParams& p, int is_bf16, int width, int sms, cudaStream_t stream);
 size_t bwd_smem_bytes(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
+int* noalloc_error_word();
 int fwd_occupancy(int is_bf16, int lpc, int spt, int dt, int has_z, int has_y);
 int bwd_occupancy(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
 }  // namespace ssm
@@ -125,6 +126,15 @@ struct DevInfo {
 };
 std::mutex g_mu;
 DevInfo g_dev[64];
+
+// The current device's DevInfo if an entry point has set it up, else nullptr (allocates
+// nothing: no kernel can have written an error word that does not exist yet).
+DevInfo* device_info_if_ready() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    return g_dev[dev].sms != 0 ? &g_dev[dev] : nullptr;
+}
 
 int device_info(DevInfo** out) {
     int dev = 0;
@@ -527,6 +537,8 @@ int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, i
             (rc = encode3d(&maps[9], a->dz, is_bf16, L, Dm, Bs, a->dz_dim_stride, a->dz_batch_stride, TB, dt, osw)))
             return rc;
     }
+    // the forward's failure-detection test hook (SSM_TEST_WITHHOLD_TMA), for the backward
+    p.test_withhold = p.use_tma && getenv("SSM_TEST_WITHHOLD_TMA") != nullptr;
     cudaError_t e = launch_scan_bwd(p, is_bf16, sp.lpc, sp.spt, maps, stream);
     if (e != cudaSuccess) return cuda_fail(e, "scan_bwd launch");
 
@@ -848,20 +860,27 @@ int ssm_conv1d_update(const ssm_conv1d_args* a, void* stream) {
 }
 
 int ssm_check_device_error(int* code, void* stream_) {
-    DevInfo* di;
-    int rc = device_info(&di);
-    if (rc) return rc;
+    // two words can hold a code: the library's per-device word (every entry point but
+    // ssm_scan_bwd_noalloc) and the one at the end of ssm_scan_bwd_noalloc's static
+    // scratch; both are read, and a word that holds a code is cleared.  Allocates nothing.
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-    int v = 0;
-    cudaError_t e = cudaMemcpyAsync(&v, di->err, sizeof(int), cudaMemcpyDeviceToHost, stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
-    if (e != cudaSuccess) return cuda_fail(e, "ssm_check_device_error");
-    if (code) *code = v;
-    if (v != 0) {
-        cudaMemsetAsync(di->err, 0, sizeof(int), stream);
-        cudaStreamSynchronize(stream);
-        return fail(SSM_ERR_DEVICE, "a kernel reported device error %d", v);
+    int* words[2] = {nullptr, ssm::noalloc_error_word()};
+    if (DevInfo* di = device_info_if_ready()) words[0] = di->err;
+    int v[2] = {0, 0};
+    for (int i = 0; i < 2; i++) {
+        if (!words[i]) continue;
+        cudaError_t e = cudaMemcpyAsync(&v[i], words[i], sizeof(int), cudaMemcpyDeviceToHost, stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return cuda_fail(e, "ssm_check_device_error");
+        if (v[i] != 0) {
+            e = cudaMemsetAsync(words[i], 0, sizeof(int), stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+            if (e != cudaSuccess) return cuda_fail(e, "ssm_check_device_error (clear)");
+        }
     }
+    const int c = v[0] != 0 ? v[0] : v[1];
+    if (code) *code = c;
+    if (c != 0) return fail(SSM_ERR_DEVICE, "a kernel reported device error %d", c);
     return SSM_OK;
 }
 

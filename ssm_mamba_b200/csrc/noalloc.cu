@@ -1,23 +1,27 @@
-// Backward selective scan with no allocation of any kind.
+// Backward selective scan that allocates nothing.
 //
-// Some hosts cannot call cudaMalloc at the point where they run the backward: code being
-// captured into a CUDA graph, a custom allocator or a framework that owns all device
-// memory, or an FFI caller that has no device-allocation API at all.  ssm_scan_bwd needs
-// a workspace from its caller; this variant instead uses a fixed scratch buffer compiled
-// into the library as a file-scope __device__ array, so the caller passes only its inputs
-// and outputs.
+// Who needs it: a caller that cannot call cudaMalloc at the point where it runs the
+// backward -- a framework or runtime whose own allocator owns every byte of device memory
+// (a second allocator would fragment or overrun its pool), or a host language binding that
+// reaches this library through a plain C FFI and has no device-allocation API at all.
+// ssm_scan_bwd needs a workspace from its caller; this variant instead uses a fixed
+// scratch buffer compiled into the library as a file-scope __device__ array, so the
+// caller passes only its inputs and outputs.
 //
 // The array is kStaticScratchBytes (16 MiB) on every GPU that loads the library, held until
-// the process exits.  The last 256 bytes are the error word of this variant's kernels; the
-// rest is the backward's workspace, so shapes whose workspace
-// (ssm_scan_bwd_workspace_size) exceeds kStaticWorkspaceBytes are rejected.  The workspace
-// is fully overwritten by every call (the per-tile and per-batch partials cover every output
-// element), so nothing needs clearing between calls.  All calls on a device share the array:
-// two calls whose kernels overlap on the GPU (different streams, or different host threads)
-// race on it and must be serialised by the caller.
+// the process exits.  Its last 256 bytes hold the error word of this variant's kernels
+// (zero at load; a bounded wait that runs out writes its code there, and
+// ssm_check_device_error reads and clears it); the rest is the backward's workspace, so
+// shapes whose workspace (ssm_scan_bwd_workspace_size) exceeds kStaticWorkspaceBytes are
+// rejected.  The workspace is fully overwritten by every call (the per-tile and per-batch
+// partials cover every output element), so nothing in it needs clearing between calls.
+// All calls on a device share the array: two calls whose kernels overlap on the GPU
+// (different streams, or different host threads) race on it and must be serialised by
+// the caller.
 //
 // The device address of the array is obtained once per device, on that device's first
-// call, with cudaGetSymbolAddress; make that first call before any stream capture.
+// call, with cudaGetSymbolAddress (host code cannot use the array's name as a device
+// address); the first call on a device should therefore come before any stream capture.
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -73,6 +77,20 @@ int static_setup(StaticDev** out) {
 }
 
 }  // namespace
+
+namespace ssm {
+
+// Device address of the current device's noalloc error word, or nullptr when no
+// ssm_scan_bwd_noalloc call has set that device up (its kernels cannot have written it).
+int* noalloc_error_word() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    const StaticDev& s = g_static_dev[dev];
+    return s.ready ? reinterpret_cast<int*>(s.base + kStaticWorkspaceBytes) : nullptr;
+}
+
+}  // namespace ssm
 
 extern "C" int ssm_scan_bwd_noalloc(const ssm_scan_bwd_args* args, void* stream) {
     if (!args) {

@@ -67,6 +67,7 @@ struct BwdParams {
     float* ws_a;         // (batch, dim, dstate): per-batch dA
     float* ws_dd;        // (batch, dim, 2): per-batch dD, ddelta_bias
     int* err;
+    int test_withhold;   // test hook: never issue the TMA loads, so the first bounded wait runs out
 };
 
 struct ReduceParams {

@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
         fence_mbar_init();
     }
     __syncthreads();
-    if (p.use_tma && tid == 0) issue(ntiles - 1);
+    if (p.use_tma && tid == 0 && !p.test_withhold) issue(ntiles - 1);
 
     // checkpoint of the first sub-tile processed, then prefetched one sub-tile ahead
     float2 h0[NP], h0n[NP];
@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(128, 3) scan_bwd_kernel(
             }
         }
         __syncthreads();
-        if (p.use_tma && tid == 0 && it > 0) issue(it - 1);  // raw tiles consumed
+        if (p.use_tma && tid == 0 && it > 0 && !p.test_withhold) issue(it - 1);  // raw tiles consumed
 
         // ---- sub-tiles, last to first -------------------------------------------------------
         unsigned char* odu = smem + S.du;

@@ -83,9 +83,15 @@ def segment_view(t: Optional[torch.Tensor], s: int) -> Optional[torch.Tensor]:
 
 class SliceGroup:
     """The ranks that share one sequence (rank r holds the r-th contiguous slice), or a
-    single process (world 1, no communication)."""
+    single process (world 1, no communication).
 
-    def __init__(self, group=None):
+    With a `store` (any torch.distributed Store the ranks share) and a `peer_timeout`
+    (datetime.timedelta), every exchange starts with a host-side liveness check
+    (check_peers): a rank that has left makes the others raise RuntimeError before any
+    collective or kernel of that exchange is launched, instead of leaving a collective on
+    the GPU waiting for the process group's timeout."""
+
+    def __init__(self, group=None, store=None, peer_timeout=None):
         import torch.distributed as dist
         self.group = group
         if group is None:
@@ -93,6 +99,30 @@ class SliceGroup:
         else:
             self.world = dist.get_world_size(group)
             self.rank = dist.get_rank(group)
+        self.store = store
+        self.peer_timeout = peer_timeout
+        self._exchanges = 0
+
+    def check_peers(self, what: str) -> None:
+        """Host-side liveness check before an exchange (no-op without a store): this rank
+        posts that it reached exchange n and waits, at most peer_timeout, until every rank
+        has.  Every rank runs the same exchanges in the same order, so n agrees across ranks.
+        Each rank then deletes its key of exchange n - 2, which every rank has passed."""
+        if self.world == 1 or self.store is None:
+            return
+        n = self._exchanges
+        self._exchanges += 1
+        key = lambda i, r: f"ssm_slices/{i}/{r}"  # noqa: E731
+        self.store.set(key(n, self.rank), what)
+        keys = [key(n, r) for r in range(self.world)]
+        try:
+            self.store.wait(keys, self.peer_timeout)
+        except Exception as e:
+            missing = [r for r in range(self.world) if not self.store.check([key(n, r)])]
+            raise RuntimeError(f"sliced scan: rank(s) {missing} did not reach exchange {n} ({what}) "
+                               f"within {self.peer_timeout}") from e
+        if n >= 2:
+            self.store.delete_key(key(n - 2, self.rank))
 
     def all_gather(self, t: torch.Tensor) -> torch.Tensor:
         """(world, *t.shape): every rank's t, in rank order."""
@@ -158,6 +188,7 @@ class SlicedScanFn(torch.autograd.Function):
         N = A.shape[1]
         if S > 1 and (Bt != 1 or L % S != 0):
             raise ValueError("segmented scan needs batch 1 and seqlen divisible by the segment count")
+        group.check_peers("forward")
         # a peer with other shapes or options would exchange carries of another size: refuse
         group.check_agreement("batch, dim, dstate, segments, z, D, delta_bias, h_init, softplus, dtype",
                               [Bt, Dm, N, S, z is not None, D is not None, delta_bias is not None,
@@ -202,6 +233,7 @@ class SlicedScanFn(torch.autograd.Function):
         sv = lambda t: segment_view(t, S)  # noqa: E731
         dout = dout.contiguous()
         u_s, d_s, B_s, C_s, z_s, dout_s = sv(u), sv(delta), sv(B), sv(C), sv(z), sv(dout)
+        group.check_peers("backward")
         # 1. every local slice's gradient into the state before it, from a zero start
         g0 = k.chunk_state_bwd(d_s, A, C_s, z_s, delta_bias, softplus, dout_s)     # (rows, Dm, N)
         per = Bc * Dm * N

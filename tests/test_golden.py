@@ -3,7 +3,7 @@ kernels (float32, built from the reference sources) on seeded inputs, committed 
 tests/golden/ by tests/golden/make_golden.py.  Runs on the CPU.
 
 Tolerances: forward outputs rtol 1e-4 / atol 1e-5 (float32); gradients rtol 5e-2 with an
-absolute floor of 1% of the largest reference magnitude."""
+absolute floor of 1e-4 of the largest reference magnitude (tests/helpers.py)."""
 import numpy as np
 import pytest
 

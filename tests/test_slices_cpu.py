@@ -200,3 +200,51 @@ def test_peer_failure_gives_a_clean_error(mode):
     else:
         assert procs[1].exitcode == 3
         assert 0 in res and res[0] != "ok", res
+
+
+def _leaving_rank_main(rank, world, port, q):
+    """Two sliced-scan steps with the host-side liveness check; rank 1 leaves after the
+    first step (between steps, nothing in flight)."""
+    import datetime
+    import torch.distributed as dist
+    try:
+        store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=30))
+        dist.init_process_group("gloo", store=store, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        group = SliceGroup(dist.group.WORLD, store=store, peer_timeout=datetime.timedelta(seconds=3))
+        x = _inputs()
+        L = x["u"].shape[-1]
+        lo, hi = rank * L // world, (rank + 1) * L // world
+        _run_slice(x, lo, hi, 2, group, last=rank == world - 1)
+        if rank == 1:
+            msg = "left"          # leaves between steps: exits without a word to its peers
+        else:
+            _run_slice(x, lo, hi, 2, group, last=rank == world - 1)
+            msg = "ok"
+    except Exception as e:  # the clean error this test expects
+        msg = f"{type(e).__name__}: {e}"
+    q.put((rank, msg))
+    q.close()
+    q.join_thread()           # flush the message before the abrupt exit
+    os._exit(0)
+
+
+def test_peer_leaving_between_steps_is_detected_on_the_host():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            r, msg = q.get(timeout=120)
+            res[r] = msg
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert res[1] == "left", res
+    assert res[0].startswith("RuntimeError: sliced scan: rank(s) [1] did not reach exchange 2"), res
