@@ -48,6 +48,8 @@ cudaError_t launch_conv1d_reduce(const float* ws, int nparts, int dim, int width
                                  float* dbias, int sms, cudaStream_t stream);
 cudaError_t launch_conv1d_update(const ConvParams& p, int is_bf16, int width, int sms, cudaStream_t stream);
 size_t bwd_smem_bytes(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
+cudaError_t launch_scan_bwd_pair(const BwdParams& p, int is_bf16, const CUtensorMap* maps, cudaStream_t stream);
+int bwd_pair_occupancy(int is_bf16, int dt, int has_z);
 int* noalloc_error_word();
 int fwd_occupancy(int is_bf16, int lpc, int spt, int dt, int has_z, int has_y);
 int bwd_occupancy(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
@@ -255,7 +257,7 @@ int cached_dt(DtKey key, int sms, OccFn occ) {
         for (int i = 0; i < g_dt_n; i++)
             if (g_dt_keys[i] == key) return g_dt_vals[i];
     }
-    const int dt = choose_dt(key.batch, key.dim, key.lpc, sms, key.kind <= 1 ? 8.0 : 4.0, occ);
+    const int dt = choose_dt(key.batch, key.dim, key.lpc, sms, (key.kind <= 1 || key.kind == 5) ? 8.0 : 4.0, occ);
     std::lock_guard<std::mutex> lk(g_dt_mu);
     const int slot = g_dt_n < 64 ? g_dt_n++ : (int)(key.dim % 64);
     g_dt_keys[slot] = key;
@@ -385,7 +387,19 @@ int ssm_scan_ckpt_from_reference(const ssm_scan_fwd_args* a, const float* ref_ck
 }
 
 // Shape checks and CTA sizing of the backward; touches no device memory.
-static int bwd_shape(const ssm_scan_bwd_args* a, int sms, StateSplit* sp, int* dt) {
+// Backward kernels: scan_bwd_pair_kernel (scan_bwd_pair.cu: two channels per lane) for
+// d_state 16 without `length` when every stream is a TMA source/target, scan_bwd_kernel
+// for everything else.  SSM_BWD_KERNEL=general forces the latter (for comparisons).
+static bool bwd_pair_shape(const ssm_scan_bwd_args* a) {
+    const char* e = getenv("SSM_BWD_KERNEL");
+    if (e && strcmp(e, "general") == 0) return false;
+    return a->dstate == 16 && a->length == nullptr;
+}
+
+// Channels per CTA of both backward kernels for these sizes: *dt for scan_bwd_kernel and
+// *dt_pair for scan_bwd_pair_kernel (0 when the shape does not take it).  The workspace
+// is sized for the smaller (more channel tiles), so it fits whichever kernel runs.
+static int bwd_shape(const ssm_scan_bwd_args* a, int sms, StateSplit* sp, int* dt, int* dt_pair) {
     if (a->batch < 1 || a->dim < 1 || a->seqlen < 1 || a->dstate < 1)
         return fail(SSM_ERR_INVALID, "ssm_scan_bwd: sizes must be positive");
     if (a->dstate > 256) return fail(SSM_ERR_INVALID, "selective_scan only supports state_dim <= 256");
@@ -404,14 +418,23 @@ static int bwd_shape(const ssm_scan_bwd_args* a, int sms, StateSplit* sp, int* d
     key.has_z = has_z; key.has_y = 0; key.batch = a->batch; key.dim = a->dim;
     *dt = cached_dt(key, sms, [&](int d) { return bwd_occupancy(is_bf16, s.lpc, s.spt, d, (int)a->dstate, has_z); });
     if (*dt < 1) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: no CTA shape fits shared memory");
+    *dt_pair = 0;
+    if (bwd_pair_shape(a)) {
+        // 16 channels per warp: choose_dt's channel step for "2 lanes per channel"
+        key.kind = 5; key.lpc = 2; key.spt = 8;
+        const int d = cached_dt(key, sms, [&](int dd) { return bwd_pair_occupancy(is_bf16, dd, has_z); });
+        *dt_pair = d > 0 ? d : 0;
+    }
     return SSM_OK;
 }
 
-static int bwd_common(const ssm_scan_bwd_args* a, DevInfo** di, StateSplit* sp, int* dt) {
+static int bwd_common(const ssm_scan_bwd_args* a, DevInfo** di, StateSplit* sp, int* dt, int* dt_pair) {
     int rc = device_info(di);
     if (rc) return rc;
-    return bwd_shape(a, (*di)->sms, sp, dt);
+    return bwd_shape(a, (*di)->sms, sp, dt, dt_pair);
 }
+
+static int ws_dt(int dt, int dt_pair) { return dt_pair > 0 && dt_pair < dt ? dt_pair : dt; }
 
 struct WsLayout { size_t bc, a, dd, total; };
 
@@ -433,9 +456,9 @@ size_t ssm_scan_bwd_workspace_size(const ssm_scan_bwd_args* a) {
     if (!a) return 0;
     DevInfo* di;
     StateSplit sp;
-    int dt;
-    if (bwd_common(a, &di, &sp, &dt)) return 0;
-    return ws_layout(a, dt).total;
+    int dt, dt_pair;
+    if (bwd_common(a, &di, &sp, &dt, &dt_pair)) return 0;
+    return ws_layout(a, ws_dt(dt, dt_pair)).total;
 }
 
 }  // extern "C"
@@ -446,9 +469,9 @@ namespace ssm {
 // shape error); touches no device memory.
 size_t scan_bwd_workspace_bytes(const ssm_scan_bwd_args* a, int sms) {
     StateSplit sp;
-    int dt;
-    if (!a || bwd_shape(a, sms, &sp, &dt)) return 0;
-    return ws_layout(a, dt).total;
+    int dt, dt_pair;
+    if (!a || bwd_shape(a, sms, &sp, &dt, &dt_pair)) return 0;
+    return ws_layout(a, ws_dt(dt, dt_pair)).total;
 }
 
 // The backward proper: validation, tensor maps and the two launches, with the caller's
@@ -458,8 +481,8 @@ int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, i
     if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: args is NULL");
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     StateSplit sp;
-    int dt;
-    int rc = bwd_shape(a, sms, &sp, &dt);
+    int dt, dt_pair;
+    int rc = bwd_shape(a, sms, &sp, &dt, &dt_pair);
     if (rc) return rc;
     if (!a->u || !a->delta || !a->A || !a->B || !a->C || !a->dout || !a->ckpt || !a->du ||
         !a->ddelta || !a->dA || !a->dB || !a->dC)
@@ -471,7 +494,7 @@ int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, i
                     sp.k, (int)a->ckpt_format, (long long)a->ckpt_len);
     if (a->length && !a->reference_length_semantics)
         return fail(SSM_ERR_INVALID, "ssm_scan_bwd: `length` is only supported with the reference's semantics");
-    const WsLayout w = ws_layout(a, dt);
+    const WsLayout w = ws_layout(a, ws_dt(dt, dt_pair));
     if (!workspace || ws_bytes < w.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
         return fail(SSM_ERR_WORKSPACE, "ssm_scan_bwd: workspace needs %zu bytes, 256-byte aligned", w.total);
     const int is_bf16 = a->dtype == SSM_BF16;
@@ -516,6 +539,12 @@ int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, i
                 tma_ok(a->du, a->du_dim_stride, a->du_batch_stride, es) &&
                 tma_ok(a->ddelta, a->ddelta_dim_stride, a->ddelta_batch_stride, es) &&
                 tma_ok(a->dz, a->dz_dim_stride, a->dz_batch_stride, es);
+    const bool pair = dt_pair > 0 && p.use_tma;
+    if (pair) {
+        dt = dt_pair;
+        p.dt = dt;
+        p.ntile_d = (int)((a->dim + dt - 1) / dt);
+    }
     CUtensorMap maps[10];
     memset(maps, 0, sizeof(maps));
     if (p.use_tma) {
@@ -539,7 +568,8 @@ int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, i
     }
     // the forward's failure-detection test hook (SSM_TEST_WITHHOLD_TMA), for the backward
     p.test_withhold = p.use_tma && getenv("SSM_TEST_WITHHOLD_TMA") != nullptr;
-    cudaError_t e = launch_scan_bwd(p, is_bf16, sp.lpc, sp.spt, maps, stream);
+    cudaError_t e = pair ? launch_scan_bwd_pair(p, is_bf16, maps, stream)
+                         : launch_scan_bwd(p, is_bf16, sp.lpc, sp.spt, maps, stream);
     if (e != cudaSuccess) return cuda_fail(e, "scan_bwd launch");
 
     ReduceParams r;

@@ -243,3 +243,34 @@ def test_large_config2_shape_properties(cuda):
                                    h1.contiguous())
     assert_close(torch.cat([o1, o2], -1), full, 1e-4, 1e-5, "split scan")
     assert_close(h2, hl, 1e-4, 1e-5, "split last state")
+
+
+# d_state 16 without `length` takes scan_bwd_pair_kernel (two channels per lane);
+# SSM_BWD_KERNEL=general forces scan_bwd_kernel.  Both against each other and the oracle.
+PAIR_CASES = [
+    (2, 64, 256, 16, F32, True, True),
+    (1, 40, 300, 16, F32, True, False),     # channels not a multiple of 16, ragged last tile
+    (3, 48, 136, 16, BF16, True, True),
+    (2, 96, 520, 16, BF16, False, False),
+    (1, 16, 16, 16, F32, False, True),      # one tile
+    (1, 200, 2050, 16, BF16, True, False),  # ragged: the last tile holds 2 tokens
+]
+
+
+@pytest.mark.parametrize("case", PAIR_CASES, ids=_ids)
+def test_pair_and_general_backward_kernels_agree(cuda, case, monkeypatch):
+    B, D, L, N, dt, with_z, with_h = case
+    inp = scan_inputs(B, D, L, N, dt, seed=B * 100 + L, device=cuda, with_z=with_z, with_h_init=with_h)
+    dh_last = torch.randn(B, D, N, device=cuda) if with_h else None
+    pair = _run_capi(inp, inp.z, inp.h_init, dh_last)
+    monkeypatch.setenv("SSM_BWD_KERNEL", "general")
+    general = _run_capi(inp, inp.z, inp.h_init, dh_last)
+    monkeypatch.delenv("SSM_BWD_KERNEL")
+    names = ["du", "ddelta", "dA", "dB", "dC", "dD", "ddelta_bias"] + (["dz"] if with_z else []) + (
+        ["dh_init"] if with_h else [])
+    for name in names:
+        assert_grad_close(pair[name], general[name], name + " pair vs general", rtol=1e-3)
+    fw = oracle_fwd(inp, z=inp.z, h_init=inp.h_init)
+    g = oracle_bwd(inp, fw, inp.dout, z=inp.z, h_init=inp.h_init, dh_last=dh_last)
+    for name in names:
+        assert_grad_close(pair[name], g[name], name + " pair vs oracle")
