@@ -48,8 +48,9 @@ cudaError_t launch_conv1d_reduce(const float* ws, int nparts, int dim, int width
                                  float* dbias, int sms, cudaStream_t stream);
 cudaError_t launch_conv1d_update(const ConvParams& p, int is_bf16, int width, int sms, cudaStream_t stream);
 size_t bwd_smem_bytes(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
-cudaError_t launch_scan_bwd_pair(const BwdParams& p, int is_bf16, const CUtensorMap* maps, cudaStream_t stream);
-int bwd_pair_occupancy(int is_bf16, int dt, int has_z);
+cudaError_t launch_scan_bwd_pair(const BwdParams& p, int is_bf16, int cpl, const CUtensorMap* maps,
+                                 cudaStream_t stream);
+int bwd_pair_occupancy(int is_bf16, int cpl, int dt, int has_z);
 int* noalloc_error_word();
 int fwd_occupancy(int is_bf16, int lpc, int spt, int dt, int has_z, int has_y);
 int bwd_occupancy(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
@@ -201,6 +202,21 @@ int encode3d(CUtensorMap* map, const void* ptr, int is_bf16, int64_t d0, int64_t
                           const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(SSM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return SSM_OK;
+}
+
+// 4-D float32 map of a (d3, d2, d1, d0=inner) tensor with element strides (s3, s2, s1, 1);
+// box (b0, b1, b2, 1), no swizzle.
+int encode4d_f32(CUtensorMap* map, const void* ptr, int64_t d0, int64_t d1, int64_t d2, int64_t d3, int64_t s1,
+                 int64_t s2, int64_t s3, int b0, int b1, int b2) {
+    cuuint64_t dims[4] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2, (cuuint64_t)d3};
+    cuuint64_t strides[3] = {(cuuint64_t)(s1 * 4), (cuuint64_t)(s2 * 4), (cuuint64_t)(s3 * 4)};
+    cuuint32_t box[4] = {(cuuint32_t)b0, (cuuint32_t)b1, (cuuint32_t)b2, 1u};
+    cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SSM_ERR_CUDA, "cuTensorMapEncodeTiled (4-D) failed (%d)", (int)r);
     return SSM_OK;
 }
 
@@ -387,9 +403,11 @@ int ssm_scan_ckpt_from_reference(const ssm_scan_fwd_args* a, const float* ref_ck
 }
 
 // Shape checks and CTA sizing of the backward; touches no device memory.
-// Backward kernels: scan_bwd_pair_kernel (scan_bwd_pair.cu: two channels per lane) for
-// d_state 16 without `length` when every stream is a TMA source/target, scan_bwd_kernel
-// for everything else.  SSM_BWD_KERNEL=general forces the latter (for comparisons).
+// Backward kernels: scan_bwd_pair_kernel (scan_bwd_pair.cu) for d_state 16 without `length`
+// when every stream is a TMA source/target -- with two channels per lane when the rows give
+// it at least 32 warps per SM (rows >= 512 * SMs), else one -- and scan_bwd_kernel for
+// everything else.  SSM_BWD_KERNEL=general forces the latter (for comparisons);
+// SSM_BWD_PAIR_CPL (1, 2) and SSM_BWD_PAIR_DT override the pair kernel's shape.
 static bool bwd_pair_shape(const ssm_scan_bwd_args* a) {
     const char* e = getenv("SSM_BWD_KERNEL");
     if (e && strcmp(e, "general") == 0) return false;
@@ -397,9 +415,9 @@ static bool bwd_pair_shape(const ssm_scan_bwd_args* a) {
 }
 
 // Channels per CTA of both backward kernels for these sizes: *dt for scan_bwd_kernel and
-// *dt_pair for scan_bwd_pair_kernel (0 when the shape does not take it).  The workspace
-// is sized for the smaller (more channel tiles), so it fits whichever kernel runs.
-static int bwd_shape(const ssm_scan_bwd_args* a, int sms, StateSplit* sp, int* dt, int* dt_pair) {
+// *dt_pair / *cpl for scan_bwd_pair_kernel (dt_pair 0 when the shape does not take it).
+// The workspace is sized for the smaller dt (more channel tiles), so it fits either kernel.
+static int bwd_shape(const ssm_scan_bwd_args* a, int sms, StateSplit* sp, int* dt, int* dt_pair, int* cpl) {
     if (a->batch < 1 || a->dim < 1 || a->seqlen < 1 || a->dstate < 1)
         return fail(SSM_ERR_INVALID, "ssm_scan_bwd: sizes must be positive");
     if (a->dstate > 256) return fail(SSM_ERR_INVALID, "selective_scan only supports state_dim <= 256");
@@ -419,19 +437,33 @@ static int bwd_shape(const ssm_scan_bwd_args* a, int sms, StateSplit* sp, int* d
     *dt = cached_dt(key, sms, [&](int d) { return bwd_occupancy(is_bf16, s.lpc, s.spt, d, (int)a->dstate, has_z); });
     if (*dt < 1) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: no CTA shape fits shared memory");
     *dt_pair = 0;
+    *cpl = 1;
     if (bwd_pair_shape(a)) {
-        // 16 channels per warp: choose_dt's channel step for "2 lanes per channel"
-        key.kind = 5; key.lpc = 2; key.spt = 8;
-        const int d = cached_dt(key, sms, [&](int dd) { return bwd_pair_occupancy(is_bf16, dd, has_z); });
+        // measured on B200: 20480 rows (4 x 5120): one channel per lane 1.07 ms, two 1.26 ms;
+        // 163840 rows (config 5 as 32 segments): one 13.6 ms, two 12.9 ms
+        int c = (a->batch * a->dim >= (int64_t)512 * (sms > 0 ? sms : 148)) ? 2 : 1;
+        if (const char* e = getenv("SSM_BWD_PAIR_CPL")) {
+            const int v = atoi(e);
+            if (v == 1 || v == 2) c = v;
+        }
+        // 8 channels per warp per channel a lane holds: choose_dt's channel step for
+        // 4 / c lanes per channel
+        key.kind = 5; key.lpc = 4 / c; key.spt = 8;
+        int d = cached_dt(key, sms, [&](int dd) { return bwd_pair_occupancy(is_bf16, c, dd, has_z); });
+        if (const char* e = getenv("SSM_BWD_PAIR_DT")) {
+            const int v = atoi(e);
+            if (v >= 8 * c && v * 4 / c <= 128 && v % (8 * c) == 0 && bwd_pair_occupancy(is_bf16, c, v, has_z) > 0) d = v;
+        }
         *dt_pair = d > 0 ? d : 0;
+        *cpl = c;
     }
     return SSM_OK;
 }
 
-static int bwd_common(const ssm_scan_bwd_args* a, DevInfo** di, StateSplit* sp, int* dt, int* dt_pair) {
+static int bwd_common(const ssm_scan_bwd_args* a, DevInfo** di, StateSplit* sp, int* dt, int* dt_pair, int* cpl) {
     int rc = device_info(di);
     if (rc) return rc;
-    return bwd_shape(a, (*di)->sms, sp, dt, dt_pair);
+    return bwd_shape(a, (*di)->sms, sp, dt, dt_pair, cpl);
 }
 
 static int ws_dt(int dt, int dt_pair) { return dt_pair > 0 && dt_pair < dt ? dt_pair : dt; }
@@ -456,8 +488,8 @@ size_t ssm_scan_bwd_workspace_size(const ssm_scan_bwd_args* a) {
     if (!a) return 0;
     DevInfo* di;
     StateSplit sp;
-    int dt, dt_pair;
-    if (bwd_common(a, &di, &sp, &dt, &dt_pair)) return 0;
+    int dt, dt_pair, cpl;
+    if (bwd_common(a, &di, &sp, &dt, &dt_pair, &cpl)) return 0;
     return ws_layout(a, ws_dt(dt, dt_pair)).total;
 }
 
@@ -469,8 +501,8 @@ namespace ssm {
 // shape error); touches no device memory.
 size_t scan_bwd_workspace_bytes(const ssm_scan_bwd_args* a, int sms) {
     StateSplit sp;
-    int dt, dt_pair;
-    if (!a || bwd_shape(a, sms, &sp, &dt, &dt_pair)) return 0;
+    int dt, dt_pair, cpl;
+    if (!a || bwd_shape(a, sms, &sp, &dt, &dt_pair, &cpl)) return 0;
     return ws_layout(a, ws_dt(dt, dt_pair)).total;
 }
 
@@ -481,8 +513,8 @@ int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, i
     if (!a) return fail(SSM_ERR_INVALID, "ssm_scan_bwd: args is NULL");
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     StateSplit sp;
-    int dt, dt_pair;
-    int rc = bwd_shape(a, sms, &sp, &dt, &dt_pair);
+    int dt, dt_pair, cpl;
+    int rc = bwd_shape(a, sms, &sp, &dt, &dt_pair, &cpl);
     if (rc) return rc;
     if (!a->u || !a->delta || !a->A || !a->B || !a->C || !a->dout || !a->ckpt || !a->du ||
         !a->ddelta || !a->dA || !a->dB || !a->dC)
@@ -539,17 +571,23 @@ int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, i
                 tma_ok(a->du, a->du_dim_stride, a->du_batch_stride, es) &&
                 tma_ok(a->ddelta, a->ddelta_dim_stride, a->ddelta_batch_stride, es) &&
                 tma_ok(a->dz, a->dz_dim_stride, a->dz_batch_stride, es);
-    const bool pair = dt_pair > 0 && p.use_tma;
+    const bool pair = dt_pair > 0 && p.use_tma && (reinterpret_cast<uintptr_t>(a->ckpt) & 15u) == 0;
     if (pair) {
         dt = dt_pair;
         p.dt = dt;
         p.ntile_d = (int)((a->dim + dt - 1) / dt);
     }
-    CUtensorMap maps[10];
+    CUtensorMap maps[11];
     memset(maps, 0, sizeof(maps));
     if (p.use_tma) {
         if ((rc = get_encoder())) return rc;
         const int TB = kBwdTile;
+        // the pair kernel stages each tile's two checkpoints by TMA: the compact checkpoints
+        // (batch, nck, dim, 16) as a 4-D tensor, box (16 states, dt channels, 2 checkpoints)
+        if (pair && (rc = encode4d_f32(&maps[10], a->ckpt, a->dstate, a->dim, p.nck, a->batch, a->dstate,
+                                       a->dim * a->dstate, (int64_t)p.nck * a->dim * a->dstate, (int)a->dstate,
+                                       dt, 2)))
+            return rc;
         const CUtensorMapSwizzle none = CU_TENSOR_MAP_SWIZZLE_NONE;
         // output rows are TB * element bytes: 32 (bf16) or 64 (f32) bytes
         const CUtensorMapSwizzle osw = is_bf16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
@@ -568,7 +606,7 @@ int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, i
     }
     // the forward's failure-detection test hook (SSM_TEST_WITHHOLD_TMA), for the backward
     p.test_withhold = p.use_tma && getenv("SSM_TEST_WITHHOLD_TMA") != nullptr;
-    cudaError_t e = pair ? launch_scan_bwd_pair(p, is_bf16, maps, stream)
+    cudaError_t e = pair ? launch_scan_bwd_pair(p, is_bf16, cpl, maps, stream)
                          : launch_scan_bwd(p, is_bf16, sp.lpc, sp.spt, maps, stream);
     if (e != cudaSuccess) return cuda_fail(e, "scan_bwd launch");
 

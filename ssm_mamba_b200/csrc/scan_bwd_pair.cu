@@ -1,27 +1,28 @@
-// Backward selective scan for sm_100a, two channels per lane: the path for d_state 16
-// without `length` (every benchmark config), beside the general kernel of scan_bwd.cu.
+// Backward selective scan for sm_100a: the path for d_state 16 without `length` (every
+// benchmark config), beside the general kernel of scan_bwd.cu.
 //
 // Same gradients as the reference backward (nmquan1503/ssm-mamba,
-// csrc/selective_scan/backward_kernel.cu:212-452) and as scan_bwd_kernel, with a work split
-// that halves the cross-lane traffic per (token, state, channel):
+// csrc/selective_scan/backward_kernel.cu:212-452) and as scan_bwd_kernel, organised to move
+// fewer bytes through shared memory and shuffles per (token, state, channel) element:
 //
-//  * A warp owns 16 channels x 16 states.  Lane (cw, g) -- channel lane cw = lane / 4, state
-//    lane g = lane % 4 -- holds states 4g .. 4g+3 of the TWO channels cw and cw + 8, so the
-//    per-token B and C loads serve 8 (token, state, channel) elements instead of 4, and dB
-//    / dC (sums over channels) are summed over the lane's two channels in registers before
-//    the cross-lane reduction.
-//  * dB / dC: the lane keeps its states in an XOR-rotated order (state 4g + (s ^ (cw & 3)) in
-//    register s; B and C are staged in 4 rotated copies), so the transpose-reduce over the 8
-//    channel lanes is 4 shuffle rounds with no selects; warps combine through shared
-//    memory, CTAs through a per-channel-tile workspace summed by scan_reduce_kernel in a
-//    fixed order.  No floating-point atomics.
-//  * du / ddelta (sums over states): the 16 per-lane partials of a 4-token quad (S1, S2 x 2
-//    channels x 4 tokens) are reduce-scattered over the 4 state lanes by shuffles; each lane
-//    then finishes 2 tokens of one channel (skip term, softplus derivative, dD, ddelta_bias).
-//  * Registers hold the decays and states of one quad (4 tokens) of the lane's 8 state
-//    chains.  Checkpoints are every 8 tokens: the second quad of an 8-token sub-tile is
-//    reached by recomputing the first quad without keeping it (1.5 exp2 per element, which
-//    the MUFU pipe affords; the backward is bound by instruction issue and shared memory).
+//  * A warp owns 8 * CPL channels x 16 states.  Lane (cw, g) -- channel lane cw = lane / 4,
+//    state lane g = lane % 4 -- holds states 4g .. 4g+3 of CPL channels (cw, and cw + 8 when
+//    CPL = 2).  With two channels the per-token B and C loads serve 8 elements instead of 4
+//    and dB / dC are summed over the lane's two channels in registers before the cross-lane
+//    reduction; one channel keeps twice the warps for shapes with few rows (config 2).
+//  * dB / dC (sums over channels): the lane keeps its states in an XOR-rotated order (state
+//    4g + (s ^ (cw & 3)) in register s; B and C are staged in 4 rotated copies), so the
+//    transpose-reduce over the 8 channel lanes is shuffles with no selects; warps combine
+//    through shared memory, CTAs through a per-channel-tile workspace summed by
+//    scan_reduce_kernel in a fixed order.  No floating-point atomics.
+//  * du / ddelta (sums over states): the per-lane partials (S1, S2) are reduce-scattered over
+//    the 4 state lanes by shuffles -- per token pair (CPL = 2) or per 4-token quad (CPL = 1)
+//    -- and each lane finishes one token (skip term, softplus derivative, dD, ddelta_bias).
+//  * Registers hold the decays, states and B values of one quad (4 tokens).  Checkpoints are
+//    every 8 tokens: the second quad of an 8-token sub-tile is reached by recomputing the
+//    first quad without keeping it (1.5 exp2 per element, which the MUFU pipe affords).  The
+//    two checkpoints a tile restarts from arrive by TMA with the tile (a 4-D box of the
+//    checkpoint tensor), double-buffered, so no register holds a prefetch.
 //  * Tiles of 16 tokens arrive by one TMA stage, refilled as soon as the tile prologue has
 //    consumed it; du, ddelta, dz leave by TMA stores.  Tokens past the end of the sequence
 //    are identity steps with zero inputs (the prologue zeroes their delta, delta*u, dout and
@@ -39,36 +40,38 @@ constexpr int kPairNS = 16;   // states (exactly 16)
 constexpr int kPairK = 8;     // checkpoint interval (tokens)
 }  // namespace
 
-template <typename IT>
+template <typename IT, int CPL>
 __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
     const __grid_constant__ BwdParams p, const __grid_constant__ CUtensorMap tm_u,
     const __grid_constant__ CUtensorMap tm_delta, const __grid_constant__ CUtensorMap tm_dout,
     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_y,
     const __grid_constant__ CUtensorMap tm_B, const __grid_constant__ CUtensorMap tm_C,
     const __grid_constant__ CUtensorMap tm_du, const __grid_constant__ CUtensorMap tm_ddelta,
-    const __grid_constant__ CUtensorMap tm_dz) {
+    const __grid_constant__ CUtensorMap tm_dz, const __grid_constant__ CUtensorMap tm_ck) {
     constexpr int ES = sizeof(IT);
     constexpr int TB = kBwdTile;
     constexpr int NS = kPairNS;
     constexpr int K = kPairK;
     constexpr int RS = TB + 4;
-    static_assert(TB % K == 0 && K == 8, "tiles of whole 8-token sub-tiles");
+    constexpr int CPW = 8 * CPL;                // channels per warp
+    static_assert(TB == 2 * K && K == 8, "tiles of two 8-token sub-tiles");
+    static_assert(CPL == 1 || CPL == 2, "one or two channels per lane");
 
     extern __shared__ __align__(1024) unsigned char smem[];
     if ((smem_u32(smem) & 1023u) != 0u) {
         if (threadIdx.x == 0) atomicExch(p.err, kDevErrSmemAlign);
         return;
     }
-    const int DT = p.dt;                        // channels per CTA, a multiple of 16
-    const int nthr = DT * 2;
+    const int DT = p.dt;                        // channels per CTA, a multiple of CPW
+    const int nthr = DT * 4 / CPL;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int cw = lane >> 2, g = lane & 3, rot = cw & 3;
-    const int lc0 = warp * 16 + cw;             // this lane's channels: lc0, lc0 + 8 (CTA-local)
+    const int lc0 = warp * CPW + cw;            // this lane's channels: lc0 (+ 8) (CTA-local)
     const int b = blockIdx.x / p.ntile_d, tile_d = blockIdx.x % p.ntile_d;
     const int d0 = tile_d * DT;
     const int Lq = p.seqlen, Dm = p.dim;
     const bool has_z = p.z != nullptr;
-    const BwdSmem S = bwd_smem_layout(DT, NS, NS, ES, 4, nthr / 32, has_z ? 1 : 0, 0);
+    const BwdPairSmem S = bwd_pair_smem_layout(DT, nthr / 32, ES, has_z ? 1 : 0);
     float* sD = reinterpret_cast<float*>(smem + S.sD);
     float* sDU = reinterpret_cast<float*>(smem + S.sDU);
     float* sG = reinterpret_cast<float*>(smem + S.sG);
@@ -81,16 +84,16 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S.bar);
 
     // ---- per-lane constants: 2 channels x 2 pairs of states, in the rotated order ----------
-    int dch[2];
-    bool dv[2];
+    int dch[CPL];
+    bool dv[CPL];
 #pragma unroll
-    for (int c = 0; c < 2; c++) {
+    for (int c = 0; c < CPL; c++) {
         dch[c] = d0 + lc0 + 8 * c;
         dv[c] = dch[c] < Dm;
     }
-    float2 A2[2][2], Gp[2][2], anp[2][2], dAp[2][2];
+    float2 A2[CPL][2], Gp[CPL][2], anp[CPL][2], dAp[CPL][2];
 #pragma unroll
-    for (int c = 0; c < 2; c++) {
+    for (int c = 0; c < CPL; c++) {
 #pragma unroll
         for (int s = 0; s < 4; s++) {
             const int n = 4 * g + (s ^ rot);
@@ -105,39 +108,26 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
             dAp[c][q] = make_float2(0.f, 0.f);
         }
     }
-    // the finishing role of this lane in every quad: channel fc, token pair fp
-    const int fc = g & 1, fp = g >> 1;
-    const int my_lc = lc0 + 8 * fc;
-    const int fin_d = fc ? dch[1] : dch[0];
-    const bool fin_ok = fc ? dv[1] : dv[0];
+    // the finishing role of this lane: with 2 channels, token fo of every token pair of
+    // channel lc0 + 8 * fc; with 1 channel, token g of every quad
+    const int fc = CPL == 2 ? g >> 1 : 0, fo = CPL == 2 ? (g & 1) : g;
+    const int fin_lc = lc0 + 8 * fc;
+    const int fin_d = fc ? dch[CPL - 1] : dch[0];
+    const bool fin_ok = fc ? dv[CPL - 1] : dv[0];
     const float Dd = (fin_ok && p.D) ? p.D[fin_d] : 0.f;
     float dD_acc = 0.f, db_acc = 0.f;
     for (int i = tid; i < DT; i += nthr) sBias[i] = (d0 + i < Dm && p.delta_bias) ? p.delta_bias[d0 + i] : 0.f;
-
-    // checkpoints: (batch, nck, dim, 16) float32; checkpoint j is the state after token
-    // K*(j+1) - 1; the sub-tile starting at token ts restarts from checkpoint ts/K - 1
-    // (h_init, or zero, for ts = 0)
-    const int64_t ck_stride = (int64_t)Dm * NS;
-    auto load_ckpt = [&](int ts, float2 (&hv)[2][2]) {
-#pragma unroll
-        for (int c = 0; c < 2; c++) {
-            const int dd = dv[c] ? dch[c] : 0;
-            const float* row = ts == 0 ? (p.h_init ? p.h_init + ((int64_t)b * Dm + dd) * NS : nullptr)
-                                       : p.ckpt + ((int64_t)b * p.nck * Dm + dd) * NS + (int64_t)(ts / K - 1) * ck_stride;
-#pragma unroll
-            for (int s = 0; s < 4; s++) {
-                const float v = (row != nullptr && dv[c]) ? row[4 * g + (s ^ rot)] : 0.f;
-                if (s & 1) hv[c][s / 2].y = v; else hv[c][s / 2].x = v;
-            }
-        }
-    };
 
     const int ntiles = (Lq + TB - 1) / TB;
     float* const ws_bc_row = p.ws_bc + (((int64_t)tile_d * p.batch + b) * 2) * NS * (int64_t)Lq;
     const uint32_t tile_bytes = (uint32_t)DT * TB * ES;
     const uint32_t bc_bytes = (uint32_t)NS * TB * ES;
-    const uint32_t stage_bytes = (has_z ? 5u : 3u) * tile_bytes + 2u * bc_bytes;
+    const uint32_t ck_bytes = 2u * (uint32_t)DT * NS * 4u;
+    const uint32_t stage_bytes = (has_z ? 5u : 3u) * tile_bytes + 2u * bc_bytes + ck_bytes;
 
+    // tile `tile`: its raw tiles, and the checkpoints its two sub-tiles restart from (the
+    // states after tokens t0 - 1 and t0 + 7: checkpoints t0/8 - 1 and t0/8; index -1, before
+    // the sequence, reads as zeros) into checkpoint buffer tile % 2
     auto issue = [&](int tile) {
         const int t0 = tile * TB;
         mbar_arrive_expect_tx(bar, stage_bytes);
@@ -150,6 +140,7 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
         }
         tma_load_3d(smem + S.B, &tm_B, bar, t0, 0, b);
         tma_load_3d(smem + S.C, &tm_C, bar, t0, 0, b);
+        tma_load_4d(smem + ((tile & 1) ? S.ck[1] : S.ck[0]), &tm_ck, bar, 0, d0, tile * 2 - 1, b);
     };
     // byte offset of (channel row, token) in a swizzled output tile
     auto out_off = [](int row, int t) -> uint32_t { return ES == 2 ? swz32(row, t * ES) : swz64(row, t * ES); };
@@ -160,9 +151,6 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
     }
     __syncthreads();
     if (tid == 0 && !p.test_withhold) issue(ntiles - 1);
-
-    float2 h0[2][2], h0n[2][2];
-    load_ckpt(((Lq - 1) / K) * K, h0);
 
     for (int it = ntiles - 1; it >= 0; it--) {
         const int t0 = it * TB;
@@ -248,27 +236,26 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
         float* const rot_dst = wslot + (4 * g + cw) * (TB + 1);   // lanes cw < 4: state 4g + cw
         const float* const sBr = sB + rot * (int)S.rot_stride;
         const float* const sCr = sC + rot * (int)S.rot_stride;
-        const float* const rowD[2] = {sD + lc0 * RS, sD + (lc0 + 8) * RS};
-        const float* const rowDU[2] = {sDU + lc0 * RS, sDU + (lc0 + 8) * RS};
-        const float* const rowG[2] = {sG + lc0 * RS, sG + (lc0 + 8) * RS};
+        const float* const ckb = reinterpret_cast<const float*>(smem + ((it & 1) ? S.ck[1] : S.ck[0]));
 
-        // the states of 4 tokens starting at tile token tq, from hs (the state before tq)
-        // into av / hv, or only to the state after them (KEEP = false)
-        auto recompute = [&](int tq, const float2 (&hs)[2][2], float2 (&av)[4][2][2], float2 (&hv)[4][2][2],
-                             auto keep_tag) {
-            constexpr bool KEEP = decltype(keep_tag)::value;
-            float4 dl4[2], du4[2];
+        // one quad of 4 tokens (tile tokens tq .. tq+3) from hs, the state before it:
+        // recompute (decays and states into registers), reverse recurrence, dB/dC into the
+        // warp slots, and per token pair the sums over states and du / ddelta of one token
+        auto quad = [&](int tq, const float2 (&hs)[CPL][2]) {
+            float4 dl4[CPL], du4[CPL], dg4[CPL];
 #pragma unroll
-            for (int c = 0; c < 2; c++) {
-                dl4[c] = lds128(rowD[c] + tq);
-                du4[c] = lds128(rowDU[c] + tq);
+            for (int c = 0; c < CPL; c++) {
+                const int lc = lc0 + 8 * c;
+                dl4[c] = lds128(sD + lc * RS + tq);
+                du4[c] = lds128(sDU + lc * RS + tq);
+                dg4[c] = lds128(sG + lc * RS + tq);
             }
+            float2 av[4][CPL][2], hv[4][CPL][2], bq[4][2];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                float2 bp[2];
-                load_state_pairs<4, NS>(sBr, tq + j, g, j, bp);   // tq % 4 == 0: swizzle term j
+                load_state_pairs<4, NS>(sBr, tq + j, g, j, bq[j]);   // tq % 4 == 0: swizzle term j
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
+                for (int c = 0; c < CPL; c++) {
                     const float dl = j == 0 ? dl4[c].x : j == 1 ? dl4[c].y : j == 2 ? dl4[c].z : dl4[c].w;
                     const float du = j == 0 ? du4[c].x : j == 1 ? du4[c].y : j == 2 ? du4[c].z : du4[c].w;
                     const float2 dl2 = make_float2(dl, dl), du2 = make_float2(du, du);
@@ -276,37 +263,23 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
                     for (int q = 0; q < 2; q++) {
                         const float2 x = __fmul2_rn(dl2, A2[c][q]);
                         const float2 a = make_float2(ex2(x.x), ex2(x.y));
-                        const float2 prev = j == 0 ? hs[c][q] : hv[KEEP ? j - 1 : 0][c][q];
-                        const float2 h = __ffma2_rn(a, prev, __fmul2_rn(du2, bp[q]));
-                        if (KEEP) { av[j][c][q] = a; hv[j][c][q] = h; }
-                        else hv[0][c][q] = h;
+                        const float2 prev = j == 0 ? hs[c][q] : hv[j - 1][c][q];
+                        av[j][c][q] = a;
+                        hv[j][c][q] = __ffma2_rn(a, prev, __fmul2_rn(du2, bq[j][q]));
                     }
                 }
             }
-        };
-
-        // one quad of 4 tokens (tile tokens tq .. tq+3) given the state before it: recompute,
-        // reverse recurrence, dB/dC into the warp slots, du/ddelta for 2 tokens of 1 channel
-        auto quad = [&](int tq, const float2 (&hs)[2][2]) {
-            float2 av[4][2][2], hv[4][2][2];
-            recompute(tq, hs, av, hv, std::true_type{});
-            float4 dl4[2], du4[2], dg4[2];
-#pragma unroll
-            for (int c = 0; c < 2; c++) {
-                dl4[c] = lds128(rowD[c] + tq);
-                du4[c] = lds128(rowDU[c] + tq);
-                dg4[c] = lds128(rowG[c] + tq);
-            }
-            float v[16];   // (S1, S2) partials: block 2 * (token pair) + channel, [S1, S2] x [even, odd]
+            // (S1, S2) partials: 2 channels -> of a token pair, [channel][even, odd][S1, S2];
+            // 1 channel -> of the quad, [token][S1, S2]
+            float v[8];
 #pragma unroll
             for (int j = 3; j >= 0; j--) {
                 const int t = tq + j;
-                float2 bp[2], cp[2];
-                load_state_pairs<4, NS>(sBr, t, g, j, bp);
+                float2 cp[2];
                 load_state_pairs<4, NS>(sCr, t, g, j, cp);
                 float2 dbp[2], dcp[2];
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
+                for (int c = 0; c < CPL; c++) {
                     const float dl = j == 0 ? dl4[c].x : j == 1 ? dl4[c].y : j == 2 ? dl4[c].z : dl4[c].w;
                     const float du = j == 0 ? du4[c].x : j == 1 ? du4[c].y : j == 2 ? du4[c].z : du4[c].w;
                     const float dg = j == 0 ? dg4[c].x : j == 1 ? dg4[c].y : j == 2 ? dg4[c].z : dg4[c].w;
@@ -319,7 +292,7 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
                         anp[c][q] = av[j][c][q];
                         const float2 prev = j == 0 ? hs[c][q] : hv[j - 1][c][q];
                         const float2 w = __fmul2_rn(Gs, __fmul2_rn(av[j][c][q], prev));
-                        s12 = __ffma2_rn(Gs, bp[q], s12);
+                        s12 = __ffma2_rn(Gs, bq[j][q], s12);
                         s22 = __ffma2_rn(A2[c][q], w, s22);
                         dAp[c][q] = __ffma2_rn(dl2, w, dAp[c][q]);
                         if (c == 0) {
@@ -330,66 +303,100 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
                             dcp[q] = __ffma2_rn(dg2, hv[j][c][q], dcp[q]);
                         }
                     }
-                    const int vi = 4 * (2 * (j >> 1) + c) + 2 * (j & 1);
+                    const int vi = CPL == 2 ? 4 * c + 2 * (j & 1) : 2 * j;
                     v[vi] = s12.x + s12.y;
                     v[vi + 1] = s22.x + s22.y;
                 }
-                // dB, dC of this token summed over the warp's 16 channels: lane (cw, g) sums
+                // dB, dC of this token summed over the warp's channels: lane (cw, g) sums
                 // state 4g + (cw & 3), which channel lane cw ^ i holds in its register i
                 float2 r2 = make_float2(dbp[0].x, dcp[0].x);
-                r2 = __fadd2_rn(r2, make_float2(__shfl_xor_sync(0xffffffffu, dbp[0].y, 4),
-                                                __shfl_xor_sync(0xffffffffu, dcp[0].y, 4)));
-                r2 = __fadd2_rn(r2, make_float2(__shfl_xor_sync(0xffffffffu, dbp[1].x, 8),
-                                                __shfl_xor_sync(0xffffffffu, dcp[1].x, 8)));
-                r2 = __fadd2_rn(r2, make_float2(__shfl_xor_sync(0xffffffffu, dbp[1].y, 12),
-                                                __shfl_xor_sync(0xffffffffu, dcp[1].y, 12)));
+                const float2 x1 = make_float2(__shfl_xor_sync(0xffffffffu, dbp[0].y, 4),
+                                              __shfl_xor_sync(0xffffffffu, dcp[0].y, 4));
+                const float2 x2 = make_float2(__shfl_xor_sync(0xffffffffu, dbp[1].x, 8),
+                                              __shfl_xor_sync(0xffffffffu, dcp[1].x, 8));
+                const float2 x3 = make_float2(__shfl_xor_sync(0xffffffffu, dbp[1].y, 12),
+                                              __shfl_xor_sync(0xffffffffu, dcp[1].y, 12));
+                r2 = __fadd2_rn(__fadd2_rn(r2, x1), __fadd2_rn(x2, x3));
                 r2 = __fadd2_rn(r2, make_float2(__shfl_xor_sync(0xffffffffu, r2.x, 16),
                                                 __shfl_xor_sync(0xffffffffu, r2.y, 16)));
                 if (cw < 4) {
                     rot_dst[t] = r2.x;
                     rot_dst[NS * (TB + 1) + t] = r2.y;
                 }
+                if (CPL == 2 ? (j & 1) == 0 : j == 0) {
+                    // sums over the 4 state lanes: lane g keeps block g -- with 2 channels
+                    // (channel g / 2, odd token if g % 2) of this token pair, with 1 channel
+                    // token g of the quad -- then finishes that token
+                    reduce_scatter_contig<4, 8>(v, g);
+                    const int tf = t + fo;
+                    const float dlf = sD[fin_lc * RS + tf], dgf = sG[fin_lc * RS + tf];
+                    const float uf = sU[fin_lc * RS + tf], spf = sSP[fin_lc * RS + tf];
+                    const float duo = fmaf(Dd, dgf, dlf * v[0]);
+                    const float ddo = fmaf(uf, v[0], kLn2 * v[1]) * spf;   // v[1]: sum of A*log2(e)*w
+                    dD_acc = fmaf(dgf, uf, dD_acc);
+                    db_acc += ddo;
+                    *reinterpret_cast<IT*>(odu + out_off(fin_lc, tf)) = from_f<IT>(duo);
+                    *reinterpret_cast<IT*>(odd + out_off(fin_lc, tf)) = from_f<IT>(ddo);
+                }
             }
-            // sums over the 4 state lanes: lane g keeps block g = (token pair g / 2, channel g % 2)
-            reduce_scatter_contig<4, 16>(v, g);
-            const int t = tq + 2 * fp;
-            const float2 dl = *reinterpret_cast<const float2*>(sD + my_lc * RS + t);
-            const float2 dg = *reinterpret_cast<const float2*>(sG + my_lc * RS + t);
-            const float2 uv = *reinterpret_cast<const float2*>(sU + my_lc * RS + t);
-            const float2 sp = *reinterpret_cast<const float2*>(sSP + my_lc * RS + t);
-            float2 du, ddl;
-            du.x = fmaf(Dd, dg.x, dl.x * v[0]);
-            du.y = fmaf(Dd, dg.y, dl.y * v[2]);
-            ddl.x = fmaf(uv.x, v[0], kLn2 * v[1]) * sp.x;   // v[1], v[3] are sums of A*log2(e)*w
-            ddl.y = fmaf(uv.y, v[2], kLn2 * v[3]) * sp.y;
-            dD_acc = fmaf(dg.x, uv.x, fmaf(dg.y, uv.y, dD_acc));
-            db_acc += ddl.x + ddl.y;
-            store_pair<IT>(odu + out_off(my_lc, t), du);
-            store_pair<IT>(odd + out_off(my_lc, t), ddl);
         };
 
-        // ---- 8-token sub-tiles, last to first --------------------------------------------------
-#pragma unroll 1
+        // ---- 8-token sub-tiles, last to first (unrolled: every shared-memory offset of a
+        // token is then a compile-time constant) ------------------------------------------------
+#pragma unroll
         for (int sub = TB / K - 1; sub >= 0; sub--) {
             const int tl0 = sub * K;
             const int ts = t0 + tl0;
             if (ts >= Lq) continue;   // past the end of the sequence: nothing to do
-            if (ts > 0) load_ckpt(ts - K, h0n);   // the next sub-tile's checkpoint, one step earlier
-            {
-                float2 hmid[4][2][2], unused[4][2][2];
-                recompute(tl0, h0, unused, hmid, std::false_type{});
-                float2 hm[2][2];
+            // the state before the sub-tile: its checkpoint (staged with the tile), or h_init
+            float2 h0[CPL][2];
+            const float* ck = ckb + sub * DT * NS;
 #pragma unroll
-                for (int c = 0; c < 2; c++)
+            for (int c = 0; c < CPL; c++) {
+                const float* row = ck + (lc0 + 8 * c) * NS;
+                const bool from_init = ts == 0 && p.h_init != nullptr;
+                const float* src = from_init ? p.h_init + ((int64_t)b * Dm + (dv[c] ? dch[c] : 0)) * NS : row;
 #pragma unroll
-                    for (int q = 0; q < 2; q++) hm[c][q] = hmid[0][c][q];
-                quad(tl0 + 4, hm);
+                for (int s = 0; s < 4; s++) {
+                    const float v = (!from_init || dv[c]) ? src[4 * g + (s ^ rot)] : 0.f;
+                    if (s & 1) h0[c][s / 2].y = v; else h0[c][s / 2].x = v;
+                }
             }
+            // the state before the second quad: run the first quad's 4 tokens without keeping them
+            float2 hm[CPL][2];
+            {
+                float4 dlA[CPL], duA[CPL];
+#pragma unroll
+                for (int c = 0; c < CPL; c++) {
+                    dlA[c] = lds128(sD + (lc0 + 8 * c) * RS + tl0);
+                    duA[c] = lds128(sDU + (lc0 + 8 * c) * RS + tl0);
+#pragma unroll
+                    for (int q = 0; q < 2; q++) hm[c][q] = h0[c][q];
+                }
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    float2 bp[2];
+                    load_state_pairs<4, NS>(sBr, tl0 + j, g, j, bp);
+#pragma unroll
+                    for (int c = 0; c < CPL; c++) {
+                        const float dl = j == 0 ? dlA[c].x : j == 1 ? dlA[c].y : j == 2 ? dlA[c].z : dlA[c].w;
+                        const float du = j == 0 ? duA[c].x : j == 1 ? duA[c].y : j == 2 ? duA[c].z : duA[c].w;
+                        const float2 dl2 = make_float2(dl, dl), du2 = make_float2(du, du);
+#pragma unroll
+                        for (int q = 0; q < 2; q++) {
+                            const float2 x = __fmul2_rn(dl2, A2[c][q]);
+                            const float2 a = make_float2(ex2(x.x), ex2(x.y));
+                            hm[c][q] = __ffma2_rn(a, hm[c][q], __fmul2_rn(du2, bp[q]));
+                        }
+                    }
+                }
+            }
+            quad(tl0 + 4, hm);
             quad(tl0, h0);
             // gradient of the initial state: decay of token 0 times dh_0
             if (ts == 0 && p.dh_init != nullptr) {
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
+                for (int c = 0; c < CPL; c++) {
                     if (!dv[c]) continue;
 #pragma unroll
                     for (int s = 0; s < 4; s++) {
@@ -397,12 +404,6 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
                         p.dh_init[((int64_t)b * Dm + dch[c]) * NS + 4 * g + (s ^ rot)] = val;
                     }
                 }
-            }
-            if (ts > 0) {
-#pragma unroll
-                for (int c = 0; c < 2; c++)
-#pragma unroll
-                    for (int q = 0; q < 2; q++) h0[c][q] = h0n[c][q];
             }
         }
         __syncthreads();
@@ -437,7 +438,7 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
 
     // ---- per-(batch, channel) partials of dA, dD, ddelta_bias --------------------------------
 #pragma unroll
-    for (int c = 0; c < 2; c++) {
+    for (int c = 0; c < CPL; c++) {
         if (!dv[c]) continue;
 #pragma unroll
         for (int s = 0; s < 4; s++) {
@@ -445,10 +446,14 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
             p.ws_a[((int64_t)b * Dm + dch[c]) * NS + 4 * g + (s ^ rot)] = val;
         }
     }
-    // lanes g and g ^ 2 finished the same channel
-    dD_acc += __shfl_xor_sync(0xffffffffu, dD_acc, 2);
-    db_acc += __shfl_xor_sync(0xffffffffu, db_acc, 2);
-    if (g < 2 && fin_ok) {
+    // the lanes that finished tokens of the same channel: g and g ^ 1 (2 channels), all 4 (1)
+    dD_acc += __shfl_xor_sync(0xffffffffu, dD_acc, 1);
+    db_acc += __shfl_xor_sync(0xffffffffu, db_acc, 1);
+    if (CPL == 1) {
+        dD_acc += __shfl_xor_sync(0xffffffffu, dD_acc, 2);
+        db_acc += __shfl_xor_sync(0xffffffffu, db_acc, 2);
+    }
+    if (fo == 0 && fin_ok) {
         p.ws_dd[((int64_t)b * Dm + fin_d) * 2 + 0] = dD_acc;
         p.ws_dd[((int64_t)b * Dm + fin_d) * 2 + 1] = db_acc;
     }
@@ -458,31 +463,39 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
 // ---------------------------------------------------------------------------------------
 // launch
 // ---------------------------------------------------------------------------------------
-size_t bwd_pair_smem_bytes(int is_bf16, int dt, int has_z) {
-    return bwd_smem_layout(dt, kPairNS, kPairNS, is_bf16 ? 2 : 4, 4, dt / 16, has_z, 0).total;
+size_t bwd_pair_smem_bytes(int is_bf16, int cpl, int dt, int has_z) {
+    return bwd_pair_smem_layout(dt, dt * 4 / cpl / 32, is_bf16 ? 2 : 4, has_z).total;
 }
 
-int bwd_pair_occupancy(int is_bf16, int dt, int has_z) {
-    const void* k = is_bf16 ? (const void*)scan_bwd_pair_kernel<__nv_bfloat16> : (const void*)scan_bwd_pair_kernel<float>;
-    const size_t smem = bwd_pair_smem_bytes(is_bf16, dt, has_z);
+template <typename IT, int CPL>
+static const void* pair_kernel() { return (const void*)scan_bwd_pair_kernel<IT, CPL>; }
+
+int bwd_pair_occupancy(int is_bf16, int cpl, int dt, int has_z) {
+    const void* k = cpl == 2 ? (is_bf16 ? pair_kernel<__nv_bfloat16, 2>() : pair_kernel<float, 2>())
+                             : (is_bf16 ? pair_kernel<__nv_bfloat16, 1>() : pair_kernel<float, 1>());
+    const size_t smem = bwd_pair_smem_bytes(is_bf16, cpl, dt, has_z);
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, dt * 2, smem) != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, dt * 4 / cpl, smem) != cudaSuccess) return 0;
     return n;
 }
 
-cudaError_t launch_scan_bwd_pair(const BwdParams& p, int is_bf16, const CUtensorMap* maps, cudaStream_t stream) {
-    if (p.dstate != kPairNS || p.dt % 16 != 0 || p.dt < 16 || p.dt > 64 || !p.use_tma || p.length)
+cudaError_t launch_scan_bwd_pair(const BwdParams& p, int is_bf16, int cpl, const CUtensorMap* maps,
+                                 cudaStream_t stream) {
+    if (p.dstate != kPairNS || (cpl != 1 && cpl != 2) || p.dt % (8 * cpl) != 0 || p.dt < 8 * cpl ||
+        p.dt * 4 / cpl > 128 || !p.use_tma || p.length)
         return cudaErrorInvalidValue;
-    const size_t smem = bwd_pair_smem_bytes(is_bf16, p.dt, p.z != nullptr);
+    const size_t smem = bwd_pair_smem_bytes(is_bf16, cpl, p.dt, p.z != nullptr);
     auto run = [&](auto kern) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        kern<<<p.batch * p.ntile_d, p.dt * 2, smem, stream>>>(p, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5],
-                                                            maps[6], maps[7], maps[8], maps[9]);
+        kern<<<p.batch * p.ntile_d, p.dt * 4 / cpl, smem, stream>>>(p, maps[0], maps[1], maps[2], maps[3], maps[4],
+                                                                   maps[5], maps[6], maps[7], maps[8], maps[9],
+                                                                   maps[10]);
         return cudaGetLastError();
     };
-    return is_bf16 ? run(scan_bwd_pair_kernel<__nv_bfloat16>) : run(scan_bwd_pair_kernel<float>);
+    if (cpl == 2) return is_bf16 ? run(scan_bwd_pair_kernel<__nv_bfloat16, 2>) : run(scan_bwd_pair_kernel<float, 2>);
+    return is_bf16 ? run(scan_bwd_pair_kernel<__nv_bfloat16, 1>) : run(scan_bwd_pair_kernel<float, 1>);
 }
 
 }  // namespace ssm

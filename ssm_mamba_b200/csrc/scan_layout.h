@@ -128,4 +128,57 @@ __host__ __device__ inline BwdSmem bwd_smem_layout(int dt, int ns, int n, int es
     return L;
 }
 
+// ---- backward, two channels per lane (scan_bwd_pair.cu): one raw stage of 16-token tiles,
+// f32 work rows, 4 rotated B/C copies, and the tile's two state checkpoints, double-buffered
+// (the checkpoints of tile i-1 arrive with its raw tiles while tile i still reads its own) ---
+struct BwdPairSmem {
+    uint32_t du, ddelta, dz;                          // output tiles (TMA store, swizzled)
+    uint32_t u, delta, dout, z, y, B, C;              // raw tiles (TMA load, dense rows)
+    uint32_t sD, sDU, sG, sSP, sU;                    // f32 [dt][TB+4]
+    uint32_t sB, sC;                                  // f32 [4][TB*16 + 16]
+    uint32_t slots;                                   // f32 [nwarps][2][16][TB+1]
+    uint32_t ck[2];                                   // f32 [2 checkpoints][dt][16], two buffers
+    uint32_t bias, bar, total;
+    uint32_t rot_stride, slot_stride;
+};
+
+__host__ __device__ inline BwdPairSmem bwd_pair_smem_layout(int dt, int nwarps, int es, int has_z) {
+    BwdPairSmem L;
+    const int TB = kBwdTile, NS = 16;
+    const uint32_t row = (uint32_t)TB * es;
+    const uint32_t otile = align_up((uint32_t)dt * row, 512u);
+    const uint32_t tile = align_up((uint32_t)dt * row, 128u);
+    const uint32_t bc = align_up((uint32_t)NS * row, 128u);
+    uint32_t o = 0;
+    L.du = o; o += otile;
+    L.ddelta = o; o += otile;
+    L.dz = o; o += has_z ? otile : 0u;
+    L.u = o; o += tile;
+    L.delta = o; o += tile;
+    L.dout = o; o += tile;
+    L.z = o; o += has_z ? tile : 0u;
+    L.y = o; o += has_z ? tile : 0u;
+    L.B = o; o += bc;
+    L.C = o; o += bc;
+    const uint32_t rows = align_up((uint32_t)dt * (TB + 4) * 4u, 128u);
+    L.sD = o; o += rows;
+    L.sDU = o; o += rows;
+    L.sG = o; o += rows;
+    L.sSP = o; o += rows;
+    L.sU = o; o += rows;
+    L.rot_stride = (uint32_t)TB * NS + 16u;
+    L.sB = o; o += align_up(4u * L.rot_stride * 4u, 128u);
+    L.sC = o; o += align_up(4u * L.rot_stride * 4u, 128u);
+    L.slot_stride = 2u * NS * (TB + 1);
+    L.slots = o; o += align_up((uint32_t)nwarps * L.slot_stride * 4u, 128u);
+    for (int i = 0; i < 2; i++) {
+        L.ck[i] = o;
+        o += align_up(2u * (uint32_t)dt * NS * 4u, 128u);
+    }
+    L.bias = o; o += align_up((uint32_t)dt * 4u, 16u);
+    L.bar = align_up(o, 8u); o = L.bar + 8u;
+    L.total = o;
+    return L;
+}
+
 }  // namespace ssm
