@@ -383,11 +383,26 @@ def run_long_seq(args, world, rank, local, pg, peak):
     torch.cuda.synchronize()
     barrier(pg)
     ms = max_over_ranks(e0.elapsed_time(e1), pg) / steps
+    # per-phase breakdown of one more (untimed) step: CUDA events between the phases of the
+    # sliced scan, each phase the max over ranks
+    from ssm_mamba_b200.slices import PhaseTimer, set_phase_timer
+    timer = PhaseTimer()
+    set_phase_timer(timer)
+    step()
+    torch.cuda.synchronize()
+    set_phase_timer(None)
+    ph = timer.durations_ms()
+    phases = {k: max_over_ranks(ph.get(k, 0.0), pg) for k in sorted(ph)}
+    barrier(pg)
     fb, bb = scan_bytes(1, Dm, Ltot, N)
     tbs = (fb + bb) / (ms / 1e3) / 1e12
     return {"metric": "long-sequence scan fwd+bwd achieved HBM TB/s", "value": tbs, "unit": "TB/s",
             "ms_per_step": ms, "steps": steps, "scaling": "strong", "segments_per_rank": S,
             "seqpar_parity": parity,
+            "phase_ms": phases,
+            "phase_what": "one extra step, CUDA events between phases, max over ranks: agree (shape agreement "
+                          "all_gather + liveness), chunk_state (the chunk-state pass), exchange (carry all_gather), "
+                          "compose (carry folding), scan (the per-segment scan), param_allreduce (dA/dD/ddelta_bias)",
             "elem_state_per_s": 1 * Dm * Ltot * N / (ms / 1e3),
             "frac_of_hbm_peak": tbs * 1e3 / world / peak,
             "gpu_launches_per_step": 8,

@@ -81,6 +81,44 @@ def segment_view(t: Optional[torch.Tensor], s: int) -> Optional[torch.Tensor]:
     return t.as_strided((s, x, L // s), (L // s, t.stride(1), 1), t.storage_offset())
 
 
+class PhaseTimer:
+    """Optional CUDA-event markers between the phases of SlicedScanFn (chunk states, carry
+    exchange, compose, the per-slice scans, the parameter-gradient all_reduce), for a
+    per-phase breakdown of a step.  Install one with set_phase_timer(); with none installed
+    (the default) the orchestration records nothing."""
+
+    def __init__(self):
+        self.marks = []
+
+    def mark(self, name: str) -> None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.marks.append((name, ev))
+
+    def durations_ms(self):
+        """{phase: ms} from consecutive marks (call after a synchronize); the duration of a
+        mark is the time from it to the next one."""
+        out = {}
+        for (name, ev), (_, nxt) in zip(self.marks, self.marks[1:]):
+            if name.startswith("end"):
+                continue
+            out[name] = out.get(name, 0.0) + ev.elapsed_time(nxt)
+        return out
+
+
+_PHASES: Optional[PhaseTimer] = None
+
+
+def set_phase_timer(timer: Optional[PhaseTimer]) -> None:
+    global _PHASES
+    _PHASES = timer
+
+
+def _mark(name: str) -> None:
+    if _PHASES is not None:
+        _PHASES.mark(name)
+
+
 class SliceGroup:
     """The ranks that share one sequence (rank r holds the r-th contiguous slice), or a
     single process (world 1, no communication).
@@ -188,6 +226,7 @@ class SlicedScanFn(torch.autograd.Function):
         N = A.shape[1]
         if S > 1 and (Bt != 1 or L % S != 0):
             raise ValueError("segmented scan needs batch 1 and seqlen divisible by the segment count")
+        _mark("fwd_agree")
         group.check_peers("forward")
         # a peer with other shapes or options would exchange carries of another size: refuse
         group.check_agreement("batch, dim, dstate, segments, z, D, delta_bias, h_init, softplus, dtype",
@@ -199,11 +238,14 @@ class SlicedScanFn(torch.autograd.Function):
         u_s, d_s, B_s, C_s, z_s = sv(u), sv(delta), sv(B), sv(C), sv(z)
 
         # 1. every local slice from a zero start: end state and delta sum
+        _mark("fwd_chunk_state")
         h0, dsum = k.chunk_state_fwd(u_s, d_s, A, B_s, delta_bias, bool(delta_softplus))
         per = Bc * Dm * N
         pack = torch.cat([h0.reshape(S, per), dsum.reshape(S, Bc * Dm)], dim=1)   # (S, per + Bc*Dm)
         # 2. carries of every slice of the sequence, in order
+        _mark("fwd_exchange")
         allp = group.all_gather(pack).reshape(group.world * S, per + Bc * Dm)
+        _mark("fwd_compose")
         M = group.world * S
         carry = allp[:, :per].unflatten(1, (Bc, Dm, N))     # slice stride per + Bc*Dm
         dsum_all = allp[:, per:].unflatten(1, (Bc, Dm))
@@ -214,6 +256,7 @@ class SlicedScanFn(torch.autograd.Function):
         h_final = carries[M].reshape(Bc, Dm, N)
         # 3. the ordinary forward of every slice from its own initial state
         need_grad = any(ctx.needs_input_grad[:9])
+        _mark("fwd_scan")
         out = torch.empty_like(u)
         y = torch.empty_like(u) if (need_grad and z is not None) else None
         _, _, ckpt, _ = k.scan_fwd_out(u_s, d_s, A, B_s, C_s, D, z_s, delta_bias, h_in, None, True,
@@ -221,6 +264,7 @@ class SlicedScanFn(torch.autograd.Function):
         if need_grad:
             ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, y, ckpt, h_in, dsum_all, h_init)
             ctx.cfg = (bool(delta_softplus), S, group, k, Bc, rows)
+        _mark("end_fwd")
         return out, h_final
 
     @staticmethod
@@ -233,14 +277,18 @@ class SlicedScanFn(torch.autograd.Function):
         sv = lambda t: segment_view(t, S)  # noqa: E731
         dout = dout.contiguous()
         u_s, d_s, B_s, C_s, z_s, dout_s = sv(u), sv(delta), sv(B), sv(C), sv(z), sv(dout)
+        _mark("bwd_agree")
         group.check_peers("backward")
         # 1. every local slice's gradient into the state before it, from a zero start
+        _mark("bwd_chunk_state")
         g0 = k.chunk_state_bwd(d_s, A, C_s, z_s, delta_bias, softplus, dout_s)     # (rows, Dm, N)
         per = Bc * Dm * N
         if dh_final is None:
             dh_final = torch.zeros(Bc, Dm, N, device=u.device, dtype=g0.dtype)
         pack = torch.cat([g0.reshape(S * per), dh_final.reshape(per).to(g0.dtype)])
+        _mark("bwd_exchange")
         allp = group.all_gather(pack)                                                # (world, (S + 1) * per)
+        _mark("bwd_compose")
         g_all = allp[:, :S * per].reshape(M, Bc, Dm, N)
         dhf_all = allp[:, S * per:].reshape(group.world, Bc, Dm, N)
         # 2. the gradient leaving every slice's end
@@ -248,6 +296,7 @@ class SlicedScanFn(torch.autograd.Function):
         r = group.rank
         dh_last = gout[r * S:(r + 1) * S].reshape(rows, Dm, N)
         # 3. the ordinary backward of every slice
+        _mark("bwd_scan")
         du, ddelta = torch.empty_like(u), torch.empty_like(u)
         dB, dC = torch.empty_like(B), torch.empty_like(C)
         dz = torch.empty_like(u) if z is not None else None
@@ -255,6 +304,7 @@ class SlicedScanFn(torch.autograd.Function):
                              ckpt, dout_s, dh_last, sv(du), sv(ddelta), sv(dB), sv(dC), sv(dz))
         dA, dD, ddb, dh_rows = res[2], res[5], res[6], res[8]
         # 4. parameter gradients are sums over the whole sequence
+        _mark("bwd_param_allreduce")
         if group.world > 1:
             parts = [dA.reshape(-1)] + [t for t in (dD, ddb) if t is not None and t.numel()]
             flat = group.all_reduce_(torch.cat(parts))
@@ -268,6 +318,7 @@ class SlicedScanFn(torch.autograd.Function):
         dh_init = None
         if h_init is not None:
             dh_init = dh_rows[:Bc].reshape_as(h_init) if r == 0 else torch.zeros_like(h_init)
+        _mark("end_bwd")
         return (du, ddelta, dA, dB, dC, dD if D is not None else None, dz,
                 ddb if delta_bias is not None else None, dh_init, None, None, None, None)
 
@@ -282,4 +333,5 @@ def sliced_scan(u, delta, A, B, C, D=None, z=None, delta_bias=None, h_init=None,
                               kernels if kernels is not None else KERNELS)
 
 
-__all__ = ["plan_segments", "segment_view", "SliceGroup", "SlicedScanFn", "sliced_scan", "KERNELS"]
+__all__ = ["plan_segments", "segment_view", "SliceGroup", "SlicedScanFn", "sliced_scan", "KERNELS", "PhaseTimer",
+           "set_phase_timer"]
