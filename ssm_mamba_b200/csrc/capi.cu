@@ -588,9 +588,11 @@ int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, i
                                        a->dim * a->dstate, (int64_t)p.nck * a->dim * a->dstate, (int)a->dstate,
                                        dt, 2)))
             return rc;
-        const CUtensorMapSwizzle none = CU_TENSOR_MAP_SWIZZLE_NONE;
-        // output rows are TB * element bytes: 32 (bf16) or 64 (f32) bytes
+        // output rows are TB * element bytes: 32 (bf16) or 64 (f32) bytes; the pair kernel with
+        // two channels per lane loads its input tiles with the same swizzle (the others read
+        // them unswizzled)
         const CUtensorMapSwizzle osw = is_bf16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
+        const CUtensorMapSwizzle none = (pair && cpl == 2) ? osw : CU_TENSOR_MAP_SWIZZLE_NONE;
         const int64_t L = a->seqlen, Dm = a->dim, Bs = a->batch, N = a->dstate;
         if ((rc = encode3d(&maps[0], a->u, is_bf16, L, Dm, Bs, a->u_dim_stride, a->u_batch_stride, TB, dt, none)) ||
             (rc = encode3d(&maps[1], a->delta, is_bf16, L, Dm, Bs, a->delta_dim_stride, a->delta_batch_stride, TB, dt, none)) ||

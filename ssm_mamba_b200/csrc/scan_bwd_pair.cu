@@ -23,10 +23,12 @@
 //    first quad without keeping it (1.5 exp2 per element, which the MUFU pipe affords).  The
 //    two checkpoints a tile restarts from arrive by TMA with the tile (a 4-D box of the
 //    checkpoint tensor), double-buffered, so no register holds a prefetch.
-//  * Tiles of 16 tokens arrive by one TMA stage, refilled as soon as the tile prologue has
-//    consumed it; du, ddelta, dz leave by TMA stores.  Tokens past the end of the sequence
-//    are identity steps with zero inputs (the prologue zeroes their delta, delta*u, dout and
-//    softplus slope), so a ragged last tile needs no other case.
+//  * Tiles of 16 tokens arrive by one TMA stage (with 2 channels per lane swizzled like the
+//    output tiles, so the prologue's reads and row stores are free of bank conflicts),
+//    refilled as soon as the tile prologue has consumed it; du, ddelta, dz leave by TMA
+//    stores.  Tokens past the end of the sequence are identity steps with zero inputs (the
+//    prologue zeroes their delta, delta*u, dout and softplus slope), so a ragged last tile
+//    needs no other case.
 #include "common.cuh"
 #include "params.h"
 #include "scan_layout.h"
@@ -54,6 +56,7 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
     constexpr int K = kPairK;
     constexpr int RS = TB + 4;
     constexpr int CPW = 8 * CPL;                // channels per warp
+    constexpr bool SWZ = CPL == 2;              // input tiles swizzled (see the prologue)
     static_assert(TB == 2 * K && K == 8, "tiles of two 8-token sub-tiles");
     static_assert(CPL == 1 || CPL == 2, "one or two channels per lane");
 
@@ -144,6 +147,8 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
     };
     // byte offset of (channel row, token) in a swizzled output tile
     auto out_off = [](int row, int t) -> uint32_t { return ES == 2 ? swz32(row, t * ES) : swz64(row, t * ES); };
+    // ... and in an input tile: swizzled like the outputs when SWZ, else dense rows
+    auto raw_off = [&](int row, int t) -> uint32_t { return SWZ ? out_off(row, t) : (uint32_t)(row * TB + t) * ES; };
 
     if (tid == 0) {
         mbar_init(bar, 1);
@@ -161,11 +166,16 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
             return;
         }
 
-        // ---- prologue: 4 tokens of one channel per work item -----------------------------
+        // ---- prologue: 4 tokens of one channel per work item.  With 2 channels per lane (SWZ)
+        // the 8 lanes of a quarter warp take 8 channels at the same tokens, so their 16-byte row
+        // stores (stride RS) hit 8 distinct bank groups and their reads of the swizzled raw
+        // tiles 8 distinct banks; with 1 channel per lane, 4 lanes per channel and unswizzled
+        // raw tiles measured faster (config 2: 0.615 vs 0.628 ms) ----------------------------
         const bool tile_short = t0 + TB > Lq;
         for (int i = tid; i < DT * (TB / 4); i += nthr) {
-            const int cc = i / (TB / 4), t4 = (i % (TB / 4)) * 4;
-            const uint32_t off = (uint32_t)(cc * TB + t4) * ES;
+            const int cc = SWZ ? (i & 7) + ((i >> 5) << 3) : i / (TB / 4);
+            const int t4 = SWZ ? ((i >> 3) & 3) * 4 : (i % (TB / 4)) * 4;
+            const uint32_t off = raw_off(cc, t4);
             float uv[4], dr[4], dg[4];
             Vec4<IT>::load(smem + S.u + off, uv);
             Vec4<IT>::load(smem + S.delta + off, dr);
@@ -211,12 +221,15 @@ __global__ void __launch_bounds__(128) scan_bwd_pair_kernel(
         }
         // B, C as float32 rows [token][16 states] in 4 XOR-rotated copies (copy r holds the
         // states of float4 group q in the order s ^ r), float4 groups swizzled by token
+        // (SWZ: item i -> group q, token tt such that a quarter warp's 8 stores land in 8
+        // distinct 16-byte bank groups)
         for (int i = tid; i < 4 * TB; i += nthr) {
-            const int q = i / TB, tt = i % TB;
+            const int q = SWZ ? ((i >> 2) & 1) + 2 * (i >> 5) : i / TB;
+            const int tt = SWZ ? (i & 3) + 4 * ((i >> 3) & 3) : i % TB;
             float vb[4], vc[4];
 #pragma unroll
             for (int k = 0; k < 4; k++) {
-                const uint32_t off = (uint32_t)((q * 4 + k) * TB + tt) * ES;
+                const uint32_t off = raw_off(q * 4 + k, tt);
                 vb[k] = to_f(*reinterpret_cast<const IT*>(smem + S.B + off));
                 vc[k] = to_f(*reinterpret_cast<const IT*>(smem + S.C + off));
             }

@@ -146,9 +146,11 @@ __host__ __device__ inline BwdPairSmem bwd_pair_smem_layout(int dt, int nwarps, 
     BwdPairSmem L;
     const int TB = kBwdTile, NS = 16;
     const uint32_t row = (uint32_t)TB * es;
+    // every TMA tile, loads included, is swizzled (32B for bf16 rows, 64B for f32 rows):
+    // 512-byte aligned bases
     const uint32_t otile = align_up((uint32_t)dt * row, 512u);
-    const uint32_t tile = align_up((uint32_t)dt * row, 128u);
-    const uint32_t bc = align_up((uint32_t)NS * row, 128u);
+    const uint32_t tile = otile;
+    const uint32_t bc = align_up((uint32_t)NS * row, 512u);
     uint32_t o = 0;
     L.du = o; o += otile;
     L.ddelta = o; o += otile;
