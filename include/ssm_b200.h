@@ -79,7 +79,9 @@ typedef struct ssm_scan_fwd_args {
     float* ckpt;                   /* may be NULL: state checkpoints for the backward */
     int32_t ckpt_format;           /* SSM_CKPT_COMPACT or SSM_CKPT_REFERENCE */
     int32_t _pad1;
-    int64_t ckpt_len;              /* tokens per checkpoint, a power of two >= 4 */
+    int64_t ckpt_len;              /* tokens per checkpoint, a power of two: for SSM_CKPT_COMPACT
+                                      >= ssm_scan_ckpt_len(dstate), for SSM_CKPT_REFERENCE >= 32
+                                      (the reference uses 128) */
     float* h_last;                 /* may be NULL: final state (batch, dim, dstate) */
 } ssm_scan_fwd_args;
 

@@ -118,6 +118,7 @@ StateSplit scan_split(int64_t n, int64_t rows, int sms, const char* env) {
     const char* e = getenv(env);
     if (e && e[0] == '2' && s2_ok) return s2;
     if (e && e[0] == '4') return s4;
+    if (e && e[0] == '8' && ns >= 16 && strcmp(env, "SSM_FWD_SPT") == 0) return {ns / 8, 8, 8};
     const double warps4 = (double)rows * (ns / 4) / 32.0 / (sms > 0 ? sms : 148);
     return (warps4 < 4.0 && s2_ok) ? s2 : s4;
 }
@@ -318,6 +319,12 @@ static int fwd_impl(const ssm_scan_fwd_args* a, const float* restart, void* stre
             return fail(SSM_ERR_INVALID, "ssm_scan_fwd: unknown checkpoint format");
         if (a->ckpt_len < 4 || (a->ckpt_len & (a->ckpt_len - 1)) != 0 || a->ckpt_len > (1 << 20))
             return fail(SSM_ERR_INVALID, "ssm_scan_fwd: ckpt_len must be a power of two >= 4");
+        // the forward writes reference-layout carries only at the ends of its token groups
+        if (a->ckpt_format == SSM_CKPT_REFERENCE && a->ckpt_len < 32)
+            return fail(SSM_ERR_INVALID, "ssm_scan_fwd: SSM_CKPT_REFERENCE needs ckpt_len >= 32");
+        if (a->ckpt_format == SSM_CKPT_COMPACT && a->ckpt_len < ssm_scan_ckpt_len(a->dstate))
+            return fail(SSM_ERR_INVALID, "ssm_scan_fwd: SSM_CKPT_COMPACT needs ckpt_len >= ssm_scan_ckpt_len(dstate) = %lld",
+                        (long long)ssm_scan_ckpt_len(a->dstate));
     }
     const int is_bf16 = a->dtype == SSM_BF16;
     const int64_t es = is_bf16 ? 2 : 4;

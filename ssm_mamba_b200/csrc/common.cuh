@@ -123,6 +123,22 @@ template <> __device__ __forceinline__ void store_pair<__nv_bfloat16>(void* p, f
     *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(v.x, v.y);
 }
 
+// Global stores of 4, 2 or 1 floats issued as ONE predicated instruction: no branch, so the
+// code around them stays one straight-line block the compiler can schedule across.  For
+// write-only buffers the kernel never reads back (no ordering against its own loads).
+__device__ __forceinline__ void stg_f32x4_if(float* p, float a, float b, float c, float d, bool on) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t@q st.global.v4.f32 [%0], {%1, %2, %3, %4};\n\t}"
+                 :: "l"(p), "f"(a), "f"(b), "f"(c), "f"(d), "r"((int)on));
+}
+__device__ __forceinline__ void stg_f32x2_if(float* p, float a, float b, bool on) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t@q st.global.v2.f32 [%0], {%1, %2};\n\t}"
+                 :: "l"(p), "f"(a), "f"(b), "r"((int)on));
+}
+__device__ __forceinline__ void stg_f32_if(float* p, float a, bool on) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.f32 [%0], %1;\n\t}"
+                 :: "l"(p), "f"(a), "r"((int)on));
+}
+
 // Programmatic dependent launch (sm_90+): wait until the preceding grid in the stream has
 // completed and its writes are visible (a no-op when this grid was launched without the
 // programmatic-serialization attribute), and let the next grid start launching.

@@ -66,6 +66,142 @@ __device__ __forceinline__ void fwd_write_ckpt(const FwdParams& p, const float2 
     }
 }
 
+// store_ckpt_row as predicated stores (no branch): 16- or 8-byte stores when `vec`, else one
+// store per valid state; nothing is stored unless `on`.
+template <int SPT>
+__device__ __forceinline__ void store_ckpt_row_if(float* dst, const float2 (&h)[SPT / 2], bool on, bool vec, int n0,
+                                                  int N) {
+    if constexpr (SPT % 4 == 0) {
+#pragma unroll
+        for (int q = 0; q < SPT / 4; q++)
+            stg_f32x4_if(dst + 4 * q, h[2 * q].x, h[2 * q].y, h[2 * q + 1].x, h[2 * q + 1].y, on && vec);
+    } else {
+        stg_f32x2_if(dst, h[0].x, h[0].y, on && vec);
+    }
+#pragma unroll
+    for (int s = 0; s < SPT; s++) stg_f32_if(dst + s, (s & 1) ? h[s / 2].y : h[s / 2].x, on && !vec && n0 + s < N);
+}
+
+// The recurrence over one group of G tokens, tile-local [q0, q0 + G), for this lane's SPT
+// states of channel row c: yv[j] = the lane's part of y at token q0 + j.  tg0 is the group's
+// first token in the sequence.  Compact checkpoints that fall inside the group (not at its
+// end; their interval is a power of two >= CKMIN) are stored here with predicated stores, so
+// the whole group is one straight-line block; everything at the group's end is
+// fwd_group_end's.
+template <int SPT, int NS, int G, int RS, int QM, int CKMIN>
+__device__ __forceinline__ void fwd_group(const float* sD, const float* sDU, const float* sB, const float* sC, int c,
+                                          int g, int q0, int tg0, const float2 (&A2)[SPT / 2], float2 (&h)[SPT / 2],
+                                          float (&yv)[G], float& Ssum, float*& ck_ptr, bool ck_compact, bool ck_vec,
+                                          int ck_mask, int64_t ck_step, int Lq, int N) {
+    constexpr int NP = SPT / 2;
+#pragma unroll
+    for (int sb = 0; sb < G; sb += 4) {
+        const int tl = q0 + sb;
+        const float4 dl4 = lds128(sD + c * RS + tl);
+        const float4 du4 = lds128(sDU + c * RS + tl);
+        const float dls[4] = {dl4.x, dl4.y, dl4.z, dl4.w};
+        const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            // q0 is a multiple of 16, so the swizzle term is a compile-time constant
+            const int t = tl + j;
+            const int sw = (sb + j) & QM;
+            const float2 dl2 = make_float2(dls[j], dls[j]);
+            const float2 du2 = make_float2(dus[j], dus[j]);
+            float2 bp[NP], cp[NP];
+            load_state_pairs<SPT, NS>(sB, t, g, sw, bp);
+            load_state_pairs<SPT, NS>(sC, t, g, sw, cp);
+            float2 y2 = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int pi = 0; pi < NP; pi++) {
+                const float2 x = __fmul2_rn(dl2, A2[pi]);
+                const float2 a = make_float2(ex2(x.x), ex2(x.y));
+                h[pi] = __ffma2_rn(a, h[pi], __fmul2_rn(du2, bp[pi]));
+                y2 = __ffma2_rn(cp[pi], h[pi], y2);
+            }
+            yv[sb + j] = y2.x + y2.y;
+        }
+        Ssum += (dls[0] + dls[1]) + (dls[2] + dls[3]);
+        if (sb + 4 < G && (sb + 4) % CKMIN == 0) {
+            const int tg_end = tg0 + sb + 4;
+            const bool on = ck_compact && (tg_end & ck_mask) == 0 && tg_end <= Lq;
+            store_ckpt_row_if<SPT>(ck_ptr, h, on, ck_vec, g * SPT, N);
+            ck_ptr = on ? ck_ptr + ck_step : ck_ptr;
+        }
+    }
+}
+
+// At the end of a group (sequence token gend): the reference backward's chunk restart (in
+// rechunk mode, every 128 tokens), then the checkpoint due at gend.  Both intervals are
+// multiples of G, so nothing of either falls inside a group except compact checkpoints.
+template <int SPT>
+__device__ __forceinline__ void fwd_group_end(const FwdParams& p, float2 (&h)[SPT / 2], const float2 (&A2)[SPT / 2],
+                                              float Ssum, int b, int d, int g, bool dvalid, bool rechunk,
+                                              bool ck_compact, bool ck_vec, float*& ck_ptr, int64_t ck_step,
+                                              int ck_mask, int gend, int Lq, int N) {
+    if (rechunk && gend < Lq && (gend & 127) == 0 && dvalid) {
+        const float* src = p.restart + (((int64_t)b * p.dim + d) * p.restart_nck + (gend / 128 - 1)) * 2 * N;
+#pragma unroll
+        for (int s = 0; s < SPT; s++) {
+            const int n = g * SPT + s;
+            const float v = n < N ? src[2 * n + 1] : 0.f;
+            if (s & 1) h[s / 2].y = v; else h[s / 2].x = v;
+        }
+    }
+    if ((gend & ck_mask) == 0 && gend <= Lq) {
+        if (ck_compact) {
+            store_ckpt_row<SPT>(ck_ptr, h, ck_vec, g * SPT, N);
+            ck_ptr += ck_step;
+        } else if (p.ckpt && dvalid) {
+            fwd_write_ckpt<SPT>(p, h, A2, Ssum, b, d, g, (gend >> p.ckpt_shift) - 1);
+        }
+    }
+}
+
+// Reduce-scatter of one group's partial y over the LPC lanes of a channel, then the epilogue
+// of the RL = G / LPC consecutive tokens lane g finishes: y = D u + sum_n C h, out = y silu(z).
+// Branch-free, so that it can be scheduled into the next group's recurrence: without a gate
+// sz points at the u tile and the gate is computed and discarded; y is stored before out, so
+// that sy == so (no pre-gate output wanted) leaves out in place.
+template <typename IT, int LPC, int G>
+__device__ __forceinline__ void fwd_finish(float (&yv)[G], int c, int g, int q0, const unsigned char* su,
+                                           const unsigned char* sz, unsigned char* so, unsigned char* sy, float Dd,
+                                           bool has_z) {
+    constexpr int ES = sizeof(IT);
+    constexpr int RL = G / LPC;
+    reduce_scatter_contig<LPC, G>(yv, g);
+    if constexpr (RL >= 4) {
+#pragma unroll
+        for (int r4 = 0; r4 < RL; r4 += 4) {
+            const int tl = q0 + g * RL + r4;
+            const uint32_t off = swz128(c, tl * ES);
+            float uv[4], zv[4], o[4], yt[4];
+            Vec4<IT>::load(su + off, uv);
+            Vec4<IT>::load(sz + off, zv);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                yt[j] = fmaf(Dd, uv[j], yv[r4 + j]);
+                const float gated = yt[j] * zv[j] * sigmoid_io<IT>(zv[j]);
+                o[j] = has_z ? gated : yt[j];
+            }
+            Vec4<IT>::store(sy + off, yt);
+            Vec4<IT>::store(so + off, o);
+        }
+    } else {
+#pragma unroll
+        for (int r = 0; r < RL; r++) {
+            const int tl = q0 + g * RL + r;
+            const uint32_t off = swz128(c, tl * ES);
+            const float uv = to_f(*reinterpret_cast<const IT*>(su + off));
+            const float zv = to_f(*reinterpret_cast<const IT*>(sz + off));
+            const float yt = fmaf(Dd, uv, yv[r]);
+            const float gated = yt * zv * sigmoid_io<IT>(zv);
+            *reinterpret_cast<IT*>(sy + off) = from_f<IT>(yt);
+            *reinterpret_cast<IT*>(so + off) = from_f<IT>(has_z ? gated : yt);
+        }
+    }
+}
+
 template <typename IT, int LPC, int SPT>
 __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     const __grid_constant__ FwdParams p, const __grid_constant__ CUtensorMap tm_u,
@@ -77,10 +213,11 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     constexpr int NS = LPC * SPT;            // padded state count
     constexpr int NP = SPT / 2;              // state pairs per thread (packed f32x2 math)
     constexpr int G = LPC > 16 ? LPC : 16;   // tokens per group (one reduce-scatter each)
-    constexpr int RL = G / LPC;              // consecutive tokens a lane finishes per group
     constexpr int Q = NS / 4;                // float4 groups per B/C row
     constexpr int QM = (Q < 8 ? Q : 8) - 1;  // swizzle mask for the f32 B/C rows
     constexpr int RS = T + 4;                // padded row of sD / sDU (floats)
+    // shortest compact checkpoint interval the host accepts: ssm_scan_ckpt_len(dstate)
+    constexpr int CKMIN = NS > 128 ? 4 : 8;
     static_assert(T % G == 0 && (SPT == 2 || SPT % 4 == 0), "tile must hold whole groups");
 
     extern __shared__ __align__(1024) unsigned char smem[];
@@ -108,12 +245,13 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
     const int ntiles = (Lq + T - 1) / T;
     const bool has_z = p.z != nullptr;
     const bool want_y = p.y != nullptr;
-    const bool want_prod = p.ckpt != nullptr && p.ckpt_format == 1;
     const int ck_mask = p.ckpt_len - 1;     // checkpoint interval is a power of two
     // compact checkpoints are written in order: checkpoint k of this thread's states sits at
     // ck_ptr after k steps of ck_step floats (vector stores when the states are whole pairs)
     const bool ck_compact = p.ckpt != nullptr && p.ckpt_format == 0 && dvalid;
-    const bool ck_vec = (g * SPT + SPT <= p.dstate) && (p.dstate & 3) == 0;
+    // whole aligned vectors of states per lane (16-byte stores for SPT >= 4, 8-byte for 2)
+    const bool ck_vec = (g * SPT + SPT <= p.dstate) && (p.dstate & 3) == 0 &&
+                        (reinterpret_cast<uintptr_t>(p.ckpt) & (SPT % 4 == 0 ? 15u : 7u)) == 0;
     float* ck_ptr = ck_compact ? p.ckpt + ((int64_t)b * p.nck * p.dim + d) * p.dstate + g * SPT : nullptr;
     const int64_t ck_step = (int64_t)p.dim * p.dstate;
 
@@ -143,7 +281,7 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
         if (s & 1) { A2[s / 2].y = a; h[s / 2].y = h0; } else { A2[s / 2].x = a; h[s / 2].x = h0; }
     }
     const float Dd = (dvalid && p.D) ? p.D[d] : 0.f;
-    float Ssum = 0.f;  // running sum of effective delta (for the reference checkpoint product)
+    float Ssum = 0.f;  // running sum of effective delta (for reference-layout checkpoint products)
     for (int i = tid; i < DT; i += nthr)
         sBias[i] = (d0 + i < p.dim && p.delta_bias) ? p.delta_bias[d0 + i] : 0.f;
 
@@ -269,99 +407,42 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
         if (p.use_tma && tid == 0) tma_store_wait_read_all();
         __syncthreads();
 
-        // ---- scan: groups of G tokens, then one reduce-scatter and the epilogue ----------
-        const unsigned char* sz = smem + stage_off(L.z, st);
+        // ---- scan: groups of G tokens ---------------------------------------------------
+        // The reduce-scatter and epilogue of group k are issued after the recurrence of
+        // group k + 1 in the same straight-line block, so their shuffle and MUFU latencies
+        // overlap it; the group-end work that needs branches comes last.
+        const unsigned char* sz = has_z ? smem + stage_off(L.z, st) : su;
         unsigned char* so = smem + L.out;
-        unsigned char* sy = smem + L.y;
+        unsigned char* sy = want_y ? smem + L.y : so;
+        if constexpr (G <= 16) {
+            float yp[G];
+            fwd_group<SPT, NS, G, RS, QM, CKMIN>(sD, sDU, sB, sC, c, g, 0, t0, A2, h, yp, Ssum, ck_ptr, ck_compact, ck_vec,
+                                          ck_mask, ck_step, Lq, N);
+            fwd_group_end<SPT>(p, h, A2, Ssum, b, d, g, dvalid, rechunk, ck_compact, ck_vec, ck_ptr, ck_step,
+                               ck_mask, t0 + G, Lq, N);
 #pragma unroll 1
-        for (int q0 = 0; q0 < T; q0 += G) {
-            float yv[G];
+            for (int q0 = G; q0 < T; q0 += G) {
+                float yv[G];
+                fwd_group<SPT, NS, G, RS, QM, CKMIN>(sD, sDU, sB, sC, c, g, q0, t0 + q0, A2, h, yv, Ssum, ck_ptr,
+                                              ck_compact, ck_vec, ck_mask, ck_step, Lq, N);
+                fwd_finish<IT, LPC, G>(yp, c, g, q0 - G, su, sz, so, sy, Dd, has_z);
 #pragma unroll
-            for (int sb = 0; sb < G; sb += 4) {
-                const int tl = q0 + sb;
-                const float4 dl4 = lds128(sD + c * RS + tl);
-                const float4 du4 = lds128(sDU + c * RS + tl);
-                const float dls[4] = {dl4.x, dl4.y, dl4.z, dl4.w};
-                const float dus[4] = {du4.x, du4.y, du4.z, du4.w};
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    // q0 is a multiple of 16, so the swizzle term is a compile-time constant
-                    const int t = tl + j;
-                    const int sw = (sb + j) & QM;
-                    const float2 dl2 = make_float2(dls[j], dls[j]);
-                    const float2 du2 = make_float2(dus[j], dus[j]);
-                    float2 bp[NP], cp[NP];
-                    load_state_pairs<SPT, NS>(sB, t, g, sw, bp);
-                    load_state_pairs<SPT, NS>(sC, t, g, sw, cp);
-                    float2 y2 = make_float2(0.f, 0.f);
-#pragma unroll
-                    for (int pi = 0; pi < NP; pi++) {
-                        const float2 x = __fmul2_rn(dl2, A2[pi]);
-                        const float2 a = make_float2(ex2(x.x), ex2(x.y));
-                        h[pi] = __ffma2_rn(a, h[pi], __fmul2_rn(du2, bp[pi]));
-                        y2 = __ffma2_rn(cp[pi], h[pi], y2);
-                    }
-                    yv[sb + j] = y2.x + y2.y;
-                }
-                if (want_prod) Ssum += (dls[0] + dls[1]) + (dls[2] + dls[3]);
-                const int tg_end = t0 + tl + 4;
-                if (rechunk && tg_end < Lq && (tg_end & 127) == 0 && dvalid) {
-                    // the reference backward restarts every chunk from the forward's state
-                    const float* src = p.restart +
-                        (((int64_t)b * p.dim + d) * p.restart_nck + (tg_end / 128 - 1)) * 2 * N;
-#pragma unroll
-                    for (int s = 0; s < SPT; s++) {
-                        const int n = g * SPT + s;
-                        const float v = n < N ? src[2 * n + 1] : 0.f;
-                        if (s & 1) h[s / 2].y = v; else h[s / 2].x = v;
-                    }
-                }
-                if ((tg_end & ck_mask) == 0 && tg_end <= Lq) {
-                    if (ck_compact) {
-                        store_ckpt_row<SPT>(ck_ptr, h, ck_vec, g * SPT, N);
-                        ck_ptr += ck_step;
-                    } else if (p.ckpt && dvalid) {
-                        fwd_write_ckpt<SPT>(p, h, A2, Ssum, b, d, g, (tg_end >> p.ckpt_shift) - 1);
-                    }
-                }
+                for (int j = 0; j < G; j++) yp[j] = yv[j];
+                fwd_group_end<SPT>(p, h, A2, Ssum, b, d, g, dvalid, rechunk, ck_compact, ck_vec, ck_ptr, ck_step,
+                                   ck_mask, t0 + q0 + G, Lq, N);
             }
-            // lane g now finishes the RL consecutive tokens q0 + g*RL ...
-            reduce_scatter_contig<LPC, G>(yv, g);
-            if (want_out) {
-#pragma unroll
-                for (int r4 = 0; r4 < RL; r4 += 4) {
-                    if (RL >= 4) {
-                        const int tl = q0 + g * RL + r4;
-                        const uint32_t off = swz128(c, tl * ES);
-                        float uv[4], o[4], yt[4];
-                        Vec4<IT>::load(su + off, uv);
-                        float zv[4];
-                        if (has_z) Vec4<IT>::load(sz + off, zv);
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            yt[j] = fmaf(Dd, uv[j], yv[r4 + j]);
-                            o[j] = has_z ? yt[j] * zv[j] * sigmoid_io<IT>(zv[j]) : yt[j];
-                        }
-                        Vec4<IT>::store(so + off, o);
-                        if (want_y) Vec4<IT>::store(sy + off, yt);
-                    }
-                }
-                if (RL < 4) {
-#pragma unroll
-                    for (int r = 0; r < RL; r++) {
-                        const int tl = q0 + g * RL + r;
-                        const uint32_t off = swz128(c, tl * ES);
-                        const float uv = to_f(*reinterpret_cast<const IT*>(su + off));
-                        const float yt = fmaf(Dd, uv, yv[r]);
-                        float o = yt;
-                        if (has_z) {
-                            const float zv = to_f(*reinterpret_cast<const IT*>(sz + off));
-                            o = yt * zv * sigmoid_io<IT>(zv);
-                        }
-                        *reinterpret_cast<IT*>(so + off) = from_f<IT>(o);
-                        if (want_y) *reinterpret_cast<IT*>(sy + off) = from_f<IT>(yt);
-                    }
-                }
+            fwd_finish<IT, LPC, G>(yp, c, g, T - G, su, sz, so, sy, Dd, has_z);
+        } else {
+            // 32-token groups (32 lanes per channel): two groups' partial sums do not fit in
+            // registers next to the states, so each group finishes before the next starts
+#pragma unroll 1
+            for (int q0 = 0; q0 < T; q0 += G) {
+                float yv[G];
+                fwd_group<SPT, NS, G, RS, QM, CKMIN>(sD, sDU, sB, sC, c, g, q0, t0 + q0, A2, h, yv, Ssum, ck_ptr,
+                                              ck_compact, ck_vec, ck_mask, ck_step, Lq, N);
+                fwd_finish<IT, LPC, G>(yv, c, g, q0, su, sz, so, sy, Dd, has_z);
+                fwd_group_end<SPT>(p, h, A2, Ssum, b, d, g, dvalid, rechunk, ck_compact, ck_vec, ck_ptr, ck_step,
+                                   ck_mask, t0 + q0 + G, Lq, N);
             }
         }
         __syncthreads();

@@ -81,6 +81,16 @@ def test_validation_errors_without_gpu():
         setattr(e, field, 0)
         assert lib.ssm_scan_fwd(ctypes.byref(e), None) == capi.SSM_ERR_INVALID
         assert b"sizes must be positive" in lib.ssm_last_error()
+    # checkpoint intervals: compact ones no shorter than ssm_scan_ckpt_len(dstate), reference-
+    # layout ones at least 32 tokens (the forward writes those only at its group ends)
+    for fmt, k, msg in ((capi.SSM_CKPT_COMPACT, 4, b"ssm_scan_ckpt_len"), (capi.SSM_CKPT_REFERENCE, 16, b">= 32"),
+                        (capi.SSM_CKPT_COMPACT, 12, b"power of two")):
+        c = capi.ScanFwdArgs()
+        c.batch, c.dim, c.seqlen, c.dstate, c.dtype = 1, 1, 64, 16, capi.SSM_F32
+        c.u = c.delta = c.A = c.B = c.C = c.out = c.ckpt = 16
+        c.ckpt_format, c.ckpt_len = fmt, k
+        assert lib.ssm_scan_fwd(ctypes.byref(c), None) == capi.SSM_ERR_INVALID
+        assert msg in lib.ssm_last_error(), lib.ssm_last_error()
     u = capi.StateUpdateArgs()
     u.batch, u.dim, u.dstate, u.dtype = 1, 1, 16, 7
     assert lib.ssm_state_update(ctypes.byref(u), None) == capi.SSM_ERR_INVALID

@@ -180,6 +180,52 @@ def test_right_padding_forward_checkpoints_equal_the_rebuilt_ones(cuda, L, lengt
     assert torch.equal(direct, rebuilt)
 
 
+@pytest.mark.parametrize("dtype", [F32, BF16])
+def test_checkpoint_intervals_agree(cuda, dtype):
+    """The forward stores compact checkpoints inside its token groups and reference-layout
+    carries at group ends.  Every interval holds the same states: checkpoint k of interval K
+    is, bit for bit, checkpoint (k + 1) K / 8 - 1 of interval 8 (one kernel, one arithmetic
+    order); the last checkpoint of a ragged sequence is its final state; reference-layout
+    carries every 32 or 128 tokens hold those states next to prod = exp(A * sum of delta),
+    checked against the oracle.  Interval 8 itself is checked by every backward parity test,
+    which restarts from those checkpoints.  Outputs do not depend on the interval."""
+    B, D, L, N = 2, 40, 300, 16
+    inp = scan_inputs(B, D, L, N, dtype, seed=7, device=cuda, with_z=True, with_h_init=True)
+    lib = capi.lib()
+
+    def run(K, fmt):
+        nck = lib.ssm_scan_num_ckpt(L, K)
+        shape = (B, nck, D, N) if fmt == capi.SSM_CKPT_COMPACT else (B, D, nck, 2 * N)
+        ck = torch.full(shape, float("nan"), device=cuda)
+        h_last = torch.empty(B, D, N, device=cuda)
+        out = torch.empty_like(inp.u)
+        capi.call_fwd(capi.fill_fwd(inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, inp.z, inp.delta_bias,
+                                    inp.h_init, out=out, ckpt=ck, ckpt_format=fmt, ckpt_len=K, h_last=h_last))
+        torch.cuda.synchronize()
+        assert capi.check_device_error() == 0
+        assert not torch.isnan(ck).any()
+        return ck, h_last, out
+
+    c8, h8, o8 = run(8, capi.SSM_CKPT_COMPACT)
+    assert torch.equal(c8[:, -1], h8)
+    for K in (16, 32, 64):
+        ck, hl, out = run(K, capi.SSM_CKPT_COMPACT)
+        full, r = L // K, K // 8
+        assert torch.equal(ck[:, :full], c8[:, r - 1:full * r:r]), f"interval {K}"
+        assert torch.equal(ck[:, -1], h8), f"interval {K}: last checkpoint"
+        assert torch.equal(hl, h8) and torch.equal(out, o8)
+    fw = oracle_fwd(inp, z=inp.z, h_init=inp.h_init)
+    for K in (32, 128):
+        ck, hl, out = run(K, capi.SSM_CKPT_REFERENCE)
+        full, r = L // K, K // 8
+        states = ck[..., 1::2]
+        assert torch.equal(states[:, :, :full].permute(0, 2, 1, 3), c8[:, r - 1:full * r:r]), f"reference {K}"
+        assert torch.equal(states[:, :, -1], h8)
+        assert torch.equal(out, o8)
+        if K == 128:   # the oracle's carries are the reference's, every 128 tokens
+            assert_close(ck, fw["ckpt"], 1e-4 if dtype == F32 else 1e-2, 1e-5 if dtype == F32 else 5e-2, "carries")
+
+
 def test_reference_api_without_length(cuda):
     from ssm_mamba_b200 import SelectiveScanFn
     inp = scan_inputs(2, 48, 640, 16, F32, seed=9, device=cuda, with_z=False, with_h_init=True)
