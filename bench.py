@@ -1068,21 +1068,33 @@ def run_ours(args, world, rank, local, pg):
     issue = {"what": "warp instructions issued per second against 4 per clock per SM (the issue limit) "
                      "at the sampled SM clock; instruction counts from ncu (profiles/)",
              "sm_mhz": mhz, "sms": sms, "peak_warp_inst_per_s": issue_peak}
-    for kname, ms_k in (("scan_bwd_pair_kernel", bwd_ms), ("scan_fwd_kernel", fwd_ms)):
+    bwd_kernel = "scan_bwd_split_kernel"   # the backward's main kernel at config 2's 12 288 rows
+    for kname, ms_k in ((bwd_kernel, bwd_ms), ("scan_fwd_kernel", fwd_ms)):
         n_inst = traffic_from_profiles(kname, key="warp_instructions_per_launch")
         if n_inst:
             issue[kname] = {"warp_inst_per_launch": n_inst, "achieved_warp_inst_per_s": n_inst / (ms_k / 1e3),
                             "frac": n_inst / (ms_k / 1e3) / issue_peak}
-    # The binding roof of each scan kernel, from its committed per-launch counts over the
-    # duration measured here: the backward is bound by the shared-memory pipe (one 128-byte
-    # wavefront or one warp shuffle per clock per SM), the forward by the MUFU pipe (16
-    # exp2 / reciprocal / tanh results per clock per SM, so a warp instruction holds it 2
-    # clocks per SM).
+    # The roofs of each scan kernel other than HBM, from its committed per-launch counts over
+    # the duration measured here: instruction issue (4 warp instructions per clock per SM), the
+    # shared-memory pipe (one 128-byte wavefront or one warp shuffle per clock per SM) and the
+    # MUFU pipe (16 exp2 / reciprocal / tanh results per clock per SM: a warp instruction
+    # holds it 2 clocks per SM).  `bound` names the highest; none is saturated at config 2
+    # (both kernels are latency-bound with ~10 warps per SM), so binding_frac is its fraction.
     sm_hz = mhz * 1e6
-    mio = traffic_from_profiles("scan_bwd_pair_kernel", key="mio_ops_per_launch")
-    mio_frac = mio / (bwd_ms / 1e3) / (sms * sm_hz) if mio else None
-    mufu = traffic_from_profiles("scan_fwd_kernel", key="mufu_warp_inst_per_launch")
-    mufu_frac = mufu * 2.0 / (fwd_ms / 1e3) / (sms * sm_hz) if mufu else None
+
+    def roofs(kname, ms_k):
+        per_s = 1.0 / (ms_k / 1e3) / (sms * sm_hz)
+        out = {}
+        for roof, key, scale in (("issue", "warp_instructions_per_launch", 0.25),
+                                 ("mio", "mio_ops_per_launch", 1.0), ("mufu", "mufu_warp_inst_per_launch", 2.0)):
+            n = traffic_from_profiles(kname, key=key)
+            if n:
+                out[roof] = n * scale * per_s
+        return out
+
+    bwd_roofs, fwd_roofs = roofs(bwd_kernel, bwd_ms), roofs("scan_fwd_kernel", fwd_ms)
+    bwd_bound = max(bwd_roofs, key=bwd_roofs.get) if bwd_roofs else "latency"
+    fwd_bound = max(fwd_roofs, key=fwd_roofs.get) if fwd_roofs else "latency"
     line = {
         "metric": "scan fwd+bwd achieved HBM TB/s (% of peak) at 1/2/4/8 B200; decode tokens/s",
         "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -1099,17 +1111,18 @@ def run_ours(args, world, rank, local, pg):
         # `bound` names the roof that binds each kernel per the committed ncu counters (DRAM is
         # 10-20% busy); achieved / peak / frac are the HBM figures of the contract,
         # binding_frac the fraction of the binding roof
-        "roofline": {"bound": "mio", "binding_frac": mio_frac,
-                     "binding_what": "shared-memory wavefronts + warp shuffles per launch (ncu, profiles/) over "
-                                     "one per clock per SM at the sampled clock",
-                     "kernel": "ssm_scan_bwd (scan_bwd_pair_kernel, 1 channel per lane at this shape, "
-                               "+ scan_reduce_kernel)",
+        "roofline": {"bound": bwd_bound, "binding_frac": bwd_roofs.get(bwd_bound), "roofs": bwd_roofs,
+                     "binding_what": "fractions of the non-HBM roofs from per-launch ncu counts (profiles/) over "
+                                     "the duration timed here at the sampled clock: issue (4 warp instructions "
+                                     "per clock per SM), mio (one shared-memory wavefront or warp shuffle per "
+                                     "clock per SM), mufu (16 results per clock per SM); none saturated: "
+                                     "latency-bound at ~10 warps per SM",
+                     "kernel": f"ssm_scan_bwd ({bwd_kernel} + scan_reduce_kernel)",
                      "achieved": bwd_gbs, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                     "frac": bwd_gbs / peak, "traffic": traffic_from_profiles("scan_bwd_pair_kernel"),
+                     "frac": bwd_gbs / peak, "traffic": traffic_from_profiles(bwd_kernel),
                      "algorithmic_bytes_per_launch": bwd_bytes},
-        "roofline_fwd": {"bound": "mufu", "binding_frac": mufu_frac,
-                         "binding_what": "MUFU warp instructions per launch (ncu, profiles/) over 0.5 per clock per "
-                                         "SM at the sampled clock",
+        "roofline_fwd": {"bound": fwd_bound, "binding_frac": fwd_roofs.get(fwd_bound), "roofs": fwd_roofs,
+                         "binding_what": "as for roofline",
                          "kernel": "scan_fwd_kernel", "achieved": fwd_gbs, "peak": peak,
                          "unit": "GB/s", "frac": fwd_gbs / peak, "traffic": traffic_from_profiles("scan_fwd_kernel"),
                          "algorithmic_bytes_per_launch": fwd_bytes},

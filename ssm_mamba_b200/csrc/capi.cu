@@ -51,6 +51,8 @@ size_t bwd_smem_bytes(int is_bf16, int lpc, int spt, int dt, int dstate, int has
 cudaError_t launch_scan_bwd_pair(const BwdParams& p, int is_bf16, int cpl, const CUtensorMap* maps,
                                  cudaStream_t stream);
 int bwd_pair_occupancy(int is_bf16, int cpl, int dt, int has_z);
+cudaError_t launch_scan_bwd_split(const BwdParams& p, int is_bf16, const CUtensorMap* maps, cudaStream_t stream);
+int bwd_split_occupancy(int is_bf16, int dt, int has_z);
 int* noalloc_error_word();
 int fwd_occupancy(int is_bf16, int lpc, int spt, int dt, int has_z, int has_y);
 int bwd_occupancy(int is_bf16, int lpc, int spt, int dt, int dstate, int has_z);
@@ -274,7 +276,7 @@ int cached_dt(DtKey key, int sms, OccFn occ) {
         for (int i = 0; i < g_dt_n; i++)
             if (g_dt_keys[i] == key) return g_dt_vals[i];
     }
-    const int dt = choose_dt(key.batch, key.dim, key.lpc, sms, (key.kind <= 1 || key.kind == 5) ? 8.0 : 4.0, occ);
+    const int dt = choose_dt(key.batch, key.dim, key.lpc, sms, (key.kind <= 1 || key.kind >= 5) ? 8.0 : 4.0, occ);
     std::lock_guard<std::mutex> lk(g_dt_mu);
     const int slot = g_dt_n < 64 ? g_dt_n++ : (int)(key.dim % 64);
     g_dt_keys[slot] = key;
@@ -410,11 +412,12 @@ int ssm_scan_ckpt_from_reference(const ssm_scan_fwd_args* a, const float* ref_ck
 }
 
 // Shape checks and CTA sizing of the backward; touches no device memory.
-// Backward kernels: scan_bwd_pair_kernel (scan_bwd_pair.cu) for d_state 16 without `length`
-// when every stream is a TMA source/target -- with two channels per lane when the rows give
-// it at least 32 warps per SM (rows >= 512 * SMs), else one -- and scan_bwd_kernel for
-// everything else.  SSM_BWD_KERNEL=general forces the latter (for comparisons);
-// SSM_BWD_PAIR_CPL (1, 2) and SSM_BWD_PAIR_DT override the pair kernel's shape.
+// Backward kernels, for d_state 16 without `length` when every stream is a TMA source/target:
+// scan_bwd_pair_kernel (scan_bwd_pair.cu) with two channels per lane when the rows give it at
+// least 32 warps per SM (rows >= 512 * SMs), else scan_bwd_split_kernel (scan_bwd_split.cu,
+// two channels x two states per lane, twice the warps); scan_bwd_kernel for everything else.
+// SSM_BWD_KERNEL=general forces the latter (for comparisons); SSM_BWD_PAIR_CPL (1: the pair
+// kernel with one channel per lane, 2, 3: split) and SSM_BWD_PAIR_DT override the choice.
 static bool bwd_pair_shape(const ssm_scan_bwd_args* a) {
     const char* e = getenv("SSM_BWD_KERNEL");
     if (e && strcmp(e, "general") == 0) return false;
@@ -446,20 +449,26 @@ static int bwd_shape(const ssm_scan_bwd_args* a, int sms, StateSplit* sp, int* d
     *dt_pair = 0;
     *cpl = 1;
     if (bwd_pair_shape(a)) {
-        // measured on B200: 20480 rows (4 x 5120): one channel per lane 1.07 ms, two 1.26 ms;
-        // 163840 rows (config 5 as 32 segments): one 13.6 ms, two 12.9 ms
-        int c = (a->batch * a->dim >= (int64_t)512 * (sms > 0 ? sms : 148)) ? 2 : 1;
+        // measured on B200: 20480 rows (4 x 5120): one channel per lane 1.07 ms, two 1.26 ms,
+        // split 1.03 ms; 12288 rows (config 2): one 0.617 ms, split 0.596 ms; 163840 rows
+        // (config 5 as 32 segments): one 13.6 ms, two 12.9 ms
+        int c = (a->batch * a->dim >= (int64_t)512 * (sms > 0 ? sms : 148)) ? 2 : 3;
         if (const char* e = getenv("SSM_BWD_PAIR_CPL")) {
             const int v = atoi(e);
-            if (v == 1 || v == 2) c = v;
+            if (v == 1 || v == 2 || v == 3) c = v;
         }
+        // c = 3: scan_bwd_split_kernel (2 channels x 2 states per lane, 8 channels per warp)
+        const int cw = c == 3 ? 1 : c;
+        auto occ = [&](int dd) {
+            return c == 3 ? bwd_split_occupancy(is_bf16, dd, has_z) : bwd_pair_occupancy(is_bf16, c, dd, has_z);
+        };
         // 8 channels per warp per channel a lane holds: choose_dt's channel step for
         // 4 / c lanes per channel
-        key.kind = 5; key.lpc = 4 / c; key.spt = 8;
-        int d = cached_dt(key, sms, [&](int dd) { return bwd_pair_occupancy(is_bf16, c, dd, has_z); });
+        key.kind = c == 3 ? 6 : 5; key.lpc = 4 / cw; key.spt = 8;
+        int d = cached_dt(key, sms, occ);
         if (const char* e = getenv("SSM_BWD_PAIR_DT")) {
             const int v = atoi(e);
-            if (v >= 8 * c && v * 4 / c <= 128 && v % (8 * c) == 0 && bwd_pair_occupancy(is_bf16, c, v, has_z) > 0) d = v;
+            if (v >= 8 * cw && v * 4 / cw <= 128 && v % (8 * cw) == 0 && occ(v) > 0) d = v;
         }
         *dt_pair = d > 0 ? d : 0;
         *cpl = c;
@@ -615,8 +624,9 @@ int scan_bwd_run(const ssm_scan_bwd_args* a, void* workspace, size_t ws_bytes, i
     }
     // the forward's failure-detection test hook (SSM_TEST_WITHHOLD_TMA), for the backward
     p.test_withhold = p.use_tma && getenv("SSM_TEST_WITHHOLD_TMA") != nullptr;
-    cudaError_t e = pair ? launch_scan_bwd_pair(p, is_bf16, cpl, maps, stream)
-                         : launch_scan_bwd(p, is_bf16, sp.lpc, sp.spt, maps, stream);
+    cudaError_t e = !pair     ? launch_scan_bwd(p, is_bf16, sp.lpc, sp.spt, maps, stream)
+                    : cpl == 3 ? launch_scan_bwd_split(p, is_bf16, maps, stream)
+                               : launch_scan_bwd_pair(p, is_bf16, cpl, maps, stream);
     if (e != cudaSuccess) return cuda_fail(e, "scan_bwd launch");
 
     ReduceParams r;

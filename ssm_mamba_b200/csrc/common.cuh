@@ -88,6 +88,23 @@ __device__ __forceinline__ float softplus_series(float x, float* t_out = nullptr
     return fmaxf(x, 0.f) + 2.f * s * p;
 }
 
+// softplus_series of two values with packed f32x2 arithmetic: per element the same
+// operations in the same order (2 s p = (2 s) p exactly), so the same results.
+__device__ __forceinline__ float2 softplus_series2(float2 x) {
+    const float2 t = make_float2(ex2(-fabsf(x.x) * kLog2e), ex2(-fabsf(x.y) * kLog2e));
+    const float2 s = make_float2(__fdividef(t.x, 2.f + t.x), __fdividef(t.y, 2.f + t.y));
+    const float2 s2 = __fmul2_rn(s, s);
+    float2 p = make_float2(1.f / 13.f, 1.f / 13.f);
+    p = __ffma2_rn(p, s2, make_float2(1.f / 11.f, 1.f / 11.f));
+    p = __ffma2_rn(p, s2, make_float2(1.f / 9.f, 1.f / 9.f));
+    p = __ffma2_rn(p, s2, make_float2(1.f / 7.f, 1.f / 7.f));
+    p = __ffma2_rn(p, s2, make_float2(1.f / 5.f, 1.f / 5.f));
+    p = __ffma2_rn(p, s2, make_float2(1.f / 3.f, 1.f / 3.f));
+    p = __ffma2_rn(p, s2, make_float2(1.f, 1.f));
+    const float2 sp = __fmul2_rn(__fmul2_rn(make_float2(2.f, 2.f), s), p);
+    return __fadd2_rn(make_float2(fmaxf(x.x, 0.f), fmaxf(x.y, 0.f)), sp);
+}
+
 // logistic sigmoid from t = e^-|x| (as returned by softplus_series)
 __device__ __forceinline__ float sigmoid_from_t(float x, float t) {
     const float r = __fdividef(1.f, 1.f + t);
@@ -148,6 +165,15 @@ __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("grid
 // L2 prefetch hint; L2 is the point of coherence, so a prefetched line is never stale
 __device__ __forceinline__ void prefetch_l2(const void* ptr) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
+// two consecutive elements as float2 (from 4 or 8 bytes of shared memory)
+template <typename T> __device__ __forceinline__ float2 load_pair(const void* p);
+template <> __device__ __forceinline__ float2 load_pair<float>(const void* p) {
+    return *reinterpret_cast<const float2*>(p);
+}
+template <> __device__ __forceinline__ float2 load_pair<__nv_bfloat16>(const void* p) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
 }
 
 // four consecutive elements as float (from 8 or 16 bytes of shared memory)

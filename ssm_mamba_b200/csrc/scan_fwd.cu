@@ -370,15 +370,23 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
             Vec4<IT>::load(sdl + off, dr);
             Vec4<IT>::load(su + off, uv);
             const float bias = sBias[cc];
+            if (tile_masked) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                float x = dr[j];
-                float u = uv[j];
-                if (tile_masked && t0 + t4 + j >= Lload) { x = 0.f; u = 0.f; }
-                x += bias;
-                dl[j] = p.delta_softplus ? softplus_series(x) : x;
-                du[j] = dl[j] * u;
-                if (tile_masked) {
+                for (int j = 0; j < 4; j++)
+                    if (t0 + t4 + j >= Lload) { dr[j] = 0.f; uv[j] = 0.f; }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; j += 2) {
+                const float2 x = make_float2(dr[j] + bias, dr[j + 1] + bias);
+                const float2 v = p.delta_softplus ? softplus_series2(x) : x;
+                dl[j] = v.x;
+                dl[j + 1] = v.y;
+                du[j] = dl[j] * uv[j];
+                du[j + 1] = dl[j + 1] * uv[j + 1];
+            }
+            if (tile_masked) {
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
                     const int tg = t0 + t4 + j;
                     if (tg >= Lq || tg < mlo || tg >= mhi) { dl[j] = 0.f; du[j] = 0.f; }
                 }
@@ -388,20 +396,26 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
         }
         const unsigned char* sBr = smem + stage_off(L.B, st);
         const unsigned char* sCr = smem + stage_off(L.C, st);
-        for (int i = tid; i < Q * T; i += nthr) {
-            const int q = i / T, tt = i % T;
-            const bool ld = t0 + tt < Lload;
-            float vb[4], vc[4];
+        // (two tokens per work item: one 4- or 8-byte load per state row and stream)
+        for (int i = tid; i < Q * (T / 2); i += nthr) {
+            const int q = i / (T / 2), tt = 2 * (i % (T / 2));
+            const bool ld0 = t0 + tt < Lload, ld1 = t0 + tt + 1 < Lload;
+            float2 vb[4], vc[4];
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 const int n = q * 4 + k;
                 const uint32_t off = swz128(n, tt * ES);
-                vb[k] = (ld && n < N) ? to_f(*reinterpret_cast<const IT*>(sBr + off)) : 0.f;
-                vc[k] = (ld && n < N) ? to_f(*reinterpret_cast<const IT*>(sCr + off)) : 0.f;
+                vb[k] = n < N ? load_pair<IT>(sBr + off) : make_float2(0.f, 0.f);
+                vc[k] = n < N ? load_pair<IT>(sCr + off) : make_float2(0.f, 0.f);
+                if (!ld0) { vb[k].x = 0.f; vc[k].x = 0.f; }
+                if (!ld1) { vb[k].y = 0.f; vc[k].y = 0.f; }
             }
-            const int pos = tt * NS + ((q ^ (tt & QM)) << 2);
-            *reinterpret_cast<float4*>(sB + pos) = make_float4(vb[0], vb[1], vb[2], vb[3]);
-            *reinterpret_cast<float4*>(sC + pos) = make_float4(vc[0], vc[1], vc[2], vc[3]);
+            const int pos0 = tt * NS + ((q ^ (tt & QM)) << 2);
+            const int pos1 = (tt + 1) * NS + ((q ^ ((tt + 1) & QM)) << 2);
+            *reinterpret_cast<float4*>(sB + pos0) = make_float4(vb[0].x, vb[1].x, vb[2].x, vb[3].x);
+            *reinterpret_cast<float4*>(sC + pos0) = make_float4(vc[0].x, vc[1].x, vc[2].x, vc[3].x);
+            *reinterpret_cast<float4*>(sB + pos1) = make_float4(vb[0].y, vb[1].y, vb[2].y, vb[3].y);
+            *reinterpret_cast<float4*>(sC + pos1) = make_float4(vc[0].y, vc[1].y, vc[2].y, vc[3].y);
         }
         // the previous tile's TMA stores must be done reading the output tiles
         if (p.use_tma && tid == 0) tma_store_wait_read_all();

@@ -291,8 +291,10 @@ def test_large_config2_shape_properties(cuda):
     assert_close(h2, hl, 1e-4, 1e-5, "split last state")
 
 
-# d_state 16 without `length` takes scan_bwd_pair_kernel (two channels per lane);
-# SSM_BWD_KERNEL=general forces scan_bwd_kernel.  Both against each other and the oracle.
+# d_state 16 without `length` takes one of the pair-family kernels: scan_bwd_pair_kernel with
+# one (SSM_BWD_PAIR_CPL=1) or two (2) channels per lane, or scan_bwd_split_kernel (3: two
+# channels x two states per lane); SSM_BWD_KERNEL=general forces scan_bwd_kernel.  Each
+# against the general kernel and the oracle.
 PAIR_CASES = [
     (2, 64, 256, 16, F32, True, True),
     (1, 40, 300, 16, F32, True, False),     # channels not a multiple of 16, ragged last tile
@@ -303,12 +305,15 @@ PAIR_CASES = [
 ]
 
 
+@pytest.mark.parametrize("layout", ["1", "2", "3"])
 @pytest.mark.parametrize("case", PAIR_CASES, ids=_ids)
-def test_pair_and_general_backward_kernels_agree(cuda, case, monkeypatch):
+def test_pair_and_general_backward_kernels_agree(cuda, case, layout, monkeypatch):
     B, D, L, N, dt, with_z, with_h = case
     inp = scan_inputs(B, D, L, N, dt, seed=B * 100 + L, device=cuda, with_z=with_z, with_h_init=with_h)
     dh_last = torch.randn(B, D, N, device=cuda) if with_h else None
+    monkeypatch.setenv("SSM_BWD_PAIR_CPL", layout)
     pair = _run_capi(inp, inp.z, inp.h_init, dh_last)
+    monkeypatch.delenv("SSM_BWD_PAIR_CPL")
     monkeypatch.setenv("SSM_BWD_KERNEL", "general")
     general = _run_capi(inp, inp.z, inp.h_init, dh_last)
     monkeypatch.delenv("SSM_BWD_KERNEL")
