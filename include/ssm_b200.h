@@ -301,6 +301,12 @@ SSM_API int ssm_conv1d_update(const ssm_conv1d_args* args, void* stream);
  * kernel's code (1: a bounded wait for a TMA copy ran out; 2: misaligned shared memory). */
 SSM_API int ssm_check_device_error(int* code, void* stream);
 
+/* Diagnostics: evaluates, for n float32 inputs x on the device, the exp2 that the carry passes
+ * (ssm_scan_chunk_state_fwd / _bwd) compute on the FMA pipe for a share of their elements
+ * (into y_fma) and the MUFU ex2.approx.ftz that the other elements use (into y_mufu), so
+ * that a test can hold the former to the latter's error bound.  No reference counterpart. */
+SSM_API int ssm_exp2_compare(const float* x, float* y_fma, float* y_mufu, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -171,6 +171,8 @@ def lib() -> ctypes.CDLL:
         L.ssm_conv1d_update.restype = ctypes.c_int
         L.ssm_check_device_error.argtypes = [ctypes.POINTER(ctypes.c_int), _p]
         L.ssm_check_device_error.restype = ctypes.c_int
+        L.ssm_exp2_compare.argtypes = [_p, _p, _p, _i64, _p]
+        L.ssm_exp2_compare.restype = ctypes.c_int
         _lib = L
     return _lib
 

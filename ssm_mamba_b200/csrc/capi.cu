@@ -51,6 +51,7 @@ size_t bwd_smem_bytes(int is_bf16, int lpc, int spt, int dt, int dstate, int has
 cudaError_t launch_scan_bwd_pair(const BwdParams& p, int is_bf16, int cpl, const CUtensorMap* maps,
                                  cudaStream_t stream);
 int bwd_pair_occupancy(int is_bf16, int cpl, int dt, int has_z);
+cudaError_t launch_exp2_compare(const float* x, float* y_fma, float* y_mufu, int64_t n, cudaStream_t stream);
 cudaError_t launch_scan_bwd_split(const BwdParams& p, int is_bf16, const CUtensorMap* maps, cudaStream_t stream);
 int bwd_split_occupancy(int is_bf16, int dt, int has_z);
 int* noalloc_error_word();
@@ -943,6 +944,18 @@ int ssm_conv1d_update(const ssm_conv1d_args* a, void* stream) {
     cudaError_t e = launch_conv1d_update(p, a->dtype == SSM_BF16, (int)a->width, di->sms,
                                          static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "conv1d_update launch");
+    return SSM_OK;
+}
+
+int ssm_exp2_compare(const float* x, float* y_fma, float* y_mufu, int64_t n, void* stream) {
+    NvtxRange r_("ssm_exp2_compare");
+    if (!x || !y_fma || !y_mufu || n < 1 || n > ((int64_t)1 << 31))
+        return fail(SSM_ERR_INVALID, "ssm_exp2_compare: x, y_fma, y_mufu must be non-NULL and 1 <= n <= 2^31");
+    DevInfo* di = nullptr;
+    int rc = device_info(&di);
+    if (rc) return rc;
+    cudaError_t e = launch_exp2_compare(x, y_fma, y_mufu, n, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "exp2_compare launch");
     return SSM_OK;
 }
 

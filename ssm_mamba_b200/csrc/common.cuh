@@ -42,6 +42,35 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// 2^x of two values on the FMA pipe (packed f32x2), for kernels whose MUFU pipe is the
+// bottleneck: a share of their exp2 is computed here instead of by ex2.approx.
+//   x = j + f, j = rint(x) by adding and subtracting 1.5 * 2^23 (round-to-nearest), |f| <= 1/2
+//   2^f ~ 1 + f (c1 + f (c2 + f (c3 + f (c4 + f c5)))), coefficients fitted here for minimax
+//       relative error on [-1/2, 1/2] with the constant term held at 1 (so 2^0 = 1 exactly):
+//       1.1e-7 in exact arithmetic, 1.6e-7 (2^-22.6) evaluated in float32 with fused
+//       multiply-adds
+//   2^j is joined by adding j to the exponent field (j sits in the low bits of the rounded
+//       sum, so (bits << 23) is j << 23)
+// x is first clamped to >= -126, so that the exponent stays in the normal range: inputs below
+// -126 give about 2^-126 (ex2.approx.ftz gives 0 there); those decays multiply states that
+// the kernels' flush-to-zero arithmetic then rounds away.  Inputs are <= 0 in the callers
+// (decays exp(delta * A), A < 0); for x > 127 the result would overflow the exponent.
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+    x = make_float2(fmaxf(x.x, -126.f), fmaxf(x.y, -126.f));
+    const float2 magic = make_float2(12582912.f, 12582912.f);   // 1.5 * 2^23
+    const float2 t = __fadd2_rn(x, magic);
+    const float2 j = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));   // exact
+    const float2 f = __ffma2_rn(j, make_float2(-1.f, -1.f), x);               // exact, |f| <= 1/2
+    float2 p = make_float2(0x1.5cb5a6p-10f, 0x1.5cb5a6p-10f);
+    p = __ffma2_rn(p, f, make_float2(0x1.3cf672p-7f, 0x1.3cf672p-7f));
+    p = __ffma2_rn(p, f, make_float2(0x1.c6b4d6p-5f, 0x1.c6b4d6p-5f));
+    p = __ffma2_rn(p, f, make_float2(0x1.ebf99ap-3f, 0x1.ebf99ap-3f));
+    p = __ffma2_rn(p, f, make_float2(0x1.62e42cp-1f, 0x1.62e42cp-1f));
+    p = __ffma2_rn(p, f, make_float2(1.f, 1.f));
+    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                       __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
 // softplus with threshold 20, as the reference computes it
 // (csrc/selective_scan/forward_kernel.cu:155-159, built with --use_fast_math).
 __device__ __forceinline__ float softplus20(float x) {

@@ -28,6 +28,11 @@
 
 namespace ssm {
 
+// The carry passes are bound by the MUFU pipe (one exp2 per token and state, ~83% busy) while
+// the FMA pipe is ~40% busy: of every 4 (token, state pair) exp2 pairs, kChunkExpOnFma are
+// computed on the FMA pipe by exp2_fma2 (common.cuh) instead of by ex2.approx.
+constexpr int kChunkExpOnFma = 1;
+
 __device__ __forceinline__ uint32_t chunk_stage(const uint32_t (&a)[2], int st) { return st ? a[1] : a[0]; }
 
 template <typename IT, int LPC, int SPT, bool REV>
@@ -216,7 +221,8 @@ __global__ void __launch_bounds__(128, 4) scan_chunk_kernel(const __grid_constan
 #pragma unroll
                     for (int pi = 0; pi < NP; pi++) {
                         const float2 e = __fmul2_rn(dl2, A2[pi]);
-                        const float2 a = make_float2(ex2(e.x), ex2(e.y));
+                        const float2 a = (k * NP + pi) % 4 < kChunkExpOnFma ? exp2_fma2(e)
+                                                                            : make_float2(ex2(e.x), ex2(e.y));
                         if (REV) {
                             // dh_t = a_{t+1} dh_{t+1} + C_t dy_t
                             h[pi] = __ffma2_rn(an[pi], h[pi], __fmul2_rn(x2, mp[pi]));
@@ -332,6 +338,28 @@ cudaError_t launch_carry_compose(const CarryParams& p, cudaStream_t stream) {
     const int64_t per = (int64_t)p.batch * p.dim * p.dstate;
     const int64_t blocks = (per + 255) / 256;
     carry_compose_kernel<<<(unsigned)blocks, 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+// ---- diagnostics: the FMA-pipe exp2 next to ex2.approx, on the same inputs ---------------
+__global__ void exp2_compare_kernel(const float* __restrict__ x, float* __restrict__ y_fma,
+                                    float* __restrict__ y_mufu, int64_t n) {
+    const int64_t i = 2 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
+    if (i >= n) return;
+    const float2 v = make_float2(x[i], i + 1 < n ? x[i + 1] : 0.f);
+    const float2 f = exp2_fma2(v);
+    y_fma[i] = f.x;
+    y_mufu[i] = ex2(v.x);
+    if (i + 1 < n) {
+        y_fma[i + 1] = f.y;
+        y_mufu[i + 1] = ex2(v.y);
+    }
+}
+
+cudaError_t launch_exp2_compare(const float* x, float* y_fma, float* y_mufu, int64_t n, cudaStream_t stream) {
+    const int64_t pairs = (n + 1) / 2;
+    const int block = 256;
+    exp2_compare_kernel<<<(unsigned)((pairs + block - 1) / block), block, 0, stream>>>(x, y_fma, y_mufu, n);
     return cudaGetLastError();
 }
 

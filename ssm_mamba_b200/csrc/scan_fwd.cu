@@ -434,7 +434,7 @@ __global__ void __launch_bounds__(128, 3) scan_fwd_kernel(
                                           ck_mask, ck_step, Lq, N);
             fwd_group_end<SPT>(p, h, A2, Ssum, b, d, g, dvalid, rechunk, ck_compact, ck_vec, ck_ptr, ck_step,
                                ck_mask, t0 + G, Lq, N);
-#pragma unroll 1
+#pragma unroll 2
             for (int q0 = G; q0 < T; q0 += G) {
                 float yv[G];
                 fwd_group<SPT, NS, G, RS, QM, CKMIN>(sD, sDU, sB, sC, c, g, q0, t0 + q0, A2, h, yv, Ssum, ck_ptr,
