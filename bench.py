@@ -26,6 +26,7 @@ own CUDA kernels on the GPU in float32 (their only dtype).
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -361,7 +362,10 @@ def run_long_seq(args, world, rank, local, pg, peak):
     inp = scan_inputs(1, Dm, Lr, N, torch.bfloat16, seed=4 + rank, device=dev, with_z=True)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     S = plan_segments(1, Dm, Lr, N, sms=sms, ranks=world)
-    group = SliceGroup(pg.group.WORLD if pg is not None else None)
+    # with the process group's store: the host-side liveness check and shape agreement of
+    # every exchange go through it (no collective, no device synchronization)
+    group = SliceGroup(pg.group.WORLD, store=pg.PrefixStore("ssm_long_seq", pg.distributed_c10d._get_default_store()),
+                       peer_timeout=datetime.timedelta(seconds=120)) if pg is not None else SliceGroup(None)
     leaves = [t.clone().requires_grad_() for t in (inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, inp.z,
                                                    inp.delta_bias)]
 

@@ -141,17 +141,21 @@ class SliceGroup:
         self.peer_timeout = peer_timeout
         self._exchanges = 0
 
-    def check_peers(self, what: str) -> None:
+    def check_peers(self, what: str, agree=None) -> None:
         """Host-side liveness check before an exchange (no-op without a store): this rank
         posts that it reached exchange n and waits, at most peer_timeout, until every rank
         has.  Every rank runs the same exchanges in the same order, so n agrees across ranks.
-        Each rank then deletes its key of exchange n - 2, which every rank has passed."""
+        Each rank then deletes its key of exchange n - 2, which every rank has passed.
+        With `agree` = (description, ints), the posted value carries the ints and every rank
+        compares all ranks' values, raising the same RuntimeError on a mismatch: the shape
+        agreement of check_agreement without a collective or a device synchronization."""
         if self.world == 1 or self.store is None:
             return
         n = self._exchanges
         self._exchanges += 1
         key = lambda i, r: f"ssm_slices/{i}/{r}"  # noqa: E731
-        self.store.set(key(n, self.rank), what)
+        values = "" if agree is None else ",".join(str(int(v)) for v in agree[1])
+        self.store.set(key(n, self.rank), f"{what}|{values}")
         keys = [key(n, r) for r in range(self.world)]
         try:
             self.store.wait(keys, self.peer_timeout)
@@ -159,6 +163,11 @@ class SliceGroup:
             missing = [r for r in range(self.world) if not self.store.check([key(n, r)])]
             raise RuntimeError(f"sliced scan: rank(s) {missing} did not reach exchange {n} ({what}) "
                                f"within {self.peer_timeout}") from e
+        if agree is not None:
+            rows = [v.decode().split("|", 1)[1] for v in self.store.multi_get(keys)]
+            if any(r != rows[0] for r in rows):
+                raise RuntimeError(f"sliced scan: ranks disagree on {agree[0]}: "
+                                   f"{[[int(x) for x in r.split(',')] for r in rows]}")
         if n >= 2:
             self.store.delete_key(key(n - 2, self.rank))
 
@@ -227,11 +236,15 @@ class SlicedScanFn(torch.autograd.Function):
         if S > 1 and (Bt != 1 or L % S != 0):
             raise ValueError("segmented scan needs batch 1 and seqlen divisible by the segment count")
         _mark("fwd_agree")
-        group.check_peers("forward")
         # a peer with other shapes or options would exchange carries of another size: refuse
-        group.check_agreement("batch, dim, dstate, segments, z, D, delta_bias, h_init, softplus, dtype",
-                              [Bt, Dm, N, S, z is not None, D is not None, delta_bias is not None,
-                               h_init is not None, bool(delta_softplus), u.element_size()], u.device)
+        # (through the store with the liveness check when there is one, else one all_gather)
+        agree = ("batch, dim, dstate, segments, z, D, delta_bias, h_init, softplus, dtype",
+                 [Bt, Dm, N, S, z is not None, D is not None, delta_bias is not None,
+                  h_init is not None, bool(delta_softplus), u.element_size()])
+        if group.store is not None:
+            group.check_peers("forward", agree)
+        else:
+            group.check_agreement(*agree, u.device)
         Bc = Bt if S == 1 else 1            # batch of one slice
         rows = Bt if S == 1 else S          # rows of the segmented views
         sv = lambda t: segment_view(t, S)  # noqa: E731

@@ -157,25 +157,31 @@ def _faulty_rank_main(rank, world, port, mode, q):
     import datetime
     import torch.distributed as dist
     try:
-        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+        store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=30))
+        dist.init_process_group("gloo", store=store, rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=20))
         if mode == "dies" and rank == 1:
             os._exit(3)                      # a rank that is gone before the exchange
         x = _inputs()
         L = x["u"].shape[-1]
         lo, hi = rank * L // world, (rank + 1) * L // world
-        segments = 2 if (mode == "shape" and rank == 1) else 1
-        _run_slice(x, lo, hi, segments, SliceGroup(dist.group.WORLD), last=rank == world - 1)
+        segments = 2 if (mode in ("shape", "shape_store") and rank == 1) else 1
+        group = SliceGroup(dist.group.WORLD)
+        if mode == "shape_store":            # the agreement through the store, with the liveness check
+            group = SliceGroup(dist.group.WORLD, store=dist.PrefixStore("t", store),
+                               peer_timeout=datetime.timedelta(seconds=10))
+        _run_slice(x, lo, hi, segments, group, last=rank == world - 1)
         q.put((rank, "ok"))
     except Exception as e:  # the clean error this test expects
         q.put((rank, f"{type(e).__name__}: {e}"))
 
 
-@pytest.mark.parametrize("mode", ["shape", "dies"])
+@pytest.mark.parametrize("mode", ["shape", "shape_store", "dies"])
 def test_peer_failure_gives_a_clean_error(mode):
-    """A rank that passes other shapes makes every rank raise the agreement error; a rank
-    that dies before the exchange makes the survivor's collective raise (connection lost or
-    the process group's timeout) instead of hanging."""
+    """A rank that passes other shapes makes every rank raise the agreement error (by the
+    all_gather of check_agreement, or with a store through check_peers); a rank that dies
+    before the exchange makes the survivor's collective raise (connection lost or the
+    process group's timeout) instead of hanging."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -185,7 +191,7 @@ def test_peer_failure_gives_a_clean_error(mode):
         p.start()
     res = {}
     try:
-        for _ in range(world if mode == "shape" else 1):
+        for _ in range(world if mode != "dies" else 1):
             r, msg = q.get(timeout=120)
             res[r] = msg
     finally:
@@ -193,7 +199,7 @@ def test_peer_failure_gives_a_clean_error(mode):
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
-    if mode == "shape":
+    if mode != "dies":
         assert set(res) == {0, 1}
         for r in (0, 1):
             assert "ranks disagree" in res[r], res
