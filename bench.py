@@ -370,6 +370,8 @@ def run_long_seq(args, world, rank, local, pg, peak):
                                                    inp.delta_bias)]
 
     def step():
+        for t in leaves:      # a training step's gradients, not an accumulation over steps
+            t.grad = None
         out, _ = sliced_scan(*leaves, None, True, segments=S, group=group)
         out.backward(inp.dout)
 
@@ -380,21 +382,20 @@ def run_long_seq(args, world, rank, local, pg, peak):
     barrier(pg)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     steps = 3
+    from ssm_mamba_b200.slices import PhaseTimer, set_phase_timer
+    timer = PhaseTimer()
     e0.record()
     for _ in range(steps):
         step()
     e1.record()
+    # per-phase breakdown of one more (untimed) step, queued behind the timed ones as in
+    # the loop: CUDA events between the phases of the sliced scan, each the max over ranks
+    set_phase_timer(timer)
+    step()
+    set_phase_timer(None)
     torch.cuda.synchronize()
     barrier(pg)
     ms = max_over_ranks(e0.elapsed_time(e1), pg) / steps
-    # per-phase breakdown of one more (untimed) step: CUDA events between the phases of the
-    # sliced scan, each phase the max over ranks
-    from ssm_mamba_b200.slices import PhaseTimer, set_phase_timer
-    timer = PhaseTimer()
-    set_phase_timer(timer)
-    step()
-    torch.cuda.synchronize()
-    set_phase_timer(None)
     ph = timer.durations_ms()
     phases = {k: max_over_ranks(ph.get(k, 0.0), pg) for k in sorted(ph)}
     barrier(pg)
@@ -404,9 +405,10 @@ def run_long_seq(args, world, rank, local, pg, peak):
             "ms_per_step": ms, "steps": steps, "scaling": "strong", "segments_per_rank": S,
             "seqpar_parity": parity,
             "phase_ms": phases,
-            "phase_what": "one extra step, CUDA events between phases, max over ranks: agree (shape agreement "
-                          "all_gather + liveness), chunk_state (the chunk-state pass), exchange (carry all_gather), "
-                          "compose (carry folding), scan (the per-segment scan), param_allreduce (dA/dD/ddelta_bias)",
+            "phase_what": "one extra step queued behind the timed ones, CUDA events between phases, max over "
+                          "ranks: agree (shape agreement and liveness of the ranks through the store, on the "
+                          "host), chunk_state (the chunk-state pass), exchange (carry all_gather), compose (carry "
+                          "folding), scan (the per-segment scan), param_allreduce (dA/dD/ddelta_bias)",
             "elem_state_per_s": 1 * Dm * Ltot * N / (ms / 1e3),
             "frac_of_hbm_peak": tbs * 1e3 / world / peak,
             "gpu_launches_per_step": 8,

@@ -29,7 +29,7 @@ CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA, "bin", "nvcc")
 
 CU_SOURCES = ["scan_fwd.cu", "scan_bwd.cu", "scan_bwd_pair.cu", "scan_bwd_split.cu", "scan_chunk.cu", "conv1d.cu", "state_update.cu", "capi.cu", "noalloc.cu"]
-HEADERS = ["common.cuh", "params.h", "scan_layout.h", "warp_reduce.cuh"]
+HEADERS = ["common.cuh", "params.h", "scan_layout.h", "warp_reduce.cuh", "bwd_prologue.cuh"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden"]
 

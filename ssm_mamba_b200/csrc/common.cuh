@@ -119,8 +119,9 @@ __device__ __forceinline__ float softplus_series(float x, float* t_out = nullptr
 
 // softplus_series of two values with packed f32x2 arithmetic: per element the same
 // operations in the same order (2 s p = (2 s) p exactly), so the same results.
-__device__ __forceinline__ float2 softplus_series2(float2 x) {
+__device__ __forceinline__ float2 softplus_series2(float2 x, float2* t_out = nullptr) {
     const float2 t = make_float2(ex2(-fabsf(x.x) * kLog2e), ex2(-fabsf(x.y) * kLog2e));
+    if (t_out) *t_out = t;
     const float2 s = make_float2(__fdividef(t.x, 2.f + t.x), __fdividef(t.y, 2.f + t.y));
     const float2 s2 = __fmul2_rn(s, s);
     float2 p = make_float2(1.f / 13.f, 1.f / 13.f);

@@ -24,6 +24,7 @@
 #include "params.h"
 #include "scan_layout.h"
 #include "warp_reduce.cuh"
+#include "bwd_prologue.cuh"
 
 namespace ssm {
 
@@ -152,49 +153,8 @@ __global__ void __launch_bounds__(128) scan_bwd_split_kernel(
         const bool tile_short = t0 + TB > Lq;
         for (int i = tid; i < DT * (TB / 4); i += nthr) {
             const int cc = i / (TB / 4), t4 = (i % (TB / 4)) * 4;
-            const uint32_t off = raw_off(cc, t4);
-            float uv[4], dr[4], dg[4];
-            Vec4<IT>::load(smem + S.u + off, uv);
-            Vec4<IT>::load(smem + S.delta + off, dr);
-            Vec4<IT>::load(smem + S.dout + off, dg);
-            const float bias = sBias[cc];
-            float dl[4], du[4], spg[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float x = dr[j] + bias;
-                if (p.delta_softplus) {
-                    float t;
-                    dl[j] = softplus_series(x, &t);
-                    spg[j] = sigmoid_from_t(x, t);
-                } else {
-                    dl[j] = x;
-                    spg[j] = 1.f;
-                }
-                du[j] = dl[j] * uv[j];
-            }
-            if (has_z) {
-                float zv[4], yv[4], dz[4];
-                Vec4<IT>::load(smem + S.z + off, zv);
-                Vec4<IT>::load(smem + S.y + off, yv);
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const float sg = sigmoid_io<IT>(zv[j]);
-                    dz[j] = dg[j] * yv[j] * sg * (1.f + zv[j] * (1.f - sg));
-                    dg[j] = dg[j] * zv[j] * sg;
-                }
-                Vec4<IT>::store(smem + S.dz + out_off(cc, t4), dz);
-            }
-            if (tile_short) {
-                // past the end of the sequence: identity steps that add nothing
-#pragma unroll
-                for (int j = 0; j < 4; j++)
-                    if (t0 + t4 + j >= Lq) { dl[j] = 0.f; du[j] = 0.f; dg[j] = 0.f; spg[j] = 0.f; uv[j] = 0.f; }
-            }
-            *reinterpret_cast<float4*>(sD + cc * RS + t4) = make_float4(dl[0], dl[1], dl[2], dl[3]);
-            *reinterpret_cast<float4*>(sDU + cc * RS + t4) = make_float4(du[0], du[1], du[2], du[3]);
-            *reinterpret_cast<float4*>(sG + cc * RS + t4) = make_float4(dg[0], dg[1], dg[2], dg[3]);
-            *reinterpret_cast<float4*>(sSP + cc * RS + t4) = make_float4(spg[0], spg[1], spg[2], spg[3]);
-            *reinterpret_cast<float4*>(sU + cc * RS + t4) = make_float4(uv[0], uv[1], uv[2], uv[3]);
+            bwd_prologue_item<IT, RS>(smem, S, cc, t4, raw_off(cc, t4), out_off(cc, t4), sBias[cc], has_z,
+                                      p.delta_softplus != 0, tile_short, t0 + t4, Lq);
         }
         // B, C as float32 rows [token][16 states] in 2 copies: copy r holds each pair of
         // states in the order s ^ r.  Copy 1 starts 16 floats (64 bytes) past a multiple of
