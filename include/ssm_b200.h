@@ -135,7 +135,8 @@ typedef struct ssm_carry_args {
     const float* delta_sum; int64_t delta_sum_slice_stride; /* (nslices, batch, dim) */
     const float* start;  int64_t start_stride;            /* nstart x (batch, dim, dstate) */
     float* result;                 /* forward: (nslices + 1, batch, dim, dstate);
-                                      reverse: (nslices, batch, dim, dstate); contiguous */
+                                      reverse: (nslices, batch, dim, dstate); contiguous;
+                                      must not overlap carry or delta_sum */
 } ssm_carry_args;
 
 typedef struct ssm_state_update_args {

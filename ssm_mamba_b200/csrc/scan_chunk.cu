@@ -263,20 +263,53 @@ __global__ void carry_compose_kernel(const __grid_constant__ CarryParams p) {
     const int64_t bd = i / p.dstate;
     const int d = (int)(bd % p.dim);
     const float a2 = p.A[(int64_t)d * p.A_sd + n] * kLog2e;
+    // result does not overlap carry or delta_sum (C ABI), so each batch of U slices' inputs
+    // is loaded before the batch's fold: the fold is sequential, its loads are not
+    const float* __restrict__ carry = p.carry;
+    const float* __restrict__ dsum = p.delta_sum;
+    float* __restrict__ res = p.result;
+    constexpr int U = 8;
     float h = 0.f;
     if (p.start)
         for (int r = 0; r < p.nstart; r++) h += p.start[r * p.start_ss + i];
+    const int M = p.nslices;
     if (!p.reverse) {
-        p.result[i] = h;
-        for (int q = 0; q < p.nslices; q++) {
-            h = fmaf(ex2(a2 * p.delta_sum[q * p.dsum_ss + bd]), h, p.carry[q * p.carry_ss + i]);
-            p.result[(int64_t)(q + 1) * per + i] = h;
+        res[i] = h;
+        for (int q0 = 0; q0 < M; q0 += U) {
+            float e[U], c[U];
+#pragma unroll
+            for (int k = 0; k < U; k++) {
+                const int q = q0 + k;
+                e[k] = q < M ? dsum[q * p.dsum_ss + bd] : 0.f;
+                c[k] = q < M ? carry[q * p.carry_ss + i] : 0.f;
+            }
+#pragma unroll
+            for (int k = 0; k < U; k++) {
+                const int q = q0 + k;
+                if (q < M) {
+                    h = fmaf(ex2(a2 * e[k]), h, c[k]);
+                    res[(int64_t)(q + 1) * per + i] = h;
+                }
+            }
         }
     } else {
-        p.result[(int64_t)(p.nslices - 1) * per + i] = h;
-        for (int q = p.nslices - 1; q >= 1; q--) {
-            h = fmaf(ex2(a2 * p.delta_sum[q * p.dsum_ss + bd]), h, p.carry[q * p.carry_ss + i]);
-            p.result[(int64_t)(q - 1) * per + i] = h;
+        res[(int64_t)(M - 1) * per + i] = h;
+        for (int q0 = M - 1; q0 >= 1; q0 -= U) {
+            float e[U], c[U];
+#pragma unroll
+            for (int k = 0; k < U; k++) {
+                const int q = q0 - k;
+                e[k] = q >= 1 ? dsum[q * p.dsum_ss + bd] : 0.f;
+                c[k] = q >= 1 ? carry[q * p.carry_ss + i] : 0.f;
+            }
+#pragma unroll
+            for (int k = 0; k < U; k++) {
+                const int q = q0 - k;
+                if (q >= 1) {
+                    h = fmaf(ex2(a2 * e[k]), h, c[k]);
+                    res[(int64_t)(q - 1) * per + i] = h;
+                }
+            }
         }
     }
 }

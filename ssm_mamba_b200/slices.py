@@ -254,19 +254,32 @@ class SlicedScanFn(torch.autograd.Function):
         _mark("fwd_chunk_state")
         h0, dsum = k.chunk_state_fwd(u_s, d_s, A, B_s, delta_bias, bool(delta_softplus))
         per = Bc * Dm * N
-        pack = torch.cat([h0.reshape(S, per), dsum.reshape(S, Bc * Dm)], dim=1)   # (S, per + Bc*Dm)
-        # 2. carries of every slice of the sequence, in order
-        _mark("fwd_exchange")
-        allp = group.all_gather(pack).reshape(group.world * S, per + Bc * Dm)
-        _mark("fwd_compose")
-        M = group.world * S
-        carry = allp[:, :per].unflatten(1, (Bc, Dm, N))     # slice stride per + Bc*Dm
-        dsum_all = allp[:, per:].unflatten(1, (Bc, Dm))
+        carry_loc = h0.reshape(S, Bc, Dm, N)
+        dsum_loc = dsum.reshape(S, Bc, Dm)
         start = h_init.reshape(1, Bc, Dm, N) if h_init is not None else None
-        carries = k.carry_compose(A, carry, dsum_all, start, False)                # (M + 1, Bc, Dm, N)
         r = group.rank
-        h_in = carries[r * S:(r + 1) * S].reshape(rows, Dm, N)
-        h_final = carries[M].reshape(Bc, Dm, N)
+        if group.world == 1:
+            # 2. the state entering every slice, in order
+            _mark("fwd_compose")
+            carries = k.carry_compose(A, carry_loc, dsum_loc, start, False)        # (S + 1, Bc, Dm, N)
+            h_final = carries[S].reshape(Bc, Dm, N)
+            dsum_rank = dsum_loc.sum(0, keepdim=True)
+        else:
+            # 2. in two levels, so that one carry per rank crosses the interconnect: this
+            # rank's slices folded into its end state from a zero start and its delta sum,
+            # those of all ranks exchanged and folded in rank order (the state entering
+            # every rank), then this rank's slices folded again from its entering state
+            _mark("fwd_compose")
+            local = k.carry_compose(A, carry_loc, dsum_loc, None, False)           # (S + 1, Bc, Dm, N)
+            pack = torch.cat([local[S].reshape(per), dsum_loc.sum(0).reshape(Bc * Dm)])
+            _mark("fwd_exchange")
+            allp = group.all_gather(pack)                                            # (world, per + Bc*Dm)
+            _mark("fwd_compose")
+            dsum_rank = allp[:, per:].reshape(group.world, Bc, Dm)
+            ranks = k.carry_compose(A, allp[:, :per].reshape(group.world, Bc, Dm, N), dsum_rank, start, False)
+            h_final = ranks[group.world].reshape(Bc, Dm, N)
+            carries = k.carry_compose(A, carry_loc, dsum_loc, ranks[r:r + 1], False)
+        h_in = carries[:S].reshape(rows, Dm, N)
         # 3. the ordinary forward of every slice from its own initial state
         need_grad = any(ctx.needs_input_grad[:9])
         _mark("fwd_scan")
@@ -275,18 +288,17 @@ class SlicedScanFn(torch.autograd.Function):
         _, _, ckpt, _ = k.scan_fwd_out(u_s, d_s, A, B_s, C_s, D, z_s, delta_bias, h_in, None, True,
                                        bool(delta_softplus), sv(out), sv(y), 1 if need_grad else 0, False)
         if need_grad:
-            ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, y, ckpt, h_in, dsum_all, h_init)
+            ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, y, ckpt, h_in, dsum_loc, dsum_rank, h_init)
             ctx.cfg = (bool(delta_softplus), S, group, k, Bc, rows)
         _mark("end_fwd")
         return out, h_final
 
     @staticmethod
     def backward(ctx, dout, dh_final):
-        u, delta, A, B, C, D, z, delta_bias, y, ckpt, h_in, dsum_all, h_init = ctx.saved_tensors
+        u, delta, A, B, C, D, z, delta_bias, y, ckpt, h_in, dsum_loc, dsum_rank, h_init = ctx.saved_tensors
         softplus, S, group, k, Bc, rows = ctx.cfg
         Bt, Dm, L = u.shape
         N = A.shape[1]
-        M = group.world * S
         sv = lambda t: segment_view(t, S)  # noqa: E731
         dout = dout.contiguous()
         u_s, d_s, B_s, C_s, z_s, dout_s = sv(u), sv(delta), sv(B), sv(C), sv(z), sv(dout)
@@ -298,16 +310,30 @@ class SlicedScanFn(torch.autograd.Function):
         per = Bc * Dm * N
         if dh_final is None:
             dh_final = torch.zeros(Bc, Dm, N, device=u.device, dtype=g0.dtype)
-        pack = torch.cat([g0.reshape(S * per), dh_final.reshape(per).to(g0.dtype)])
-        _mark("bwd_exchange")
-        allp = group.all_gather(pack)                                                # (world, (S + 1) * per)
-        _mark("bwd_compose")
-        g_all = allp[:, :S * per].reshape(M, Bc, Dm, N)
-        dhf_all = allp[:, S * per:].reshape(group.world, Bc, Dm, N)
-        # 2. the gradient leaving every slice's end
-        gout = k.carry_compose(A, g_all, dsum_all, dhf_all, True)                   # (M, Bc, Dm, N)
+        g_loc = g0.reshape(S, Bc, Dm, N)
         r = group.rank
-        dh_last = gout[r * S:(r + 1) * S].reshape(rows, Dm, N)
+        if group.world == 1:
+            # 2. the gradient leaving every slice's end
+            _mark("bwd_compose")
+            dh_last = k.carry_compose(A, g_loc, dsum_loc, dh_final.reshape(1, Bc, Dm, N).to(g0.dtype), True)
+        else:
+            # 2. in two levels (as the forward): this rank's slices folded, from a zero
+            # gradient at its end, into the gradient entering its start (a reverse fold over
+            # S + 1 entries whose entry 0 is never read); those of all ranks exchanged with
+            # the ranks' final-state gradients and folded in reverse rank order (the gradient
+            # leaving every rank's end); then this rank's slices folded again from it
+            _mark("bwd_compose")
+            ext = torch.cat([g_loc[:1], g_loc])
+            dext = torch.cat([dsum_loc[:1], dsum_loc])
+            local = k.carry_compose(A, ext, dext, None, True)                       # (S + 1, Bc, Dm, N)
+            pack = torch.cat([local[0].reshape(per), dh_final.reshape(per).to(g0.dtype)])
+            _mark("bwd_exchange")
+            allp = group.all_gather(pack)                                            # (world, 2 per)
+            _mark("bwd_compose")
+            ranks = k.carry_compose(A, allp[:, :per].reshape(group.world, Bc, Dm, N), dsum_rank,
+                                    allp[:, per:].reshape(group.world, Bc, Dm, N), True)
+            dh_last = k.carry_compose(A, g_loc, dsum_loc, ranks[r:r + 1], True)      # (S, Bc, Dm, N)
+        dh_last = dh_last.reshape(rows, Dm, N)
         # 3. the ordinary backward of every slice
         _mark("bwd_scan")
         du, ddelta = torch.empty_like(u), torch.empty_like(u)
