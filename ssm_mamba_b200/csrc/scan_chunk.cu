@@ -28,9 +28,11 @@
 
 namespace ssm {
 
-// The carry passes are bound by the MUFU pipe (one exp2 per token and state, ~83% busy) while
-// the FMA pipe is ~40% busy: of every 4 (token, state pair) exp2 pairs, kChunkExpOnFma are
-// computed on the FMA pipe by exp2_fma2 (common.cuh) instead of by ex2.approx.
+// With every exp2 on the MUFU pipe (one per token and state) the carry passes are bound by the
+// queue that feeds MUFU and shared-memory instructions (XU ~83% busy, FMA ~40%): of every 4
+// (token, state pair) exp2 pairs, kChunkExpOnFma are computed on the FMA pipe by exp2_fma2
+// (common.cuh) instead of by ex2.approx.  Measured on B200 at config 5's segment shape: a
+// quarter is the best share (issue, MUFU and FMA then 60-70% busy each); a half is slower.
 constexpr int kChunkExpOnFma = 1;
 
 __device__ __forceinline__ uint32_t chunk_stage(const uint32_t (&a)[2], int st) { return st ? a[1] : a[0]; }

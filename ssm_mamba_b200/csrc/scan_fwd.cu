@@ -9,7 +9,9 @@
 //    registers, so there is no block scan and no per-chunk carry through shared memory.
 //  * A thread owns one channel and SPT consecutive states; the LPC = NS/SPT lanes of a
 //    channel are adjacent.  y_t = sum_n C h needs one reduce-scatter across those lanes
-//    every G = max(4, LPC) tokens.
+//    every G = max(16, LPC) tokens; each group of G tokens is straight-line code (in-group
+//    checkpoints are predicated stores) and its reduce-scatter and epilogue overlap the
+//    next group's recurrence.
 //  * Each tile's u, delta, z and the (B, C) tile are brought in by 3-D TMA loads
 //    (128-byte swizzle, 2 stages, mbarrier completion) and the outputs leave by TMA stores.
 //    B and C are loaded once per CTA and shared by all of its channels (the reference
