@@ -97,6 +97,18 @@ __device__ __forceinline__ float sigmoid_io(float x) {
     else return sigmoidf_fast(x);
 }
 
+// sigmoid_io of two values, the multiplications and adds packed (same results per element)
+template <typename IT>
+__device__ __forceinline__ float2 sigmoid_io2(float2 x) {
+    if constexpr (sizeof(IT) == 2) {
+        const float2 h = __fmul2_rn(make_float2(0.5f, 0.5f), x);
+        return __ffma2_rn(make_float2(0.5f, 0.5f), make_float2(tanh_approx(h.x), tanh_approx(h.y)),
+                          make_float2(0.5f, 0.5f));
+    } else {
+        return make_float2(sigmoidf_fast(x.x), sigmoidf_fast(x.y));
+    }
+}
+
 // log(1 + e^x) = max(x, 0) + log1p(t), t = e^-|x| in (0, 1], with log1p(t) = 2 atanh(s),
 // s = t / (2 + t) in (0, 1/3], from the series 2 atanh(s) = 2 s (1 + s^2/3 + s^4/5 + ...).
 // Truncated after s^12/13 the series error is below (1/3)^14/15 ~ 1.4e-8 relative; the

@@ -171,29 +171,46 @@ __global__ void __launch_bounds__(128, 4) scan_chunk_kernel(const __grid_constan
             if (has_z) Vec4<IT>::load(s2 + off, zv);
             const float bias = sBias[cc];
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const float x = dr[k] + bias;
-                dl[k] = p.delta_softplus ? softplus_series(x) : x;
+            for (int k = 0; k < 4; k += 2) {
+                // token pairs in packed f32x2 arithmetic (the same operations per element)
+                const float2 x = make_float2(dr[k] + bias, dr[k + 1] + bias);
+                const float2 v = p.delta_softplus ? softplus_series2(x) : x;
+                dl[k] = v.x;
+                dl[k + 1] = v.y;
+                float2 o;
                 if (REV)
-                    xo[k] = has_z ? xv[k] * zv[k] * sigmoid_io<IT>(zv[k]) : xv[k];
+                    o = has_z ? __fmul2_rn(__fmul2_rn(make_float2(xv[k], xv[k + 1]), make_float2(zv[k], zv[k + 1])),
+                                           make_float2(sigmoid_io<IT>(zv[k]), sigmoid_io<IT>(zv[k + 1])))
+                              : make_float2(xv[k], xv[k + 1]);
                 else
-                    xo[k] = dl[k] * xv[k];
-                if (tile_short && t0 + t4 + k >= Lq) { dl[k] = 0.f; xo[k] = 0.f; }
+                    o = __fmul2_rn(v, make_float2(xv[k], xv[k + 1]));
+                xo[k] = o.x;
+                xo[k + 1] = o.y;
+            }
+            if (tile_short) {
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    if (t0 + t4 + k >= Lq) { dl[k] = 0.f; xo[k] = 0.f; }
             }
             *reinterpret_cast<float4*>(sD + cc * RS + t4) = make_float4(dl[0], dl[1], dl[2], dl[3]);
             *reinterpret_cast<float4*>(sX + cc * RS + t4) = make_float4(xo[0], xo[1], xo[2], xo[3]);
         }
         const unsigned char* s3 = smem + chunk_stage(L.x3, st);
-        for (int i = tid; i < Q * T; i += nthr) {
-            const int q = i / T, tt = i % T;
-            const bool ld = t0 + tt < Lq;
-            float v[4];
+        // (two tokens per work item: one 4- or 8-byte load per state row)
+        for (int i = tid; i < Q * (T / 2); i += nthr) {
+            const int q = i / (T / 2), tt = 2 * (i % (T / 2));
+            const bool ld0 = t0 + tt < Lq, ld1 = t0 + tt + 1 < Lq;
+            float2 v[4];
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 const int n = q * 4 + k;
-                v[k] = (ld && n < N) ? to_f(*reinterpret_cast<const IT*>(s3 + swz128(n, tt * ES))) : 0.f;
+                v[k] = n < N ? load_pair<IT>(s3 + swz128(n, tt * ES)) : make_float2(0.f, 0.f);
+                if (!ld0) v[k].x = 0.f;
+                if (!ld1) v[k].y = 0.f;
             }
-            *reinterpret_cast<float4*>(sM + tt * NS + ((q ^ (tt & QM)) << 2)) = make_float4(v[0], v[1], v[2], v[3]);
+            *reinterpret_cast<float4*>(sM + tt * NS + ((q ^ (tt & QM)) << 2)) = make_float4(v[0].x, v[1].x, v[2].x, v[3].x);
+            *reinterpret_cast<float4*>(sM + (tt + 1) * NS + ((q ^ ((tt + 1) & QM)) << 2)) =
+                make_float4(v[0].y, v[1].y, v[2].y, v[3].y);
         }
         __syncthreads();
         // the raw stage is consumed: refill it with the tile after next

@@ -181,10 +181,15 @@ __device__ __forceinline__ void fwd_finish(float (&yv)[G], int c, int g, int q0,
             Vec4<IT>::load(su + off, uv);
             Vec4<IT>::load(sz + off, zv);
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                yt[j] = fmaf(Dd, uv[j], yv[r4 + j]);
-                const float gated = yt[j] * zv[j] * sigmoid_io<IT>(zv[j]);
-                o[j] = has_z ? gated : yt[j];
+            for (int j = 0; j < 4; j += 2) {   // token pairs, packed (same results per element)
+                const float2 z2 = make_float2(zv[j], zv[j + 1]);
+                const float2 y2 = __ffma2_rn(make_float2(Dd, Dd), make_float2(uv[j], uv[j + 1]),
+                                             make_float2(yv[r4 + j], yv[r4 + j + 1]));
+                const float2 gated = __fmul2_rn(__fmul2_rn(y2, z2), sigmoid_io2<IT>(z2));
+                yt[j] = y2.x;
+                yt[j + 1] = y2.y;
+                o[j] = has_z ? gated.x : y2.x;
+                o[j + 1] = has_z ? gated.y : y2.y;
             }
             Vec4<IT>::store(sy + off, yt);
             Vec4<IT>::store(so + off, o);
