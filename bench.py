@@ -57,6 +57,20 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def _pure(name):
+    """ssm_mamba_b200/<name>.py (workloads, weights: plain torch, no native code) loaded by path,
+    without importing the ssm_mamba_b200 package, so that the reference arm, which uses these
+    input generators, imports nothing of this library."""
+    import importlib.util
+    key = "_bench_pure_" + name
+    if key not in sys.modules:
+        spec = importlib.util.spec_from_file_location(key, os.path.join(ROOT, "ssm_mamba_b200", name + ".py"))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[key] = mod
+        spec.loader.exec_module(mod)
+    return sys.modules[key]
+
+
 def traffic_from_profiles(name, key="traffic_bytes_per_launch"):
     """Per-launch DRAM bytes of a kernel, from a committed ncu summary (profiles/*.txt
     lines `traffic_bytes_per_launch <kernel> <bytes>`; another per-launch figure with
@@ -228,7 +242,7 @@ def cpu_baseline_sample(target_s=10.0, batch=1, dim=96):
     import numpy as np
     import torch
     oracle = host_oracle()
-    from ssm_mamba_b200.workloads import scan_inputs
+    scan_inputs = _pure("workloads").scan_inputs
     L, N = CFG2["seqlen"], CFG2["dstate"]
     inp = scan_inputs(batch, dim, L, N, torch.bfloat16, seed=1, device="cpu", with_z=True)
     f = lambda t: t.float().numpy()  # noqa: E731
@@ -256,7 +270,7 @@ def cpu_decode_sample(target_s=3.0):
     import numpy as np
     import torch
     oracle = host_oracle()
-    from ssm_mamba_b200.workloads import decode_inputs
+    decode_inputs = _pure("workloads").decode_inputs
     Bd, Dd, Nd = CFG3["batch"], CFG3["dim"], CFG3["dstate"]
     dec = decode_inputs(Bd, Dd, Nd, 4, torch.bfloat16, seed=2, device="cpu")
     f = lambda t: t.float().numpy()  # noqa: E731
@@ -281,7 +295,7 @@ def cpu_long_seq_sample(target_s=3.0, dim=48, seqlen=8192):
     import numpy as np
     import torch
     oracle = host_oracle()
-    from ssm_mamba_b200.workloads import scan_inputs
+    scan_inputs = _pure("workloads").scan_inputs
     N = CFG5["dstate"]
     inp = scan_inputs(1, dim, seqlen, N, torch.bfloat16, seed=4, device="cpu", with_z=True)
     f = lambda t: t.float().numpy()  # noqa: E731
@@ -308,7 +322,7 @@ def run_decode(args, world, rank, local, pg, peak):
     (168 MB > L2) so every step reads and writes its state in HBM."""
     import torch
     from ssm_mamba_b200 import selective_state_update
-    from ssm_mamba_b200.workloads import decode_inputs
+    decode_inputs = _pure("workloads").decode_inputs
     dev = torch.device("cuda", local)
     Bd, Dd, Nd, S, Ly = CFG3["batch"], CFG3["dim"], CFG3["dstate"], CFG3["steps"], CFG3["layers"]
     dec = decode_inputs(Bd, Dd, Nd, S, torch.bfloat16, seed=2 + rank, device=dev)
@@ -355,7 +369,7 @@ def run_long_seq(args, world, rank, local, pg, peak):
     the total work is fixed)."""
     import torch
     from ssm_mamba_b200.slices import SliceGroup, plan_segments, sliced_scan
-    from ssm_mamba_b200.workloads import scan_inputs
+    scan_inputs = _pure("workloads").scan_inputs
     dev = torch.device("cuda", local)
     Ltot, Dm, N = (args.long_seqlen or CFG5["seqlen"]), CFG5["dim"], CFG5["dstate"]
     Lr = Ltot // world
@@ -426,7 +440,7 @@ def _seqpar_parity(dev, rank, world, group, pg):
     Every rank takes the same collectives; the verdict is the worst over the ranks."""
     import torch
     from ssm_mamba_b200.slices import sliced_scan
-    from ssm_mamba_b200.workloads import scan_inputs
+    scan_inputs = _pure("workloads").scan_inputs
     L, Dm, N = 8192, 256, 16
     inp = scan_inputs(1, Dm, L, N, torch.float32, seed=21, device="cpu", with_z=True, with_h_init=True)
     dh = torch.randn(1, Dm, N, generator=torch.Generator().manual_seed(5))
@@ -493,7 +507,7 @@ def _decode_graph_us(apply_fn, dev, seed=2):
     selective_update.cpp:208-209) over 8 rotating layer states (168 MB > L2), 256 steps in
     one CUDA graph; float32 (config 3 shape)."""
     import torch
-    from ssm_mamba_b200.workloads import decode_inputs
+    decode_inputs = _pure("workloads").decode_inputs
     Bd, Dd, Nd, Ly = CFG3["batch"], CFG3["dim"], CFG3["dstate"], CFG3["layers"]
     S = 256
     dec = decode_inputs(Bd, Dd, Nd, S, torch.float32, seed=seed, device=dev)
@@ -520,7 +534,7 @@ def run_equal_precision(dev, forward_backward, update_apply):
     backward, `update_apply` one out-of-place decode step.  Same shapes and seeds in both
     arms of bench.py."""
     import torch
-    from ssm_mamba_b200.workloads import scan_inputs
+    scan_inputs = _pure("workloads").scan_inputs
     res = {}
     for name, (Bs, Dm, L, seed) in EQ_SCAN.items():
         inp = scan_inputs(Bs, Dm, L, 16, torch.float32, seed=seed, device=dev, with_z=False)
@@ -544,7 +558,7 @@ def run_varlen(dev, forward_backward, dtypes=("fp32",)):
     reference-shaped call `forward_backward(inputs, length, padding)`; float32 (the
     reference kernels' only dtype) and, where given, bf16."""
     import torch
-    from ssm_mamba_b200.workloads import scan_inputs
+    scan_inputs = _pure("workloads").scan_inputs
     Bs, Dm, L, N = CFG2["batch"], CFG2["dim"], CFG2["seqlen"], CFG2["dstate"]
     g = torch.Generator().manual_seed(5)
     length = torch.randint(L // 2, L + 1, (Bs,), generator=g).to(dev)
@@ -620,8 +634,8 @@ LAYER = dict(batch=64, model=2560, inner=5120, state=16, rank=160, width=4)
 def _layer_weights(dev, dtype, seed=11):
     """Random weights of a Mamba-2.8B-width layer (ssm_mamba_b200.weights.MambaLayerWeights)."""
     import torch
-    from ssm_mamba_b200.weights import MambaLayerWeights
-    from ssm_mamba_b200.workloads import dt_bias_init, s4d_real_A
+    MambaLayerWeights = _pure("weights").MambaLayerWeights
+    dt_bias_init, s4d_real_A = _pure("workloads").dt_bias_init, _pure("workloads").s4d_real_A
     c = LAYER
     g = torch.Generator(device=dev).manual_seed(seed)
     r = lambda *sh, sc=0.02: (torch.randn(*sh, device=dev, generator=g) * sc)  # noqa: E731
@@ -693,8 +707,8 @@ def _lm_weights(dev, dtype, seed=3):
     A from the S4D-real log_A; D = 1; RMSNorm weights 0 (the norm scales by 1 + weight); no
     biases.  Returns (embedding, [(norm weight, MambaLayerWeights)], final norm weight)."""
     import torch
-    from ssm_mamba_b200.weights import MambaLayerWeights
-    from ssm_mamba_b200.workloads import dt_bias_init, s4d_real_A
+    MambaLayerWeights = _pure("weights").MambaLayerWeights
+    dt_bias_init, s4d_real_A = _pure("workloads").dt_bias_init, _pure("workloads").s4d_real_A
     c = CFG4
     g = torch.Generator(device=dev).manual_seed(seed)
     r = lambda *sh: torch.randn(*sh, device=dev, generator=g, dtype=torch.float32).mul_(0.02).to(dtype)  # noqa: E731
@@ -801,8 +815,8 @@ def run_train_layer(dev, dtype, variants, reps=10, graph=False):
     layer(weights, hidden) -> output.  With `graph`, the first variant's step is also
     captured once in a CUDA graph and replayed."""
     import torch
-    from ssm_mamba_b200.weights import MambaLayerWeights
-    from ssm_mamba_b200.workloads import dt_bias_init, s4d_real_A
+    MambaLayerWeights = _pure("weights").MambaLayerWeights
+    dt_bias_init, s4d_real_A = _pure("workloads").dt_bias_init, _pure("workloads").s4d_real_A
     c = TRAIN
     g = torch.Generator(device=dev).manual_seed(13)
     r = lambda *sh: torch.randn(*sh, device=dev, generator=g, dtype=torch.float32).mul_(0.02).to(dtype)  # noqa: E731
@@ -887,7 +901,7 @@ def run_ours(args, world, rank, local, pg):
     import torch
     from ssm_mamba_b200._ext import _C
     from ssm_mamba_b200 import selective_scan_fn, selective_state_update
-    from ssm_mamba_b200.workloads import scan_inputs
+    scan_inputs = _pure("workloads").scan_inputs
     dev = torch.device("cuda", local)
     if args.decode_only:
         return {"decode": run_decode(args, world, rank, local, pg, measured_peaks()[0])}
@@ -1149,7 +1163,7 @@ def run_reference(args, world, rank, local, pg):
         return None
     import numpy as np
     oracle = host_oracle()
-    from ssm_mamba_b200.workloads import scan_inputs
+    scan_inputs = _pure("workloads").scan_inputs
     L, N = CFG2["seqlen"], CFG2["dstate"]
     sb, sd = 1, 48
     inp = scan_inputs(sb, sd, L, N, torch.bfloat16, seed=1, device="cpu", with_z=True)
@@ -1326,9 +1340,9 @@ def run_reference(args, world, rank, local, pg):
 
 def _loaded_library_evidence():
     """What of this repository the process has loaded: the ssm_mamba_b200 Python modules and
-    every in-tree shared library mapped (/proc/self/maps).  The reference arm imports only the
-    pure-torch input generators (ssm_mamba_b200.workloads, .weights), so it must map no
-    native library of ssm_mamba_b200."""
+    every in-tree shared library mapped (/proc/self/maps).  The reference arm loads only the
+    pure-torch input generators (ssm_mamba_b200/workloads.py, weights.py) by path, without the
+    package, so it must list no module and map no native library of ssm_mamba_b200."""
     mods = sorted(m for m in sys.modules if m == "ssm_mamba_b200" or m.startswith("ssm_mamba_b200."))
     libs = set()
     try:
